@@ -1,0 +1,325 @@
+"""Benchmark: candidate-pixel decodes per second of ES training iterations on B200.
+
+A step is one ES-phase training iteration of the benchmark's config 2 (512x512 synthetic RGB8 image,
+level 0 = 512x512x1 2-bit --qat selector plane, level 1 = 128x128x2 bilinear, 24-24 MLP -> 3, population
+8192 = 4096 antithetic pairs, minibatch 4096, 4 latent pairs): mlp_step + lat_step + qat_search, which is
+2N M + 2K W H + sum_c 2^B_c W H = 36.7 M candidate-pixel decodes.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
+
+--impl ours (default): the CUDA backend. N > 1 (torchrun, one process per GPU): the ES population is sharded
+over the ranks (each evaluates its pairs, regenerating their noise from the counter); one NCCL all-gather of
+the per-pair fitness (2 doubles per pair) feeds the identical gradient + Adam on every rank; the latent step
+and the selector search run as replicas.
+--impl reference: the reference's own CPU trainer (main.cpp compiled from source, OpenMP on every host
+thread) timed on a bounded sample of the same iteration (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)   # ~2 s timed: long enough for the 200 ms clock samples
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def reference_arm(args, world, rank):
+    """The reference CPU trainer (oracle/_ref/libntc_refcpu.so, main.cpp compiled unmodified) on all host threads."""
+    if world > 1 and rank != 0:
+        return
+    from neural_block_textures_b200 import model
+    from oracle.oracle import RefSession, refcpu_available, refcpu_lib
+    cfg = model.config(args.config)
+    line = {"impl": "reference", "metric": "candidate-pixel decodes/s (ES training iteration)", "unit": "decodes/s",
+            "higher_is_better": True, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup}
+    if not refcpu_available():
+        line["unavailable"] = "oracle/_ref/libntc_refcpu.so was not built (the reference tree was absent at build time)"
+        print(json.dumps(line)); return
+    sess, sample_pairs, dec, cores = _ref_sample_setup(cfg)
+    for _ in range(args.warmup):
+        _ref_sample_step(sess, cfg, sample_pairs, 1)
+    ts = []
+    for k in range(args.steps):
+        t0 = time.perf_counter()
+        _ref_sample_step(sess, cfg, sample_pairs, 2 + k)
+        ts.append(time.perf_counter() - t0)
+    total = sum(ts)
+    value = dec * args.steps / total
+    line.update({"value": value, "ms_per_step": 1e3 * total / args.steps, "scaling": "none", "vs_baseline": None,
+                 "dtype": "f32", "data": "synthetic",
+                 "config": {"workload": cfg.name, "cli": cfg.cli, "sample": f"{sample_pairs} of {cfg.pairs} ES pairs per step + "
+                            "the full latent step + the full selector search", "l2": "n/a (CPU)"},
+                 "cpu_baseline": {"value": value, "unit": "decodes/s", "cores": cores, "kind": "reference",
+                                  "sample": f"per step: MLP ES with {sample_pairs} pairs x M={cfg.batch}, latent ES K={cfg.lat_pairs}, "
+                                            f"qat search; {dec / 1e6:.2f} M decodes"},
+                 "e2e": {"value": value, "unit": "decodes/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    print(json.dumps(line))
+
+
+def _ref_sample_setup(cfg):
+    from oracle.oracle import RefSession, refcpu_lib
+    lib = refcpu_lib()
+    cores = int(lib.ref_max_threads())
+    spec = cfg.spec
+    sess = RefSession(spec, cfg.target())
+    z, p = spec.init_params()
+    sess.set_model(z, p)
+    sample_pairs = min(cfg.pairs, 256)
+    d = cfg.decodes_per_iter()
+    dec = 2 * sample_pairs * cfg.batch + d["latent"] + d["qat"]
+    return sess, sample_pairs, dec, cores
+
+
+def _ref_sample_step(sess, cfg, pairs, it):
+    sess.iteration(it, pairs, cfg.batch, cfg.mlp_sigma, cfg.mlp_lr, 0, cfg.fd_h, cfg.lat_pairs, cfg.lat_sigma, cfg.lat_lr)
+
+
+def cpu_baseline_leg(cfg, budget_s=12.0):
+    """The reference CPU path on the host cores (rank 0, N=1), bounded to ~budget_s seconds of work."""
+    from oracle.oracle import refcpu_available
+    if not refcpu_available():
+        return None
+    sess, pairs, dec, cores = _ref_sample_setup(cfg)
+    _ref_sample_step(sess, cfg, pairs, 1)
+    n, t_all = 0, 0.0
+    while t_all < budget_s and n < 50:
+        t0 = time.perf_counter()
+        _ref_sample_step(sess, cfg, pairs, 2 + n)
+        t_all += time.perf_counter() - t0
+        n += 1
+    return {"value": dec * n / t_all, "unit": "decodes/s", "cores": cores, "kind": "reference",
+            "sample": f"{n} reference CPU iterations of {cfg.name} with {pairs} of {cfg.pairs} ES pairs (+ full latent step "
+                      f"and selector search): {dec / 1e6:.2f} M decodes each, {t_all:.1f} s"}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from neural_block_textures_b200 import Trainer, load_library, model
+
+    cfg = model.config(args.config)
+    spec = cfg.spec
+    target = cfg.target()
+    z0, p0 = spec.init_params()
+    tr = Trainer()
+    ok, why = tr.init(spec.model_desc(), z0, p0, target)
+    if not ok:
+        raise SystemExit(f"init failed: {why}")
+    stream = torch.cuda.Stream()
+    tr.set_stream(stream.cuda_stream)
+    N, M, K = cfg.pairs, cfg.batch, cfg.lat_pairs
+    if N % world:
+        raise SystemExit(f"{N} pairs do not split evenly over {world} ranks")
+    per = N // world
+    p_begin, p_end = min(N, rank * per), min(N, (rank + 1) * per)
+    fit_local = torch.zeros(2 * per, dtype=torch.float64, device="cuda")
+    fit_all = torch.zeros(2 * per * world, dtype=torch.float64, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    dec = cfg.decodes_per_iter()
+    decodes = sum(dec.values())
+
+    def step(it):
+        if world == 1:
+            tr.mlp_step(it, cfg.mlp_sigma, cfg.mlp_lr, N, M)
+        else:
+            tr.shard_mlp_eval(it, cfg.mlp_sigma, N, M, p_begin, p_end, fit_local.data_ptr())
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(fit_all, fit_local)
+            tr.shard_mlp_apply(it, cfg.mlp_sigma, cfg.mlp_lr, N, M, fit_all.data_ptr())
+        tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
+        tr.qat_search()
+
+    it = 1
+    for _ in range(args.warmup):
+        step(it); it += 1
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    tr.kernel_timing(True)
+    launches0 = tr.launch_count()
+    evs = []
+    with ClockSampler(local) as clk:
+        time.sleep(0.6)            # nvidia-smi's first sample lands before the timed steps start
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()          # L2 flush between steps, outside the timed events
+                e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            step(it); it += 1
+            with torch.cuda.stream(stream):
+                e1.record(stream)
+            evs.append((e0, e1))
+        stream.synchronize()
+    torch.cuda.synchronize()
+    launches = tr.launch_count() - launches0
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    eval_ms, eval_n = tr.kernel_time("mlp_eval")
+    lat_ms, lat_n = tr.kernel_time("lat_eval")
+    qat_ms, qat_n = tr.kernel_time("qat")
+    tr.kernel_timing(False)
+    if dist:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = decodes * args.steps / (ms * 1e-3)
+
+    # ---- end to end through the public API with host buffers (pinned), copies inside the timed region
+    zh = torch.empty(spec.nz, dtype=torch.float32, pin_memory=True).numpy()
+    ph = torch.empty(spec.P, dtype=torch.float32, pin_memory=True).numpy()
+    zh[:] = z0; ph[:] = p0
+    e2e_steps = args.e2e_steps
+    for _ in range(2):
+        tr.upload_model(zh, ph); step(it); it += 1
+        zz, pp = tr.download_model(); tr.mlp_stats()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        tr.upload_model(zh, ph)
+        step(it); it += 1
+        zz, pp = tr.download_model()
+        tr.mlp_stats()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = decodes * e2e_steps / e2e_s
+    h2d = 4 * (spec.nz + spec.P)
+    d2h = 4 * (spec.nz + spec.P) + 16 * N
+
+    if rank == 0:
+        lib = load_library()
+        ffma = float(lib.ntcb_fp32_peak_tflops())
+        fpd = cfg.flops_per_decode()
+        eval_flops = 2 * per * M * fpd if world > 1 else 2 * N * M * fpd
+        eval_avg_s = (eval_ms / max(eval_n, 1)) * 1e-3
+        achieved = eval_flops / eval_avg_s / 1e12 if eval_n else None
+        peaks = {}
+        pk = ROOT / "MEASURED_PEAKS.json"
+        if pk.exists():
+            peaks = json.loads(pk.read_text())
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get(cfg.name, {}).get("mlp_eval_dram_bytes_per_launch")
+        line = {
+            "metric": "candidate-pixel decodes/s (ES training iteration)", "value": value, "unit": "decodes/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg.name, "cli": cfg.cli, "decodes_per_step": dec, "parallelism": f"population x{world}",
+                       "l2": "flushed between steps (256 MiB memset outside the timed events)"},
+            "roofline": {"kernel": "k_pop_eval_fixed (MLP ES population evaluation)", "bound": "fp32",
+                         "achieved": achieved, "peak": ffma, "unit": "TFLOP/s",
+                         "frac": (achieved / ffma) if achieved else None, "traffic": traffic,
+                         "peak_source": "FP32 FFMA throughput measured on this GPU by ntcb_fp32_peak_tflops",
+                         "flops_per_launch": eval_flops, "avg_launch_ms": eval_avg_s * 1e3,
+                         "frac_of_measured_bf16_tensor": (achieved / peaks["bf16_tflops"]) if (achieved and "bf16_tflops" in peaks) else None},
+            "phase_ms_per_step": {"mlp_eval": eval_ms / args.steps, "lat_eval": lat_ms / args.steps, "qat": qat_ms / args.steps},
+            "e2e": {"value": e2e_value, "unit": "decodes/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_leg(cfg)
+        print(json.dumps(line))
+    tr.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+/* libntc_b200.so: flat C ABI of the B200 ES training backend for neural_block_textures.
+ *
+ * Every entry point mirrors one member of the reference backend's C++ class
+ * ntc_cuda::Trainer (cuda/ntc_cuda.h:78-132, cited per function) with plain pointers and
+ * sizes, so that any FFI (ctypes, cgo, JNI) can drive the same engine that the C++ class in
+ * ntc_cuda.h exposes to main.cpp. The description structs have exactly the layout of
+ * ntc_cuda::LevelDesc / ModelDesc / QesDesc / DctDesc (static_assert-ed in the library).
+ *
+ * Conventions (as the reference): host buffers are read or written synchronously inside the call
+ * and never retained; ntcb_init reports an unsupported model by returning 0 and writing a reason;
+ * every later runtime failure (a CUDA error, a size above what init sized) prints a message to
+ * stderr and exits the process, because the reference's caller has no error path.
+ * The ntcb_shard_* / ntcb_set_stream / ntcb_kernel_time entries are additions with no member
+ * counterpart (multi-GPU population sharding and measurement); they are marked as such. */
+#ifndef NTC_B200_H
+#define NTC_B200_H
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NTCB_MAX_LEVELS 3
+#define NTCB_MAX_POS 16
+#define NTCB_MAX_OUT 12
+#define NTCB_MAX_HIDDEN 8
+#define NTCB_MAX_CH 16
+#define NTCB_MAX_QES_CH 64
+#define NTCB_MAX_DCT_CH 4
+
+/* = ntc_cuda::LevelDesc (cuda/ntc_cuda.h:25) */
+typedef struct ntcb_level_desc { int W, H, C; size_t off; bool nearest; } ntcb_level_desc;
+/* = ntc_cuda::PosDesc (cuda/ntc_cuda.h:26) */
+typedef struct ntcb_pos_desc { int kind; } ntcb_pos_desc;
+/* = ntc_cuda::ModelDesc (cuda/ntc_cuda.h:29-52) */
+typedef struct ntcb_model_desc {
+    int W, H, T;
+    int nlev; ntcb_level_desc lv[NTCB_MAX_LEVELS];
+    int npos; ntcb_pos_desc pos[NTCB_MAX_POS];
+    int nin, nout;
+    int nhidden; int hidden[NTCB_MAX_HIDDEN];
+    float leak;
+    bool clamp_out;
+    float cw[NTCB_MAX_OUT];
+    float wsum;
+    int qat_bits[NTCB_MAX_CH];
+    int qat;
+    const float* qat_grid;
+    int qes_bits[NTCB_MAX_LEVELS];
+    int dct, dct_C, dct_N, dct_dc_step;
+    int dct_q[NTCB_MAX_DCT_CH];
+    const float* dct_basis;
+    const int* dct_zigzag;
+    int max_pairs, max_batch;
+    uint64_t seed;
+} ntcb_model_desc;
+/* = ntc_cuda::QesDesc (cuda/ntc_cuda.h:58-64) */
+typedef struct ntcb_qes_desc {
+    int bits[NTCB_MAX_LEVELS];
+    int live, frozen;
+    float lo[NTCB_MAX_LEVELS][NTCB_MAX_QES_CH], hi[NTCB_MAX_LEVELS][NTCB_MAX_QES_CH], range[NTCB_MAX_LEVELS][NTCB_MAX_QES_CH];
+    int grid_off[NTCB_MAX_LEVELS][NTCB_MAX_QES_CH];
+} ntcb_qes_desc;
+/* = ntc_cuda::DctDesc (cuda/ntc_cuda.h:69-76) */
+typedef struct ntcb_dct_desc {
+    int live, C, BW, BH, N, dc_step;
+    int rate_es, rate_trunc; float rate_scale; float lam_t16[16];
+    int lo_w16;
+    int deadzone;
+} ntcb_dct_desc;
+
+typedef struct ntcb_trainer ntcb_trainer;
+
+/* Trainer::Trainer() (cuda/ntc_cuda.h:80): an uninitialised trainer; touches no GPU. */
+ntcb_trainer* ntcb_create(void);
+/* Trainer::~Trainer() (cuda/ntc_cuda.h:81): frees every device buffer. */
+void ntcb_destroy(ntcb_trainer* t);
+/* Trainer::init (cuda/ntc_cuda.h:85): allocates device state on the current CUDA device and uploads
+ * z (the flat latent), p (the flat MLP) and target (W*H*nout floats in [0,1], interleaved).
+ * Returns 1 on success; 0 with a NUL-terminated reason in why[0..why_cap) otherwise. */
+int ntcb_init(ntcb_trainer* t, const ntcb_model_desc* d, const float* z, const float* p, const float* target,
+              char* why, size_t why_cap);
+/* Trainer::banner (cuda/ntc_cuda.h:86): device / runtime line; returns the full length. */
+size_t ntcb_banner(const ntcb_trainer* t, char* buf, size_t cap);
+/* Trainer::upload_model (cuda/ntc_cuda.h:88): replaces shadow latent and weights, re-snaps the decode copy. */
+void ntcb_upload_model(ntcb_trainer* t, const float* z, const float* p);
+/* Trainer::download_model (cuda/ntc_cuda.h:89): the fp32 shadow latent and the weights. */
+void ntcb_download_model(ntcb_trainer* t, float* z, float* p);
+/* Trainer::set_qes (cuda/ntc_cuda.h:93): host-fitted --qes ranges and grid table (grid_n floats), then snap. */
+void ntcb_set_qes(ntcb_trainer* t, const ntcb_qes_desc* q, const float* grid, size_t grid_n);
+/* Trainer::snap_latent (cuda/ntc_cuda.h:94): rebuild the decode copy from the shadow. */
+void ntcb_snap_latent(ntcb_trainer* t);
+/* Trainer::shadow_pull (cuda/ntc_cuda.h:95): z[off..off+n) += f * (zq - z), then snap. */
+void ntcb_shadow_pull(ntcb_trainer* t, size_t off, size_t n, float f);
+/* Trainer::download_zq (cuda/ntc_cuda.h:96): the decode buffer (the shadow when nothing is snapped). */
+void ntcb_download_zq(ntcb_trainer* t, float* zq);
+/* Trainer::set_dct (cuda/ntc_cuda.h:100): description, scale codes, symbols, step tables; rebuilds level 0 of the copy. */
+void ntcb_set_dct(ntcb_trainer* t, const ntcb_dct_desc* d, const uint8_t* code, const int16_t* sym, const int* step);
+/* Trainer::download_dct (cuda/ntc_cuda.h:101) */
+void ntcb_download_dct(ntcb_trainer* t, int16_t* sym, uint8_t* code);
+/* Trainer::download_dct_rate (cuda/ntc_cuda.h:105): every pointer may be NULL. */
+void ntcb_download_dct_rate(ntcb_trainer* t, int32_t* bits, int32_t* dbits_last_pair, int* ntrunc, int* nz_before,
+                            int* hits, int* evals);
+/* Trainer::mlp_step (cuda/ntc_cuda.h:109): one antithetic ES step on the MLP, N pairs, M-pixel minibatch. */
+void ntcb_mlp_step(ntcb_trainer* t, int it, float sigma, float lr, int N, int M);
+/* Trainer::mlp_step_fd (cuda/ntc_cuda.h:111): one central-difference step on the MLP. */
+void ntcb_mlp_step_fd(ntcb_trainer* t, int it, float h, float lr, int M);
+/* Trainer::reset_mlp_adam (cuda/ntc_cuda.h:112) */
+void ntcb_reset_mlp_adam(ntcb_trainer* t);
+/* Trainer::mlp_stats (cuda/ntc_cuda.h:114): mean batch loss and dstd (ES) or fd-rms (FD) of the last step. */
+void ntcb_mlp_stats(ntcb_trainer* t, double* batch_loss, double* diff_std);
+/* Trainer::lat_step (cuda/ntc_cuda.h:117): one latent ES step with K pairs. */
+void ntcb_lat_step(ntcb_trainer* t, int it, float sigma, float lr, int K);
+/* Trainer::qat_search (cuda/ntc_cuda.h:119): exhaustive per-texel selector search on level 0. */
+void ntcb_qat_search(ntcb_trainer* t);
+/* Trainer::decode_full (cuda/ntc_cuda.h:122): z_host NULL decodes the device latent; img gets W*H*nout floats. */
+void ntcb_decode_full(ntcb_trainer* t, const float* z_host, float* img);
+/* Trainer::debug_last_batch (cuda/ntc_cuda.h:126): minibatch pixel indices of the last MLP step.
+ * Writes min(cap, count) entries; returns count. */
+size_t ntcb_debug_last_batch(const ntcb_trainer* t, int* out, size_t cap);
+/* Trainer::debug_last_dl (cuda/ntc_cuda.h:127): per-pair (ES) or per-weight (FD) loss differences. */
+size_t ntcb_debug_last_dl(const ntcb_trainer* t, double* out, size_t cap);
+/* Trainer::debug_last_zgrad (cuda/ntc_cuda.h:128): the latent ES gradient of the last lat_step (before Adam). */
+size_t ntcb_debug_last_zgrad(const ntcb_trainer* t, float* out, size_t cap);
+
+/* ---- additions (no ntc_cuda::Trainer counterpart) ---- */
+/* Per-candidate fitness of the last ES step: lp[i] = L(w + sigma eps_i), lm[i] = L(w - sigma eps_i) for the
+ * pairs this trainer evaluated (normalised like loss_subset). Returns the pair count. */
+size_t ntcb_debug_last_fitness(const ntcb_trainer* t, double* lp, double* lm, size_t cap);
+/* Launch every subsequent kernel of this trainer on `stream` (a cudaStream_t; NULL restores the trainer's own). */
+void ntcb_set_stream(ntcb_trainer* t, void* stream);
+/* Kernel timing with CUDA events on the trainer's stream: enable, then read the summed device time and the launch
+ * count of one kernel class since the last read ("mlp_eval", "lat_eval", "lat_gather", "qat", "mlp_grad", "decode",
+ * "noise", "batch", "fd_eval"). Reading synchronises the stream. */
+void ntcb_kernel_timing(ntcb_trainer* t, int enable);
+void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int* launches);
+/* Fills n draws of the counter-based noise on the current CUDA device (no trainer needed): gauss_host[i] and
+ * u32_host[i] for index index0 + i of (seed, stream, step, pair); either pointer may be NULL. For tests. */
+void ntcb_noise_fill(uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, size_t n,
+                     float* gauss_host, uint32_t* u32_host);
+/* Measured FP32 FMA throughput of the current device in TFLOP/s (the roofline of the population kernels). */
+double ntcb_fp32_peak_tflops(void);
+/* Number of kernels this trainer has launched since creation. */
+long long ntcb_launch_count(const ntcb_trainer* t);
+
+/* Population sharding over G ranks (one process and one GPU per rank). A rank evaluates only the pairs
+ * [pair_begin, pair_end) of an N-pair ES step, regenerating their noise from the counter, and writes the
+ * per-pair fitness (lp, lm) as 2 doubles per pair into fit_dev (a DEVICE buffer of 2 * (pair_end - pair_begin)
+ * doubles, on this trainer's stream). After the caller all-gathers every rank's slice into a device buffer of
+ * 2 * N doubles (rank order = pair order), ntcb_shard_mlp_apply turns it into the ES gradient and the Adam
+ * step; every rank computes the identical update, so the replicas stay bit-identical. */
+void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, double* fit_dev);
+void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NTC_B200_H */

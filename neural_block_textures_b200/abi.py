@@ -1,0 +1,138 @@
+"""ctypes binding of libntc_b200.so (include/ntc_b200.h).
+
+The structures mirror the C description structs field for field; test_abi.py checks their layout
+against the C++ compiler's view of include/ntc_cuda.h and the reference's cuda/ntc_cuda.h. Loading
+fails loudly: there is no fallback implementation of any entry point.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+MAX_LEVELS = 3
+MAX_POS = 16
+MAX_OUT = 12
+MAX_HIDDEN = 8
+MAX_CH = 16
+MAX_QES_CH = 64
+MAX_DCT_CH = 4
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libntc_b200.so"
+
+
+class LevelDesc(C.Structure):
+    _fields_ = [("W", C.c_int), ("H", C.c_int), ("C", C.c_int), ("off", C.c_size_t), ("nearest", C.c_bool)]
+
+
+class PosDesc(C.Structure):
+    _fields_ = [("kind", C.c_int)]
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [
+        ("W", C.c_int), ("H", C.c_int), ("T", C.c_int),
+        ("nlev", C.c_int), ("lv", LevelDesc * MAX_LEVELS),
+        ("npos", C.c_int), ("pos", PosDesc * MAX_POS),
+        ("nin", C.c_int), ("nout", C.c_int),
+        ("nhidden", C.c_int), ("hidden", C.c_int * MAX_HIDDEN),
+        ("leak", C.c_float),
+        ("clamp_out", C.c_bool),
+        ("cw", C.c_float * MAX_OUT),
+        ("wsum", C.c_float),
+        ("qat_bits", C.c_int * MAX_CH),
+        ("qat", C.c_int),
+        ("qat_grid", C.POINTER(C.c_float)),
+        ("qes_bits", C.c_int * MAX_LEVELS),
+        ("dct", C.c_int), ("dct_C", C.c_int), ("dct_N", C.c_int), ("dct_dc_step", C.c_int),
+        ("dct_q", C.c_int * MAX_DCT_CH),
+        ("dct_basis", C.POINTER(C.c_float)),
+        ("dct_zigzag", C.POINTER(C.c_int)),
+        ("max_pairs", C.c_int), ("max_batch", C.c_int),
+        ("seed", C.c_uint64),
+    ]
+
+
+class QesDesc(C.Structure):
+    _fields_ = [
+        ("bits", C.c_int * MAX_LEVELS),
+        ("live", C.c_int), ("frozen", C.c_int),
+        ("lo", (C.c_float * MAX_QES_CH) * MAX_LEVELS),
+        ("hi", (C.c_float * MAX_QES_CH) * MAX_LEVELS),
+        ("range", (C.c_float * MAX_QES_CH) * MAX_LEVELS),
+        ("grid_off", (C.c_int * MAX_QES_CH) * MAX_LEVELS),
+    ]
+
+
+class DctDesc(C.Structure):
+    _fields_ = [
+        ("live", C.c_int), ("C", C.c_int), ("BW", C.c_int), ("BH", C.c_int), ("N", C.c_int), ("dc_step", C.c_int),
+        ("rate_es", C.c_int), ("rate_trunc", C.c_int), ("rate_scale", C.c_float), ("lam_t16", C.c_float * 16),
+        ("lo_w16", C.c_int),
+        ("deadzone", C.c_int),
+    ]
+
+
+_fp = C.POINTER(C.c_float)
+_dp = C.POINTER(C.c_double)
+_ip = C.POINTER(C.c_int)
+_i16p = C.POINTER(C.c_int16)
+_u8p = C.POINTER(C.c_uint8)
+_i32p = C.POINTER(C.c_int32)
+_vp = C.c_void_p
+
+# name -> (restype, argtypes); the list is the ABI surface of include/ntc_b200.h.
+SIGNATURES = {
+    "ntcb_create": (_vp, []),
+    "ntcb_destroy": (None, [_vp]),
+    "ntcb_init": (C.c_int, [_vp, C.POINTER(ModelDesc), _fp, _fp, _fp, C.c_char_p, C.c_size_t]),
+    "ntcb_banner": (C.c_size_t, [_vp, C.c_char_p, C.c_size_t]),
+    "ntcb_upload_model": (None, [_vp, _fp, _fp]),
+    "ntcb_download_model": (None, [_vp, _fp, _fp]),
+    "ntcb_set_qes": (None, [_vp, C.POINTER(QesDesc), _fp, C.c_size_t]),
+    "ntcb_snap_latent": (None, [_vp]),
+    "ntcb_shadow_pull": (None, [_vp, C.c_size_t, C.c_size_t, C.c_float]),
+    "ntcb_download_zq": (None, [_vp, _fp]),
+    "ntcb_set_dct": (None, [_vp, C.POINTER(DctDesc), _u8p, _i16p, _ip]),
+    "ntcb_download_dct": (None, [_vp, _i16p, _u8p]),
+    "ntcb_download_dct_rate": (None, [_vp, _i32p, _i32p, _ip, _ip, _ip, _ip]),
+    "ntcb_mlp_step": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int]),
+    "ntcb_mlp_step_fd": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int]),
+    "ntcb_reset_mlp_adam": (None, [_vp]),
+    "ntcb_mlp_stats": (None, [_vp, _dp, _dp]),
+    "ntcb_lat_step": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int]),
+    "ntcb_qat_search": (None, [_vp]),
+    "ntcb_decode_full": (None, [_vp, _fp, _fp]),
+    "ntcb_debug_last_batch": (C.c_size_t, [_vp, _ip, C.c_size_t]),
+    "ntcb_debug_last_dl": (C.c_size_t, [_vp, _dp, C.c_size_t]),
+    "ntcb_debug_last_zgrad": (C.c_size_t, [_vp, _fp, C.c_size_t]),
+    "ntcb_debug_last_fitness": (C.c_size_t, [_vp, _dp, _dp, C.c_size_t]),
+    "ntcb_set_stream": (None, [_vp, _vp]),
+    "ntcb_kernel_timing": (None, [_vp, C.c_int]),
+    "ntcb_kernel_time": (None, [_vp, C.c_char_p, _dp, _ip]),
+    "ntcb_launch_count": (C.c_longlong, [_vp]),
+    "ntcb_fp32_peak_tflops": (C.c_double, []),
+    "ntcb_noise_fill": (None, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_size_t, _fp, C.POINTER(C.c_uint32)]),
+    "ntcb_shard_mlp_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_mlp_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _vp]),
+}
+
+_lib = None
+
+
+def load_library(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Loads the in-tree libntc_b200.so (built by neural_block_textures_b200.build). Raises if missing."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(f"libntc_b200.so not found at {p}: build it with `python -m neural_block_textures_b200.build`")
+    lib = C.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib

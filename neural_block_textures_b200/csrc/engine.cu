@@ -1,0 +1,878 @@
+// Host orchestration of the B200 ES training backend: device state, the training steps, the flat
+// C ABI (include/ntc_b200.h) and the drop-in C++ class ntc_cuda::Trainer (include/ntc_cuda.h).
+//
+// One Engine (= ntc_cuda::Trainer::Impl) owns every device buffer of one model on one GPU and
+// launches all of its kernels on one stream. Public calls follow the reference's contract
+// (cuda/ntc_cuda.cu:699-1179): host buffers are consumed or filled before the call returns, runtime
+// failures print and exit(1), init() reports unsupported models with false + a reason.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstddef>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/ntc_b200.h"
+#include "../../include/ntc_cuda.h"
+#include "kernels.h"
+#include "kernels_snap.h"
+
+// The C description structs are the C++ ones byte for byte (main.cpp fills the C++ ones; FFI callers the C ones).
+static_assert(sizeof(ntcb_level_desc) == sizeof(ntc_cuda::LevelDesc), "LevelDesc layout");
+static_assert(offsetof(ntcb_level_desc, off) == offsetof(ntc_cuda::LevelDesc, off), "LevelDesc layout");
+static_assert(offsetof(ntcb_level_desc, nearest) == offsetof(ntc_cuda::LevelDesc, nearest), "LevelDesc layout");
+static_assert(sizeof(ntcb_model_desc) == sizeof(ntc_cuda::ModelDesc), "ModelDesc layout");
+#define NTCB_SAME_OFFSET(F) static_assert(offsetof(ntcb_model_desc, F) == offsetof(ntc_cuda::ModelDesc, F), "ModelDesc." #F);
+NTCB_SAME_OFFSET(W) NTCB_SAME_OFFSET(T) NTCB_SAME_OFFSET(nlev) NTCB_SAME_OFFSET(lv) NTCB_SAME_OFFSET(npos) NTCB_SAME_OFFSET(pos)
+NTCB_SAME_OFFSET(nin) NTCB_SAME_OFFSET(nout) NTCB_SAME_OFFSET(nhidden) NTCB_SAME_OFFSET(hidden) NTCB_SAME_OFFSET(leak)
+NTCB_SAME_OFFSET(clamp_out) NTCB_SAME_OFFSET(cw) NTCB_SAME_OFFSET(wsum) NTCB_SAME_OFFSET(qat_bits) NTCB_SAME_OFFSET(qat)
+NTCB_SAME_OFFSET(qat_grid) NTCB_SAME_OFFSET(qes_bits) NTCB_SAME_OFFSET(dct) NTCB_SAME_OFFSET(dct_C) NTCB_SAME_OFFSET(dct_N)
+NTCB_SAME_OFFSET(dct_dc_step) NTCB_SAME_OFFSET(dct_q) NTCB_SAME_OFFSET(dct_basis) NTCB_SAME_OFFSET(dct_zigzag)
+NTCB_SAME_OFFSET(max_pairs) NTCB_SAME_OFFSET(max_batch) NTCB_SAME_OFFSET(seed)
+#undef NTCB_SAME_OFFSET
+static_assert(sizeof(ntcb_qes_desc) == sizeof(ntc_cuda::QesDesc), "QesDesc layout");
+static_assert(sizeof(ntcb_dct_desc) == sizeof(ntc_cuda::DctDesc), "DctDesc layout");
+static_assert(sizeof(ntcb::QesTables) == sizeof(ntc_cuda::QesDesc), "QesTables mirrors QesDesc");
+
+namespace ntc_cuda {
+
+struct Trainer::Impl {
+    ModelDesc d{};
+    ntcb::DevModel dm{};
+    int shape = 0;
+    int P = 0;
+    long long nz = 0, npix = 0, n0 = 0;
+    int device = -1;
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+    bool ready = false;
+
+    // latent
+    float *z = nullptr, *zgrad = nullptr, *zm = nullptr, *zv = nullptr, *ztmp = nullptr, *zq = nullptr, *zdec = nullptr;
+    float* qgrid = nullptr;
+    ntcb::QesTables* qes_dev = nullptr;
+    bool qes = false;
+    float* lat_eps = nullptr; long long lat_eps_cap = 0;   // [K][nz]
+    float* dpix = nullptr; long long dpix_cap = 0;         // [K][npix]
+    std::vector<int*> lvl_xr, lvl_yr;                      // per level footprint ranges (device)
+    int* ranges = nullptr;
+    // DCT
+    bool dct = false, dct_live = false, rate_es = false, rate_trunc = false;
+    long long dct_n = 0;
+    ntcb::DctTables dtab{};
+    int16_t* dsym = nullptr; uint8_t* dcode = nullptr; int* dsteps = nullptr; float* dlam = nullptr;
+    int32_t* dbits = nullptr; int32_t* ddbits = nullptr; long long ddbits_cap = 0; int* dcnt = nullptr;
+    int dct_evals = 0, dct_last_K = 0; float rate_scale = 0.0f;
+    // MLP
+    float *w = nullptr, *wgrad = nullptr, *wm = nullptr, *wv = nullptr;
+    float *tgt = nullptr, *img = nullptr;
+    int* bidx = nullptr; float *feat_t = nullptr, *tgt_t = nullptr; int Mcap = 0, mstride = 0;
+    float* mlp_eps = nullptr; int pairs_cap = 0;
+    double* part = nullptr; long long part_cap = 0;
+    double *fit = nullptr, *dl = nullptr, *lsum = nullptr, *hh = nullptr;
+    double* fit_stats = nullptr;
+    float* gpart = nullptr; long long gpart_cap = 0;
+    float* qat_grid = nullptr; int* qat_bits = nullptr;
+    // counters
+    int mlp_t = 0, lat_t = 0, lat_step_no = 0;
+    int last_N = 0, last_M = 0, last_pairs = 0; bool last_fd = false;
+    long long launches = 0;
+    // timing
+    bool timing = false;
+    struct Pending { std::string cls; cudaEvent_t a, b; };
+    std::vector<Pending> pending;
+    std::map<std::string, std::pair<double, int>> totals;
+    // banner
+    std::string dev_name; int sm_major = 0, sm_minor = 0, sms = 0, rt_ver = 0;
+};
+
+}  // namespace ntc_cuda
+
+using Impl = ntc_cuda::Trainer::Impl;
+
+namespace {
+
+void die(const char* msg) { fprintf(stderr, "ntc_b200: %s\n", msg); exit(1); }
+
+template <class T>
+T* dalloc(size_t n) {
+    T* p = nullptr;
+    NTCB_CHECK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    return p;
+}
+template <class T>
+void dfree(T*& p) { if (p) { cudaFree(p); p = nullptr; } }
+
+// Records CUDA events around one launch of kernel class `cls` when timing is on.
+template <class F>
+void timed(Impl& I, const char* cls, int nlaunch, F&& launch) {
+    if (!I.timing) { launch(); I.launches += nlaunch; return; }
+    Impl::Pending p{cls, nullptr, nullptr};
+    NTCB_CHECK(cudaEventCreate(&p.a)); NTCB_CHECK(cudaEventCreate(&p.b));
+    NTCB_CHECK(cudaEventRecord(p.a, I.stream));
+    launch();
+    NTCB_CHECK(cudaEventRecord(p.b, I.stream));
+    I.pending.push_back(p);
+    I.launches += nlaunch;
+}
+void flush_timing(Impl& I) {
+    if (I.pending.empty()) return;
+    NTCB_CHECK(cudaStreamSynchronize(I.stream));
+    for (auto& p : I.pending) {
+        float ms = 0.0f;
+        NTCB_CHECK(cudaEventElapsedTime(&ms, p.a, p.b));
+        auto& t = I.totals[p.cls];
+        t.first += ms; t.second += 1;
+        cudaEventDestroy(p.a); cudaEventDestroy(p.b);
+    }
+    I.pending.clear();
+}
+
+void sync(Impl& I) { NTCB_CHECK(cudaStreamSynchronize(I.stream)); }
+void set_device(Impl& I) { if (I.device >= 0) NTCB_CHECK(cudaSetDevice(I.device)); }
+
+// Footprint rectangles of every texel of a level (per texel column [xb, xe), per texel row [yb, ye)):
+// nearest levels use the cell rule of qat_search (main.cpp:2095-2096); bilinear levels the rule of the
+// latent scatter (main.cpp:2015-2024): a pixel feeds texel tx if its clamped tap x0 == tx, or x1 == tx
+// with x1 != x0. The pixels of a texel form one contiguous range per axis; init() verifies that.
+bool axis_ranges(int npx, int ntex, bool nearest, std::vector<int>& lo, std::vector<int>& hi) {
+    lo.assign(ntex, npx); hi.assign(ntex, 0);
+    std::vector<int> count(ntex, 0);
+    for (int px = 0; px < npx; px++) {
+        const float u = ((float)px + 0.5f) / (float)npx;
+        int t0, t1;
+        if (nearest) {
+            const float x = u * (float)ntex;
+            t0 = t1 = std::max(0, std::min(ntex - 1, (int)std::floor(x)));
+        } else {
+            const float x = std::fmaf(u, (float)ntex, -0.5f);
+            const int x0 = (int)std::floor(x);
+            t0 = std::max(0, std::min(ntex - 1, x0));
+            t1 = std::max(0, std::min(ntex - 1, x0 + 1));
+        }
+        lo[t0] = std::min(lo[t0], px); hi[t0] = std::max(hi[t0], px + 1); count[t0]++;
+        if (t1 != t0) { lo[t1] = std::min(lo[t1], px); hi[t1] = std::max(hi[t1], px + 1); count[t1]++; }
+    }
+    for (int t = 0; t < ntex; t++)
+        if (count[t] && hi[t] - lo[t] != count[t]) return false;
+    return true;
+}
+
+void ensure_part(Impl& I, long long need) {
+    if (need <= I.part_cap) return;
+    dfree(I.part);
+    I.part = dalloc<double>((size_t)need);
+    I.part_cap = need;
+}
+void ensure_lat(Impl& I, int K) {
+    if ((long long)K * I.nz > I.lat_eps_cap) {
+        dfree(I.lat_eps);
+        I.lat_eps_cap = (long long)K * I.nz;
+        I.lat_eps = dalloc<float>((size_t)I.lat_eps_cap);
+        NTCB_CHECK(cudaMemsetAsync(I.lat_eps, 0, (size_t)I.lat_eps_cap * sizeof(float), I.stream));
+    }
+    if ((long long)K * I.npix > I.dpix_cap) {
+        dfree(I.dpix);
+        I.dpix_cap = (long long)K * I.npix;
+        I.dpix = dalloc<float>((size_t)I.dpix_cap);
+    }
+    if (I.dct && (long long)K * I.dct_n > I.ddbits_cap) {
+        dfree(I.ddbits);
+        I.ddbits_cap = (long long)K * I.dct_n;
+        I.ddbits = dalloc<int32_t>((size_t)I.ddbits_cap);
+        NTCB_CHECK(cudaMemsetAsync(I.ddbits, 0, (size_t)I.ddbits_cap * sizeof(int32_t), I.stream));
+    }
+}
+void ensure_gpart(Impl& I, long long need) {
+    if (need <= I.gpart_cap) return;
+    dfree(I.gpart);
+    I.gpart = dalloc<float>((size_t)need);
+    I.gpart_cap = need;
+}
+
+// Rows of the minibatch one population CTA covers: a multiple of the CTA's pass, about M / 4 so that the
+// grid has ~4 CTAs per candidate pair (a short last wave).
+int pop_chunk(const Impl& I, int M) {
+    const int rows = ntcb::pop_chunk_rows(I.shape);
+    if (const char* e = getenv("NTCB_POP_CHUNK")) { const int c = atoi(e); if (c >= rows && c % rows == 0) return c; }
+    const int passes = (M + rows - 1) / rows;
+    return rows * std::max(1, (passes + 3) / 4);
+}
+
+void adam_coeffs(int t, float& c1, float& c2) {
+    c1 = 1.0f - powf(0.9f, (float)t);
+    c2 = 1.0f - powf(0.999f, (float)t);
+}
+
+// The snapped decode copy (cuda/ntc_cuda.cu:920-932): --qes grid snap (a plain copy for levels without
+// bits), then the DCT snap of level 0 once live, or the pre-start clamp.
+void snap_latent_impl(Impl& I) {
+    if (!I.qes && !I.dct) return;
+    timed(I, "snap", 1, [&] { ntcb::launch_qes_snap(I.stream, I.dm, I.qes_dev, I.z, I.zq, I.qgrid, I.nz); });
+    if (I.dct) {
+        if (I.dct_live) {
+            if (I.rate_es || I.rate_trunc) NTCB_CHECK(cudaMemsetAsync(I.dcnt, 0, 2 * sizeof(int), I.stream));
+            timed(I, "dct_snap", 1, [&] {
+                ntcb::launch_dct_snap(I.stream, I.dm, I.dtab, I.z, I.zq, I.dsym, I.dcode, I.dsteps, I.dlam, I.dbits, I.dcnt);
+            });
+        } else {
+            timed(I, "snap", 1, [&] { ntcb::launch_dct_clamp0(I.stream, I.z, I.zq, I.dm.lv[0].off, I.n0); });
+        }
+    }
+}
+
+void free_all(Impl& I) {
+    dfree(I.z); dfree(I.zgrad); dfree(I.zm); dfree(I.zv); dfree(I.ztmp); dfree(I.zq); dfree(I.qgrid); dfree(I.qes_dev);
+    dfree(I.lat_eps); dfree(I.dpix); dfree(I.ranges);
+    dfree(I.dsym); dfree(I.dcode); dfree(I.dsteps); dfree(I.dlam); dfree(I.dbits); dfree(I.ddbits); dfree(I.dcnt);
+    dfree(I.w); dfree(I.wgrad); dfree(I.wm); dfree(I.wv); dfree(I.tgt); dfree(I.img);
+    dfree(I.bidx); dfree(I.feat_t); dfree(I.tgt_t); dfree(I.mlp_eps); dfree(I.part);
+    dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart);
+    dfree(I.qat_grid); dfree(I.qat_bits);
+    for (auto& p : I.pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
+    I.pending.clear();
+    if (I.own_stream) { cudaStreamDestroy(I.own_stream); I.own_stream = nullptr; }
+}
+
+bool init_impl(Impl& I, const ntc_cuda::ModelDesc& d, const float* z, const float* p, const float* target, std::string& why) {
+    using namespace ntcb;
+    I.d = d;
+    // The reference's envelope (cuda/ntc_cuda.cu:751-785), kept so that the same models are accepted.
+    int need = d.nin;
+    for (int l = 0; l < d.nhidden; l++) need = std::max(need, d.hidden[l]);
+    if (need > kMaxWidth) { why = "the B200 backend supports at most 64 units per layer (input and hidden)"; return false; }
+    if (d.nhidden < 0 || d.nhidden > kMaxHidden) { why = "too many hidden layers"; return false; }
+    if (d.nout < 1 || d.nout > kMaxOut) { why = "too many MLP outputs"; return false; }
+    if (d.nlev < 1 || d.nlev > kMaxLevels) { why = "bad level count"; return false; }
+    if (d.lv[0].C > kMaxCh) { why = "the B200 backend supports at most 16 level-0 channels"; return false; }
+    if (d.npos < 0 || d.npos > kMaxPos) { why = "too many positional features"; return false; }
+    I.qes = false;
+    for (int l = 0; l < d.nlev; l++)
+        if (d.qes_bits[l] > 0) {
+            I.qes = true;
+            if (d.qes_bits[l] < 2 || d.qes_bits[l] > 12) { why = "--qes bits out of range"; return false; }
+            if (d.lv[l].C > 64) { why = "the B200 backend supports at most 64 channels on a --qes level"; return false; }
+        }
+    I.dct = d.dct != 0; I.dct_live = false;
+    if (I.dct) {
+        if (d.dct_N != 8) { why = "--dct-q: the B200 backend supports --dct-block 8 only"; return false; }
+        if (d.dct_C < 1 || d.dct_C > 4 || d.dct_C != d.lv[0].C) { why = "--dct-q: level 0 must have 1..4 channels (= dct_C)"; return false; }
+        if (!d.lv[0].nearest || d.lv[0].W != d.W || d.lv[0].H != d.H || d.W % 8 != 0 || d.H % 8 != 0) {
+            why = "--dct-q: level 0 must be a full-resolution nearest level with a size that is a multiple of 8"; return false;
+        }
+        if (!d.dct_basis) { why = "--dct-q needs the host basis table"; return false; }
+        if (!d.dct_zigzag) { why = "--dct-q needs the host zigzag table"; return false; }
+        if (d.dct_dc_step < 1 || d.dct_dc_step > 64) { why = "--dct-q: DC step out of range"; return false; }
+    }
+    if ((long long)d.W * d.H >= (1ll << 28)) { why = "the B200 backend supports images below 2^28 pixels"; return false; }
+    if (d.W < 1 || d.H < 1) { why = "empty image"; return false; }
+    if (d.max_pairs < 1 || d.max_batch < 1) { why = "bad pair / batch counts"; return false; }
+    {
+        int ncur = d.nin; long long n = 0;
+        for (int l = 0; l < d.nhidden; l++) { n += (long long)d.hidden[l] * ncur + d.hidden[l]; ncur = d.hidden[l]; }
+        n += (long long)d.nout * ncur + d.nout;
+        if (n * 4 > 48 * 1024) { why = "the B200 backend supports MLPs up to 12288 weights"; return false; }
+        I.P = (int)n;
+    }
+    int nin_check = 0;
+    for (int l = 0; l < d.nlev; l++) nin_check += d.lv[l].C;
+    nin_check += 2 * d.npos;
+    if (nin_check != d.nin) { why = "nin does not match the level channels plus the positional features"; return false; }
+    for (int q = 0; q < d.npos; q++)
+        if (d.pos[q].kind == ntc_cuda::PK_LV1LOCAL && d.nlev < 2) { why = "lv1local needs a second level"; return false; }
+    if (d.qat > 0) {
+        if (!d.lv[0].nearest) { why = "--qat needs nearest sampling on level 0"; return false; }
+        if (!d.qat_grid) { why = "--qat needs the host grid table"; return false; }
+        for (int c = 0; c < d.lv[0].C; c++)
+            if (d.qat_bits[c] < 1 || d.qat_bits[c] > 8) { why = "--qat bits out of range"; return false; }
+    }
+
+    if (cudaGetDevice(&I.device) != cudaSuccess) { why = "no CUDA device"; return false; }
+    cudaDeviceProp prop;
+    NTCB_CHECK(cudaGetDeviceProperties(&prop, I.device));
+    I.dev_name = prop.name; I.sm_major = prop.major; I.sm_minor = prop.minor; I.sms = prop.multiProcessorCount;
+    NTCB_CHECK(cudaRuntimeGetVersion(&I.rt_ver));
+    if (prop.major != 10) { why = "libntc_b200 is built for sm_100a (B200) only; this device is sm_" + std::to_string(prop.major * 10 + prop.minor); return false; }
+    NTCB_CHECK(cudaStreamCreateWithFlags(&I.own_stream, cudaStreamNonBlocking));
+    I.stream = I.own_stream;
+
+    // device model
+    DevModel& m = I.dm;
+    memset(&m, 0, sizeof(m));
+    m.W = d.W; m.H = d.H; m.nlev = d.nlev;
+    I.nz = 0;
+    for (int l = 0; l < d.nlev; l++) {
+        m.lv[l].W = d.lv[l].W; m.lv[l].H = d.lv[l].H; m.lv[l].C = d.lv[l].C; m.lv[l].nearest = d.lv[l].nearest ? 1 : 0;
+        m.lv[l].off = (long long)d.lv[l].off;
+        I.nz = std::max<long long>(I.nz, (long long)d.lv[l].off + (long long)d.lv[l].W * d.lv[l].H * d.lv[l].C);
+    }
+    m.npos = d.npos;
+    for (int q = 0; q < d.npos; q++) m.pos_kind[q] = d.pos[q].kind;
+    m.nin = d.nin; m.nout = d.nout; m.nhidden = d.nhidden;
+    for (int l = 0; l < d.nhidden; l++) m.hidden[l] = d.hidden[l];
+    m.leak = d.leak; m.clamp_out = d.clamp_out ? 1 : 0;
+    for (int c = 0; c < kMaxOut; c++) m.cw[c] = c < d.nout ? d.cw[c] : 0.0f;
+    m.wsum = d.wsum; m.P = I.P;
+    I.shape = shape_id(m);
+    if (const char* e = getenv("NTCB_FORCE_GENERIC")) if (atoi(e)) I.shape = 0;
+    I.npix = (long long)d.W * d.H;
+    I.n0 = (long long)d.lv[0].W * d.lv[0].H * d.lv[0].C;
+
+    // footprint ranges per level
+    {
+        std::vector<int> all;
+        std::vector<size_t> offs;
+        for (int l = 0; l < d.nlev; l++) {
+            std::vector<int> xb, xe, yb, ye;
+            const bool nr = d.lv[l].nearest;
+            if (!axis_ranges(d.W, d.lv[l].W, nr, xb, xe) || !axis_ranges(d.H, d.lv[l].H, nr, yb, ye)) {
+                why = "a texel footprint is not contiguous (unsupported level geometry)"; free_all(I); return false;
+            }
+            offs.push_back(all.size());
+            all.insert(all.end(), xb.begin(), xb.end()); all.insert(all.end(), xe.begin(), xe.end());
+            offs.push_back(all.size());
+            all.insert(all.end(), yb.begin(), yb.end()); all.insert(all.end(), ye.begin(), ye.end());
+        }
+        I.ranges = dalloc<int>(all.size());
+        NTCB_CHECK(cudaMemcpy(I.ranges, all.data(), all.size() * sizeof(int), cudaMemcpyHostToDevice));
+        I.lvl_xr.clear(); I.lvl_yr.clear();
+        for (int l = 0; l < d.nlev; l++) { I.lvl_xr.push_back(I.ranges + offs[2 * l]); I.lvl_yr.push_back(I.ranges + offs[2 * l + 1]); }
+    }
+
+    // buffers
+    I.z = dalloc<float>(I.nz); I.zgrad = dalloc<float>(I.nz); I.zm = dalloc<float>(I.nz); I.zv = dalloc<float>(I.nz);
+    I.ztmp = dalloc<float>(I.nz);
+    NTCB_CHECK(cudaMemset(I.zm, 0, I.nz * sizeof(float))); NTCB_CHECK(cudaMemset(I.zv, 0, I.nz * sizeof(float)));
+    NTCB_CHECK(cudaMemset(I.zgrad, 0, I.nz * sizeof(float)));
+    if (I.qes || I.dct) {
+        I.zq = dalloc<float>(I.nz);
+        I.qes_dev = dalloc<QesTables>(1);
+        NTCB_CHECK(cudaMemset(I.qes_dev, 0, sizeof(QesTables)));
+        QesTables qt; memset(&qt, 0, sizeof(qt));
+        for (int l = 0; l < d.nlev; l++) qt.bits[l] = d.qes_bits[l];
+        NTCB_CHECK(cudaMemcpy(I.qes_dev, &qt, sizeof(qt), cudaMemcpyHostToDevice));
+        if (I.qes) {
+            const size_t ng = (size_t)kMaxLevels * 64 * 4096;
+            I.qgrid = dalloc<float>(ng);
+            NTCB_CHECK(cudaMemset(I.qgrid, 0, ng * sizeof(float)));
+        }
+        if (I.dct) {
+            I.dct_n = (long long)(d.W / 8) * (d.H / 8) * d.dct_C;
+            I.dsym = dalloc<int16_t>((size_t)I.dct_n * 64); I.dcode = dalloc<uint8_t>((size_t)I.dct_n);
+            I.dsteps = dalloc<int>((size_t)d.dct_C * 16 * 64); I.dlam = dalloc<float>(16);
+            I.dbits = dalloc<int32_t>((size_t)I.dct_n); I.dcnt = dalloc<int>(3);
+            NTCB_CHECK(cudaMemset(I.dsym, 0, (size_t)I.dct_n * 64 * sizeof(int16_t)));
+            NTCB_CHECK(cudaMemset(I.dcode, 0, (size_t)I.dct_n));
+            NTCB_CHECK(cudaMemset(I.dsteps, 0, (size_t)d.dct_C * 16 * 64 * sizeof(int)));
+            NTCB_CHECK(cudaMemset(I.dlam, 0, 16 * sizeof(float)));
+            NTCB_CHECK(cudaMemset(I.dbits, 0, (size_t)I.dct_n * sizeof(int32_t)));
+            NTCB_CHECK(cudaMemset(I.dcnt, 0, 3 * sizeof(int)));
+            DctTables& T = I.dtab;
+            memset(&T, 0, sizeof(T));
+            T.C = d.dct_C; T.BW = d.W / 8; T.BH = d.H / 8; T.dc_step = d.dct_dc_step; T.deadzone = 1; T.lo_w16 = 16; T.rate_on = 0;
+            memcpy(T.basis, d.dct_basis, 64 * sizeof(float));
+            memcpy(T.zigzag, d.dct_zigzag, 64 * sizeof(int));
+        }
+        I.zdec = I.zq;
+    } else {
+        I.zdec = I.z;
+    }
+    I.w = dalloc<float>(I.P); I.wgrad = dalloc<float>(I.P); I.wm = dalloc<float>(I.P); I.wv = dalloc<float>(I.P);
+    NTCB_CHECK(cudaMemset(I.wm, 0, I.P * sizeof(float))); NTCB_CHECK(cudaMemset(I.wv, 0, I.P * sizeof(float)));
+    NTCB_CHECK(cudaMemset(I.wgrad, 0, I.P * sizeof(float)));
+    I.tgt = dalloc<float>((size_t)I.npix * d.nout); I.img = dalloc<float>((size_t)I.npix * d.nout);
+    I.Mcap = d.max_batch;
+    I.mstride = (I.Mcap + 31) / 32 * 32;
+    I.bidx = dalloc<int>(I.Mcap);
+    NTCB_CHECK(cudaMemset(I.bidx, 0, I.Mcap * sizeof(int)));
+    I.feat_t = dalloc<float>((size_t)d.nin * I.mstride);
+    I.tgt_t = dalloc<float>((size_t)d.nout * I.mstride);
+    I.pairs_cap = d.max_pairs;
+    I.mlp_eps = dalloc<float>((size_t)I.pairs_cap * I.P);
+    const int cands = std::max(I.pairs_cap, I.P);
+    I.fit = dalloc<double>(2 * (size_t)cands);
+    I.dl = dalloc<double>(cands); I.lsum = dalloc<double>(cands); I.hh = dalloc<double>(I.P);
+    NTCB_CHECK(cudaMemset(I.dl, 0, cands * sizeof(double))); NTCB_CHECK(cudaMemset(I.lsum, 0, cands * sizeof(double)));
+    NTCB_CHECK(cudaMemset(I.fit, 0, 2 * cands * sizeof(double)));
+    I.fit_stats = dalloc<double>(2);
+    ensure_part(I, (long long)cands * 2 * 8);
+    ensure_gpart(I, (long long)((I.pairs_cap + 63) / 64 + 1) * I.P);
+    if (d.qat > 0) {
+        I.qat_grid = dalloc<float>(9 * 257);
+        NTCB_CHECK(cudaMemcpy(I.qat_grid, d.qat_grid, 9 * 257 * sizeof(float), cudaMemcpyHostToDevice));
+        I.qat_bits = dalloc<int>(kMaxCh);
+        NTCB_CHECK(cudaMemcpy(I.qat_bits, d.qat_bits, kMaxCh * sizeof(int), cudaMemcpyHostToDevice));
+    }
+    NTCB_CHECK(cudaMemcpy(I.tgt, target, (size_t)I.npix * d.nout * sizeof(float), cudaMemcpyHostToDevice));
+    NTCB_CHECK(cudaDeviceSynchronize());
+    I.ready = true;
+    return true;
+}
+
+void require_ready(const Impl& I) { if (!I.ready) die("trainer used before a successful init"); }
+
+void upload_model_impl(Impl& I, const float* z, const float* p) {
+    require_ready(I); set_device(I);
+    NTCB_CHECK(cudaMemcpyAsync(I.z, z, I.nz * sizeof(float), cudaMemcpyHostToDevice, I.stream));
+    NTCB_CHECK(cudaMemcpyAsync(I.w, p, I.P * sizeof(float), cudaMemcpyHostToDevice, I.stream));
+    snap_latent_impl(I);
+    sync(I);
+}
+
+void download_model_impl(Impl& I, float* z, float* p) {
+    require_ready(I); set_device(I);
+    NTCB_CHECK(cudaMemcpyAsync(z, I.z, I.nz * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
+    NTCB_CHECK(cudaMemcpyAsync(p, I.w, I.P * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+}
+
+void draw_batch(Impl& I, int it, int M) {
+    timed(I, "batch", 1, [&] { ntcb::launch_batch(I.stream, I.dm, I.d.seed, it, M, I.mstride, I.zdec, I.tgt, I.bidx, I.feat_t, I.tgt_t); });
+    I.last_M = M;
+}
+
+// Evaluates the ES pairs [p0, p1) of step `it` on the current minibatch; writes (lp, lm) per pair to fit.
+void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* fit) {
+    const int n = p1 - p0;
+    if (n <= 0) return;
+    timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, p0, n, I.P, I.mlp_eps); });
+    ntcb::PopArgs a{};
+    a.mode = 0; a.it = it; a.sigma = sigma; a.fd_h = 0.0f; a.cand_begin = p0; a.ncand = n;
+    a.M = M; a.mstride = I.mstride; a.chunk = pop_chunk(I, M);
+    a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t;
+    const int chunks = ntcb::pop_chunks(M, a.chunk);
+    ensure_part(I, (long long)n * 2 * chunks);
+    a.part = I.part;
+    timed(I, "mlp_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, n, chunks, 3.0 * (double)I.d.wsum * M, fit); });
+}
+
+// ES gradient from the fitness of all N pairs (pair order) and the Adam step on the weights.
+void es_apply(Impl& I, int it, float sigma, float lr, int N, const double* fit_all, bool regenerate_noise) {
+    if (regenerate_noise) timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, 0, N, I.P, I.mlp_eps); });
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit_all, N, I.dl, I.lsum); });
+    const float scale = 1.0f / (2.0f * (float)N * sigma);
+    const int seglen = N <= 256 ? N : 64;
+    const int nseg = (N + seglen - 1) / seglen;
+    ensure_gpart(I, (long long)nseg * I.P);
+    timed(I, "mlp_grad", 2, [&] {
+        ntcb::launch_es_grad_partial(I.stream, I.dl, I.mlp_eps, N, I.P, scale, seglen, I.gpart);
+        I.mlp_t++;
+        float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
+        ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
+    });
+    I.last_N = N; I.last_fd = false; I.last_pairs = N;
+}
+
+void mlp_step_impl(Impl& I, int it, float sigma, float lr, int N, int M) {
+    require_ready(I); set_device(I);
+    if (N > I.pairs_cap || M > I.Mcap || N < 1 || M < 1) {
+        fprintf(stderr, "ntc_b200: MLP step with %d pairs / %d pixels exceeds the buffers sized at init (%d / %d)\n", N, M, I.pairs_cap, I.Mcap);
+        exit(1);
+    }
+    draw_batch(I, it, M);
+    es_eval_pairs(I, it, sigma, M, 0, N, I.fit);
+    es_apply(I, it, sigma, lr, N, I.fit, false);
+}
+
+void mlp_step_fd_impl(Impl& I, int it, float h, float lr, int M) {
+    require_ready(I); set_device(I);
+    if (M > I.Mcap || M < 1) {
+        fprintf(stderr, "ntc_b200: FD step with %d pixels exceeds the buffers sized at init (%d)\n", M, I.Mcap);
+        exit(1);
+    }
+    draw_batch(I, it, M);
+    // the unperturbed loss for the stats line: one sigma-0 "pair" (cuda/ntc_cuda.cu:1059-1068)
+    ntcb::PopArgs a{};
+    a.mode = 0; a.it = it; a.sigma = 0.0f; a.cand_begin = 0; a.ncand = 1; a.M = M; a.mstride = I.mstride;
+    a.chunk = pop_chunk(I, M); a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t;
+    const int chunks = ntcb::pop_chunks(M, a.chunk);
+    ensure_part(I, (long long)std::max(1, I.P) * 2 * chunks);
+    a.part = I.part;
+    const double norm = 3.0 * (double)I.d.wsum * M;
+    timed(I, "fd_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, 1, chunks, norm, I.fit_stats); });
+    // central differences over every weight (both signs in one CTA)
+    a.mode = 1; a.fd_h = h; a.ncand = I.P;
+    timed(I, "fd_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
+    timed(I, "mlp_finish", 2, [&] {
+        ntcb::launch_pop_finish(I.stream, I.part, I.P, chunks, norm, I.fit);
+        ntcb::launch_fd_reduce(I.stream, I.fit, I.w, h, I.P, I.dl, I.hh);
+    });
+    timed(I, "mlp_grad", 1, [&] {
+        I.mlp_t++;
+        float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
+        ntcb::launch_fd_grad_adam(I.stream, I.dl, I.hh, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
+    });
+    I.last_N = I.P; I.last_fd = true; I.last_pairs = 0;
+}
+
+void mlp_stats_impl(Impl& I, double& batch_loss, double& diff_std) {
+    require_ready(I); set_device(I);
+    if (I.last_N == 0) { batch_loss = 0; diff_std = 0; return; }
+    if (!I.last_fd) {
+        std::vector<double> dl(I.last_N), ls(I.last_N);
+        NTCB_CHECK(cudaMemcpyAsync(dl.data(), I.dl, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        NTCB_CHECK(cudaMemcpyAsync(ls.data(), I.lsum, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        sync(I);
+        double mean = 0, mean2 = 0, lmean = 0;
+        for (int i = 0; i < I.last_N; i++) { mean += dl[i]; mean2 += dl[i] * dl[i]; lmean += ls[i]; }
+        mean /= I.last_N; mean2 /= I.last_N; lmean /= I.last_N;
+        diff_std = std::sqrt(std::max(0.0, mean2 - mean * mean));
+        batch_loss = lmean;
+    } else {
+        std::vector<double> dl(I.P); double l0[2];
+        NTCB_CHECK(cudaMemcpyAsync(dl.data(), I.dl, I.P * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        NTCB_CHECK(cudaMemcpyAsync(l0, I.fit_stats, 2 * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        sync(I);
+        double ss = 0;
+        for (int j = 0; j < I.P; j++) ss += dl[j] * dl[j];
+        diff_std = std::sqrt(ss / I.P);
+        batch_loss = 0.5 * (l0[0] + l0[1]);
+    }
+}
+
+void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
+    (void)it;
+    require_ready(I); set_device(I);
+    if (K < 1) die("lat_step needs K >= 1 pairs");
+    const bool qat = I.d.qat > 0;
+    unsigned mask = 0;
+    for (int l = 0; l < I.d.nlev; l++) if (!(qat && l == 0)) mask |= 1u << l;
+    NTCB_CHECK(cudaMemsetAsync(I.zgrad, 0, I.nz * sizeof(float), I.stream));
+    const bool rate = I.dct_live && I.rate_es;
+    if (rate) NTCB_CHECK(cudaMemsetAsync(I.dcnt + 2, 0, sizeof(int), I.stream));
+    I.dct_evals = rate ? (int)(I.dct_n * K) : 0;
+    const int step = I.lat_step_no;
+    if (mask) {
+        ensure_lat(I, K);
+        int nact = 0;
+        for (int l = 0; l < I.d.nlev; l++) if (mask & (1u << l)) nact++;
+        timed(I, "lat_noise", nact, [&] { ntcb::launch_lat_noise(I.stream, I.d.seed, step, K, I.dm, mask, I.nz, I.lat_eps); });
+        const float inv_px = 1.0f / (3.0f * I.d.wsum * (float)I.d.W * (float)I.d.H);
+        timed(I, "lat_eval", 1, [&] {
+            ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, I.dpix);
+        });
+        ntcb::RateTerm rt{nullptr, 0.0f, 0, 0};
+        if (rate) {
+            timed(I, "dct_rate", 1, [&] {
+                ntcb::launch_dct_rate_pairs(I.stream, I.dm, I.dtab, K, sigma, I.z, I.lat_eps, I.nz, I.dcode, I.dsteps, I.dlam, I.ddbits, I.dcnt + 2);
+            });
+            rt.dbits = I.ddbits; rt.rate_scale = I.rate_scale; rt.BW = I.dtab.BW; rt.C = I.dtab.C;
+            I.dct_last_K = K;
+        }
+        const float scale = 1.0f / (2.0f * (float)K * sigma);
+        for (int l = 0; l < I.d.nlev; l++) {
+            if (!(mask & (1u << l))) continue;
+            const ntcb::RateTerm r = (l == 0) ? rt : ntcb::RateTerm{nullptr, 0.0f, 0, 0};
+            timed(I, "lat_gather", 1, [&] {
+                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], I.dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad);
+            });
+        }
+    }
+    timed(I, "adam", 1, [&] {
+        I.lat_t++;
+        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
+        ntcb::launch_adam(I.stream, I.z, I.zgrad, I.zm, I.zv, I.nz, lr, c1, c2);
+    });
+    snap_latent_impl(I);
+    I.lat_step_no++;
+}
+
+void qat_search_impl(Impl& I) {
+    require_ready(I); set_device(I);
+    if (I.d.qat <= 0) die("qat_search without --qat in the model description");
+    timed(I, "qat", 1, [&] {
+        ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits);
+    });
+    if (I.zdec != I.z)
+        NTCB_CHECK(cudaMemcpyAsync(I.z + I.dm.lv[0].off, I.zdec + I.dm.lv[0].off, I.n0 * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+}
+
+void decode_full_impl(Impl& I, const float* z_host, float* img) {
+    require_ready(I); set_device(I);
+    const float* src = I.zdec;
+    if (z_host) {
+        NTCB_CHECK(cudaMemcpyAsync(I.ztmp, z_host, I.nz * sizeof(float), cudaMemcpyHostToDevice, I.stream));
+        src = I.ztmp;
+    }
+    timed(I, "decode", 1, [&] { ntcb::launch_decode(I.stream, I.shape, I.dm, I.w, src, I.img); });
+    NTCB_CHECK(cudaMemcpyAsync(img, I.img, (size_t)I.npix * I.d.nout * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+}
+
+void set_qes_impl(Impl& I, const ntc_cuda::QesDesc& q, const float* grid, size_t grid_n) {
+    require_ready(I); set_device(I);
+    if (!I.qes) die("set_qes without a --qes level in the model description");
+    if (grid_n > (size_t)ntcb::kMaxLevels * 64 * 4096) die("--qes grid table too large");
+    NTCB_CHECK(cudaMemcpyAsync(I.qes_dev, &q, sizeof(q), cudaMemcpyHostToDevice, I.stream));
+    if (grid_n) NTCB_CHECK(cudaMemcpyAsync(I.qgrid, grid, grid_n * sizeof(float), cudaMemcpyHostToDevice, I.stream));
+    snap_latent_impl(I);
+    sync(I);
+}
+
+void set_dct_impl(Impl& I, const ntc_cuda::DctDesc& d, const uint8_t* code, const int16_t* sym, const int* step) {
+    require_ready(I); set_device(I);
+    if (!I.dct) die("set_dct without --dct-q in the model description");
+    if (d.C != I.d.dct_C || (long long)d.BW * d.BH * d.C != I.dct_n || d.N != 8) die("set_dct description mismatch");
+    ntcb::DctTables& T = I.dtab;
+    T.C = d.C; T.BW = d.BW; T.BH = d.BH; T.dc_step = d.dc_step; T.deadzone = d.deadzone; T.lo_w16 = d.lo_w16;
+    T.rate_on = (d.rate_es || d.rate_trunc) ? 1 : 0;
+    I.rate_es = d.rate_es != 0; I.rate_trunc = d.rate_trunc != 0; I.rate_scale = d.rate_scale;
+    NTCB_CHECK(cudaMemcpyAsync(I.dlam, d.lam_t16, 16 * sizeof(float), cudaMemcpyHostToDevice, I.stream));
+    NTCB_CHECK(cudaMemcpyAsync(I.dsteps, step, (size_t)d.C * 16 * 64 * sizeof(int), cudaMemcpyHostToDevice, I.stream));
+    NTCB_CHECK(cudaMemcpyAsync(I.dcode, code, (size_t)I.dct_n, cudaMemcpyHostToDevice, I.stream));
+    NTCB_CHECK(cudaMemcpyAsync(I.dsym, sym, (size_t)I.dct_n * 64 * sizeof(int16_t), cudaMemcpyHostToDevice, I.stream));
+    I.dct_live = true;
+    timed(I, "dct_recon", 1, [&] { ntcb::launch_dct_recon(I.stream, I.dm, I.dtab, I.dsym, I.dcode, I.dsteps, I.zq, I.dbits); });
+    sync(I);
+}
+
+void download_dct_rate_impl(Impl& I, int32_t* bits, int32_t* dbl, int* ntrunc, int* nz_before, int* hits, int* evals) {
+    require_ready(I); set_device(I);
+    if (!I.dct) return;
+    if (bits) NTCB_CHECK(cudaMemcpyAsync(bits, I.dbits, (size_t)I.dct_n * sizeof(int32_t), cudaMemcpyDeviceToHost, I.stream));
+    if (dbl) {
+        if (I.ddbits && I.dct_last_K > 0)
+            NTCB_CHECK(cudaMemcpyAsync(dbl, I.ddbits + (long long)(I.dct_last_K - 1) * I.dct_n, (size_t)I.dct_n * sizeof(int32_t),
+                                       cudaMemcpyDeviceToHost, I.stream));
+        else memset(dbl, 0, (size_t)I.dct_n * sizeof(int32_t));
+    }
+    int cnt[3];
+    NTCB_CHECK(cudaMemcpyAsync(cnt, I.dcnt, 3 * sizeof(int), cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+    if (ntrunc) *ntrunc = cnt[0];
+    if (nz_before) *nz_before = cnt[1];
+    if (hits) *hits = cnt[2];
+    if (evals) *evals = I.dct_evals;
+}
+
+
+void shadow_pull_impl(Impl& I, size_t off, size_t n, float f) {
+    require_ready(I); set_device(I);
+    if (!I.zq || n == 0) return;
+    if ((long long)(off + n) > I.nz) die("shadow_pull range outside the latent");
+    timed(I, "snap", 1, [&] { ntcb::launch_shadow_pull(I.stream, I.z, I.zq, (long long)off, (long long)n, f); });
+    snap_latent_impl(I);
+}
+void download_zq_impl(Impl& I, float* zq) {
+    require_ready(I); set_device(I);
+    NTCB_CHECK(cudaMemcpyAsync(zq, I.zdec, I.nz * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+}
+void download_dct_impl(Impl& I, int16_t* sym, uint8_t* code) {
+    require_ready(I); set_device(I);
+    if (!I.dct) return;
+    NTCB_CHECK(cudaMemcpyAsync(sym, I.dsym, (size_t)I.dct_n * 64 * sizeof(int16_t), cudaMemcpyDeviceToHost, I.stream));
+    NTCB_CHECK(cudaMemcpyAsync(code, I.dcode, (size_t)I.dct_n, cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+}
+void reset_mlp_adam_impl(Impl& I) {
+    require_ready(I); set_device(I);
+    NTCB_CHECK(cudaMemsetAsync(I.wm, 0, I.P * sizeof(float), I.stream));
+    NTCB_CHECK(cudaMemsetAsync(I.wv, 0, I.P * sizeof(float), I.stream));
+    I.mlp_t = 0;
+}
+
+std::string banner_impl(const Impl& I) {
+    char buf[320];
+    snprintf(buf, sizeof(buf), "%s (sm_%d%d, %d SMs), CUDA runtime %d.%d, B200 backend (libntc_b200), MLP kernels %s",
+             I.dev_name.c_str(), I.sm_major, I.sm_minor, I.sms, I.rt_ver / 1000, (I.rt_ver % 1000) / 10,
+             I.shape ? "register-tiled fixed shape" : "runtime-shaped");
+    return buf;
+}
+
+template <class T>
+size_t copy_out(const Impl& I, const T* dev, size_t count, T* out, size_t cap) {
+    const size_t n = std::min(count, cap);
+    if (n && out) {
+        NTCB_CHECK(cudaMemcpyAsync(out, dev, n * sizeof(T), cudaMemcpyDeviceToHost, I.stream));
+        NTCB_CHECK(cudaStreamSynchronize(I.stream));
+    }
+    return count;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+struct ntcb_trainer { Impl impl; };
+
+extern "C" {
+
+ntcb_trainer* ntcb_create(void) { return new ntcb_trainer(); }
+void ntcb_destroy(ntcb_trainer* t) {
+    if (!t) return;
+    if (t->impl.ready || t->impl.own_stream) { set_device(t->impl); flush_timing(t->impl); free_all(t->impl); }
+    delete t;
+}
+int ntcb_init(ntcb_trainer* t, const ntcb_model_desc* d, const float* z, const float* p, const float* target, char* why, size_t why_cap) {
+    std::string reason;
+    if (t->impl.ready) { reason = "trainer already initialised"; }
+    else if (init_impl(t->impl, *reinterpret_cast<const ntc_cuda::ModelDesc*>(d), z, p, target, reason)) {
+        upload_model_impl(t->impl, z, p);
+        return 1;
+    }
+    if (why && why_cap) { strncpy(why, reason.c_str(), why_cap - 1); why[why_cap - 1] = 0; }
+    return 0;
+}
+size_t ntcb_banner(const ntcb_trainer* t, char* buf, size_t cap) {
+    const std::string b = banner_impl(t->impl);
+    if (buf && cap) { strncpy(buf, b.c_str(), cap - 1); buf[cap - 1] = 0; }
+    return b.size();
+}
+void ntcb_upload_model(ntcb_trainer* t, const float* z, const float* p) { upload_model_impl(t->impl, z, p); }
+void ntcb_download_model(ntcb_trainer* t, float* z, float* p) { download_model_impl(t->impl, z, p); }
+void ntcb_set_qes(ntcb_trainer* t, const ntcb_qes_desc* q, const float* grid, size_t grid_n) {
+    set_qes_impl(t->impl, *reinterpret_cast<const ntc_cuda::QesDesc*>(q), grid, grid_n);
+}
+void ntcb_snap_latent(ntcb_trainer* t) { require_ready(t->impl); set_device(t->impl); snap_latent_impl(t->impl); sync(t->impl); }
+void ntcb_shadow_pull(ntcb_trainer* t, size_t off, size_t n, float f) { shadow_pull_impl(t->impl, off, n, f); }
+void ntcb_download_zq(ntcb_trainer* t, float* zq) { download_zq_impl(t->impl, zq); }
+void ntcb_set_dct(ntcb_trainer* t, const ntcb_dct_desc* d, const uint8_t* code, const int16_t* sym, const int* step) {
+    set_dct_impl(t->impl, *reinterpret_cast<const ntc_cuda::DctDesc*>(d), code, sym, step);
+}
+void ntcb_download_dct(ntcb_trainer* t, int16_t* sym, uint8_t* code) { download_dct_impl(t->impl, sym, code); }
+void ntcb_download_dct_rate(ntcb_trainer* t, int32_t* bits, int32_t* dbl, int* ntrunc, int* nz_before, int* hits, int* evals) {
+    download_dct_rate_impl(t->impl, bits, dbl, ntrunc, nz_before, hits, evals);
+}
+void ntcb_mlp_step(ntcb_trainer* t, int it, float sigma, float lr, int N, int M) { mlp_step_impl(t->impl, it, sigma, lr, N, M); }
+void ntcb_mlp_step_fd(ntcb_trainer* t, int it, float h, float lr, int M) { mlp_step_fd_impl(t->impl, it, h, lr, M); }
+void ntcb_reset_mlp_adam(ntcb_trainer* t) { reset_mlp_adam_impl(t->impl); }
+void ntcb_mlp_stats(ntcb_trainer* t, double* batch_loss, double* diff_std) {
+    double a = 0, b = 0;
+    mlp_stats_impl(t->impl, a, b);
+    if (batch_loss) *batch_loss = a;
+    if (diff_std) *diff_std = b;
+}
+void ntcb_lat_step(ntcb_trainer* t, int it, float sigma, float lr, int K) { lat_step_impl(t->impl, it, sigma, lr, K); }
+void ntcb_qat_search(ntcb_trainer* t) { qat_search_impl(t->impl); }
+void ntcb_decode_full(ntcb_trainer* t, const float* z_host, float* img) { decode_full_impl(t->impl, z_host, img); }
+size_t ntcb_debug_last_batch(const ntcb_trainer* t, int* out, size_t cap) {
+    const Impl& I = t->impl;
+    if (!I.ready) return 0;
+    return copy_out(I, I.bidx, (size_t)I.last_M, out, cap);
+}
+size_t ntcb_debug_last_dl(const ntcb_trainer* t, double* out, size_t cap) {
+    const Impl& I = t->impl;
+    if (!I.ready) return 0;
+    return copy_out(I, I.dl, (size_t)I.last_N, out, cap);
+}
+size_t ntcb_debug_last_zgrad(const ntcb_trainer* t, float* out, size_t cap) {
+    const Impl& I = t->impl;
+    if (!I.ready) return 0;
+    return copy_out(I, I.zgrad, (size_t)I.nz, out, cap);
+}
+size_t ntcb_debug_last_fitness(const ntcb_trainer* t, double* lp, double* lm, size_t cap) {
+    const Impl& I = t->impl;
+    if (!I.ready) return 0;
+    const size_t n = (size_t)I.last_pairs;
+    std::vector<double> f(2 * n);
+    copy_out(I, I.fit, 2 * n, f.data(), 2 * n);
+    for (size_t i = 0; i < std::min(n, cap); i++) { if (lp) lp[i] = f[2 * i]; if (lm) lm[i] = f[2 * i + 1]; }
+    return n;
+}
+void ntcb_set_stream(ntcb_trainer* t, void* stream) {
+    Impl& I = t->impl;
+    I.stream = stream ? (cudaStream_t)stream : I.own_stream;
+}
+void ntcb_kernel_timing(ntcb_trainer* t, int enable) {
+    Impl& I = t->impl;
+    flush_timing(I);
+    I.timing = enable != 0;
+}
+void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int* launches) {
+    Impl& I = t->impl;
+    flush_timing(I);
+    auto it = I.totals.find(kernel ? kernel : "");
+    if (it == I.totals.end()) { if (total_ms) *total_ms = 0.0; if (launches) *launches = 0; return; }
+    if (total_ms) *total_ms = it->second.first;
+    if (launches) *launches = it->second.second;
+    I.totals.erase(it);
+}
+long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
+double ntcb_fp32_peak_tflops(void) {
+    int dev = 0; cudaDeviceProp prop;
+    NTCB_CHECK(cudaGetDevice(&dev));
+    NTCB_CHECK(cudaGetDeviceProperties(&prop, dev));
+    return ntcb::measure_ffma_tflops(prop.multiProcessorCount);
+}
+void ntcb_noise_fill(uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, size_t n,
+                     float* gauss_host, uint32_t* u32_host) {
+    if (n == 0) return;
+    float* g = dalloc<float>(n);
+    uint32_t* u = dalloc<uint32_t>(n);
+    ntcb::launch_noise_fill(nullptr, seed, stream, step, pair, index0, (long long)n, g, u);
+    if (gauss_host) NTCB_CHECK(cudaMemcpy(gauss_host, g, n * sizeof(float), cudaMemcpyDeviceToHost));
+    if (u32_host) NTCB_CHECK(cudaMemcpy(u32_host, u, n * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    NTCB_CHECK(cudaDeviceSynchronize());
+    dfree(g); dfree(u);
+}
+
+void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, double* fit_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (pair_begin < 0 || pair_end > N || pair_begin > pair_end || N > I.pairs_cap || M > I.Mcap || M < 1)
+        die("shard_mlp_eval: pair range or sizes outside the buffers sized at init");
+    draw_batch(I, it, M);
+    es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit_dev);
+}
+void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (N > I.pairs_cap || N < 1) die("shard_mlp_apply: N outside the buffers sized at init");
+    (void)M;
+    NTCB_CHECK(cudaMemcpyAsync(I.fit, fit_all_dev, 2 * (size_t)N * sizeof(double), cudaMemcpyDeviceToDevice, I.stream));
+    es_apply(I, it, sigma, lr, N, I.fit, true);
+}
+
+}  // extern "C"
+
+// ====================================================================== drop-in C++ class
+namespace ntc_cuda {
+
+Trainer::Trainer() : im(new Impl) {}
+Trainer::~Trainer() {
+    if (im->ready || im->own_stream) { set_device(*im); flush_timing(*im); free_all(*im); }
+    delete im;
+}
+bool Trainer::init(const ModelDesc& d, const float* z, const float* p, const float* target, std::string& why) {
+    if (im->ready) { why = "trainer already initialised"; return false; }
+    if (!init_impl(*im, d, z, p, target, why)) return false;
+    upload_model_impl(*im, z, p);
+    return true;
+}
+std::string Trainer::banner() const { return banner_impl(*im); }
+void Trainer::upload_model(const float* z, const float* p) { upload_model_impl(*im, z, p); }
+void Trainer::download_model(float* z, float* p) { download_model_impl(*im, z, p); }
+void Trainer::set_qes(const QesDesc& q, const float* grid, size_t grid_n) { set_qes_impl(*im, q, grid, grid_n); }
+void Trainer::snap_latent() { require_ready(*im); set_device(*im); snap_latent_impl(*im); sync(*im); }
+void Trainer::shadow_pull(size_t off, size_t n, float f) { shadow_pull_impl(*im, off, n, f); }
+void Trainer::download_zq(float* zq) { download_zq_impl(*im, zq); }
+void Trainer::set_dct(const DctDesc& d, const uint8_t* code, const int16_t* sym, const int* step) { set_dct_impl(*im, d, code, sym, step); }
+void Trainer::download_dct(int16_t* sym, uint8_t* code) { download_dct_impl(*im, sym, code); }
+void Trainer::download_dct_rate(int32_t* bits, int32_t* dbl, int* ntrunc, int* nz_before, int* hits, int* evals) {
+    download_dct_rate_impl(*im, bits, dbl, ntrunc, nz_before, hits, evals);
+}
+void Trainer::mlp_step(int it, float sigma, float lr, int N, int M) { mlp_step_impl(*im, it, sigma, lr, N, M); }
+void Trainer::mlp_step_fd(int it, float h, float lr, int M) { mlp_step_fd_impl(*im, it, h, lr, M); }
+void Trainer::reset_mlp_adam() { reset_mlp_adam_impl(*im); }
+void Trainer::mlp_stats(double& batch_loss, double& diff_std) { mlp_stats_impl(*im, batch_loss, diff_std); }
+void Trainer::lat_step(int it, float sigma, float lr, int K) { lat_step_impl(*im, it, sigma, lr, K); }
+void Trainer::qat_search() { qat_search_impl(*im); }
+void Trainer::decode_full(const float* z_host, float* img) { decode_full_impl(*im, z_host, img); }
+void Trainer::debug_last_batch(std::vector<int>& bidx) const {
+    bidx.resize(im->last_M);
+    if (im->ready) copy_out(*im, im->bidx, bidx.size(), bidx.data(), bidx.size());
+}
+void Trainer::debug_last_dl(std::vector<double>& dl) const {
+    dl.resize(im->last_N);
+    if (im->ready) copy_out(*im, im->dl, dl.size(), dl.data(), dl.size());
+}
+void Trainer::debug_last_zgrad(std::vector<float>& g) const {
+    g.resize(im->nz);
+    if (im->ready) copy_out(*im, im->zgrad, g.size(), g.data(), g.size());
+}
+
+}  // namespace ntc_cuda

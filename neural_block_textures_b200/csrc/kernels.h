@@ -1,0 +1,72 @@
+// Host-side launchers of the backend's kernels. Every launcher takes the trainer's stream and the
+// by-value model description; the shape id selects a compile-time-shaped instantiation
+// (shape_id() == 0 selects the runtime-shaped fallback).
+#pragma once
+#include "device_model.cuh"
+
+namespace ntcb {
+
+// The compile-time MLP shapes (nin, hidden1, hidden2, nout) with specialised kernels. Every other
+// shape inside the envelope runs the runtime-shaped kernels.
+#define NTCB_FIXED_SHAPES(X) \
+    X(1, 5, 24, 24, 3)       \
+    X(2, 6, 24, 24, 3)       \
+    X(3, 8, 24, 24, 3)       \
+    X(4, 8, 24, 24, 12)
+
+int shape_id(const DevModel& m);
+double measure_ffma_tflops(int sms);   // FP32 FMA peak of the current device, TFLOP/s
+
+// ---- MLP population (kernels_mlp.cu) ----
+struct PopArgs {
+    int mode;                  // 0 = ES pairs (w0 +- sigma eps), 1 = FD (w0 with weight j at +- h)
+    int it;                    // iteration (noise step)
+    float sigma;               // ES sigma (0: the unperturbed weights, no noise read)
+    float fd_h;                // FD step
+    int cand_begin, ncand;     // ES: global pair index range; FD: weight index range
+    int M, mstride;            // minibatch size and the row stride of feat_t / tgt_t
+    int chunk;                 // rows per CTA along the batch (multiple of the tile rows)
+    const float* w0;           // base weights (flat reference layout)
+    const float* eps;          // ES noise [ncand][P] (row = pair - cand_begin)
+    const float* feat_t;       // [nin][mstride]
+    const float* tgt_t;        // [nout][mstride]
+    double* part;              // [ncand][2][chunks] per-CTA partial sums
+};
+int pop_chunks(int M, int chunk);
+int pop_chunk_rows(int shape);                 // rows one CTA pass covers (chunk granularity)
+void launch_batch(cudaStream_t s, const DevModel& m, uint64_t seed, int it, int M, int mstride, const float* zdec,
+                  const float* tgt, int* bidx, float* feat_t, float* tgt_t);
+void launch_noise_fill(cudaStream_t s, uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, long long n,
+                       float* gauss, uint32_t* u32);
+void launch_mlp_noise(cudaStream_t s, uint64_t seed, int it, int pair_begin, int npairs, int P, float* eps);
+void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a);
+// Sum the chunk partials of every candidate in order, normalise, and write (lp, lm) pairs to fit[2*i], fit[2*i+1].
+void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit);
+// ES: dl, lsum from the fitness of all N pairs; FD: dl, hh.
+void launch_es_reduce(cudaStream_t s, const double* fit, int N, double* dl, double* lsum);
+void launch_fd_reduce(cudaStream_t s, const double* fit, const float* w0, float h, int P, double* dl, double* hh);
+// ES gradient partials over pair segments: gpart[seg][k] = sum_{i in seg} ((float)dl[i] * scale) * eps[i][k].
+void launch_es_grad_partial(cudaStream_t s, const double* dl, const float* eps, int N, int P, float scale, int seglen, float* gpart);
+// grad[k] = sum_seg gpart[seg][k] (fixed order), then Adam on (theta, m, v).
+void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, float* grad, float* theta, float* m, float* v,
+                         float lr, float c1, float c2);
+void launch_fd_grad_adam(cudaStream_t s, const double* dl, const double* hh, int P, float* grad, float* theta, float* m, float* v,
+                         float lr, float c1, float c2);
+void launch_adam(cudaStream_t s, float* theta, const float* g, float* m, float* v, long long n, float lr, float c1, float c2);
+void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* z, float* img);
+
+// ---- latent ES and selector search (kernels_latent.cu) ----
+void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevModel& m, unsigned active_mask, long long nz, float* eps);
+void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
+                     long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix);
+struct RateTerm {              // DCT rate term of the latent gradient (level 0), null dbits = off
+    const int* dbits;          // [K][nblk * C]
+    float rate_scale;
+    int BW, C;
+};
+void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
+                       const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad);
+void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
+                const int* xr0, const int* yr0, const float* grid, const int* bits);
+
+}  // namespace ntcb

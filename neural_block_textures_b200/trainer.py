@@ -1,0 +1,185 @@
+"""Python mirror of the reference backend's ntc_cuda::Trainer (cuda/ntc_cuda.h:78-132) over the C ABI.
+
+Every method has the reference member's name and argument meaning and takes / returns host numpy
+arrays; all work runs in libntc_b200.so on the current CUDA device. As in the reference, a runtime
+failure inside the library prints a message and ends the process (the caller has no error path);
+init() returns False plus a reason for a model the backend does not support.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import abi
+
+
+def _fptr(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def _ptr(a: np.ndarray | None, ctype):
+    if a is None:
+        return None
+    assert a.flags.c_contiguous
+    return a.ctypes.data_as(C.POINTER(ctype))
+
+
+class Trainer:
+    def __init__(self) -> None:
+        self.lib = abi.load_library()
+        self.h = self.lib.ntcb_create()
+        self.nz = 0
+        self.P = 0
+        self.npix = 0
+        self.nout = 0
+        self._desc = None
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.ntcb_destroy(self.h)
+            self.h = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ---- Trainer::init (cuda/ntc_cuda.h:85)
+    def init(self, desc: abi.ModelDesc, z: np.ndarray, p: np.ndarray, target: np.ndarray) -> tuple[bool, str]:
+        why = C.create_string_buffer(512)
+        self._desc = desc
+        self.nz = int(z.size)
+        self.P = int(p.size)
+        self.npix = desc.W * desc.H
+        self.nout = desc.nout
+        assert target.size == self.npix * self.nout
+        ok = self.lib.ntcb_init(self.h, C.byref(desc), _fptr(z), _fptr(p), _fptr(target), why, 512)
+        return bool(ok), why.value.decode()
+
+    def banner(self) -> str:
+        buf = C.create_string_buffer(512)
+        self.lib.ntcb_banner(self.h, buf, 512)
+        return buf.value.decode()
+
+    def upload_model(self, z: np.ndarray, p: np.ndarray) -> None:
+        self.lib.ntcb_upload_model(self.h, _fptr(z), _fptr(p))
+
+    def download_model(self) -> tuple[np.ndarray, np.ndarray]:
+        z = np.empty(self.nz, np.float32)
+        p = np.empty(self.P, np.float32)
+        self.lib.ntcb_download_model(self.h, _fptr(z), _fptr(p))
+        return z, p
+
+    def set_qes(self, q: abi.QesDesc, grid: np.ndarray) -> None:
+        self.lib.ntcb_set_qes(self.h, C.byref(q), _fptr(grid), grid.size)
+
+    def snap_latent(self) -> None:
+        self.lib.ntcb_snap_latent(self.h)
+
+    def shadow_pull(self, off: int, n: int, f: float) -> None:
+        self.lib.ntcb_shadow_pull(self.h, off, n, f)
+
+    def download_zq(self) -> np.ndarray:
+        z = np.empty(self.nz, np.float32)
+        self.lib.ntcb_download_zq(self.h, _fptr(z))
+        return z
+
+    def set_dct(self, d: abi.DctDesc, code: np.ndarray, sym: np.ndarray, step: np.ndarray) -> None:
+        self.lib.ntcb_set_dct(self.h, C.byref(d), _ptr(code, C.c_uint8), _ptr(sym, C.c_int16), _ptr(step, C.c_int))
+
+    def download_dct(self, n_blocks_channels: int) -> tuple[np.ndarray, np.ndarray]:
+        sym = np.empty(n_blocks_channels * 64, np.int16)
+        code = np.empty(n_blocks_channels, np.uint8)
+        self.lib.ntcb_download_dct(self.h, _ptr(sym, C.c_int16), _ptr(code, C.c_uint8))
+        return sym, code
+
+    def download_dct_rate(self, n_blocks_channels: int) -> dict:
+        bits = np.empty(n_blocks_channels, np.int32)
+        dbl = np.empty(n_blocks_channels, np.int32)
+        v = [C.c_int() for _ in range(4)]
+        self.lib.ntcb_download_dct_rate(self.h, _ptr(bits, C.c_int32), _ptr(dbl, C.c_int32), *[C.byref(x) for x in v])
+        return {"bits": bits, "dbits_last_pair": dbl, "ntrunc": v[0].value, "nz_before": v[1].value,
+                "hits": v[2].value, "evals": v[3].value}
+
+    # ---- steps
+    def mlp_step(self, it: int, sigma: float, lr: float, N: int, M: int) -> None:
+        self.lib.ntcb_mlp_step(self.h, it, sigma, lr, N, M)
+
+    def mlp_step_fd(self, it: int, h: float, lr: float, M: int) -> None:
+        self.lib.ntcb_mlp_step_fd(self.h, it, h, lr, M)
+
+    def reset_mlp_adam(self) -> None:
+        self.lib.ntcb_reset_mlp_adam(self.h)
+
+    def mlp_stats(self) -> tuple[float, float]:
+        a, b = C.c_double(), C.c_double()
+        self.lib.ntcb_mlp_stats(self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    def lat_step(self, it: int, sigma: float, lr: float, K: int) -> None:
+        self.lib.ntcb_lat_step(self.h, it, sigma, lr, K)
+
+    def qat_search(self) -> None:
+        self.lib.ntcb_qat_search(self.h)
+
+    def decode_full(self, z_host: np.ndarray | None = None) -> np.ndarray:
+        img = np.empty(self.npix * self.nout, np.float32)
+        self.lib.ntcb_decode_full(self.h, _fptr(z_host), _fptr(img))
+        return img
+
+    # ---- verification helpers
+    def debug_last_batch(self) -> np.ndarray:
+        n = self.lib.ntcb_debug_last_batch(self.h, None, 0)
+        out = np.empty(n, np.int32)
+        self.lib.ntcb_debug_last_batch(self.h, _ptr(out, C.c_int), n)
+        return out
+
+    def debug_last_dl(self) -> np.ndarray:
+        n = self.lib.ntcb_debug_last_dl(self.h, None, 0)
+        out = np.empty(n, np.float64)
+        self.lib.ntcb_debug_last_dl(self.h, _ptr(out, C.c_double), n)
+        return out
+
+    def debug_last_zgrad(self) -> np.ndarray:
+        out = np.empty(self.nz, np.float32)
+        self.lib.ntcb_debug_last_zgrad(self.h, _fptr(out), self.nz)
+        return out
+
+    def debug_last_fitness(self) -> tuple[np.ndarray, np.ndarray]:
+        n = self.lib.ntcb_debug_last_fitness(self.h, None, None, 0)
+        lp = np.empty(n, np.float64)
+        lm = np.empty(n, np.float64)
+        self.lib.ntcb_debug_last_fitness(self.h, _ptr(lp, C.c_double), _ptr(lm, C.c_double), n)
+        return lp, lm
+
+    # ---- additions
+    def set_stream(self, stream_handle: int | None) -> None:
+        self.lib.ntcb_set_stream(self.h, C.c_void_p(stream_handle) if stream_handle else None)
+
+    def kernel_timing(self, enable: bool) -> None:
+        self.lib.ntcb_kernel_timing(self.h, 1 if enable else 0)
+
+    def kernel_time(self, kernel: str) -> tuple[float, int]:
+        ms, n = C.c_double(), C.c_int()
+        self.lib.ntcb_kernel_time(self.h, kernel.encode(), C.byref(ms), C.byref(n))
+        return ms.value, n.value
+
+    def launch_count(self) -> int:
+        return int(self.lib.ntcb_launch_count(self.h))
+
+    def shard_mlp_eval(self, it: int, sigma: float, N: int, M: int, p0: int, p1: int, fit_dev_ptr: int) -> None:
+        self.lib.ntcb_shard_mlp_eval(self.h, it, sigma, N, M, p0, p1, C.c_void_p(fit_dev_ptr))
+
+    def shard_mlp_apply(self, it: int, sigma: float, lr: float, N: int, M: int, fit_all_dev_ptr: int) -> None:
+        self.lib.ntcb_shard_mlp_apply(self.h, it, sigma, lr, N, M, C.c_void_p(fit_all_dev_ptr))
