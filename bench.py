@@ -198,24 +198,18 @@ def main():
     stream = torch.cuda.Stream()
     tr.set_stream(stream.cuda_stream)
     N, M, K = cfg.pairs, cfg.batch, cfg.lat_pairs
-    if N % world:
-        raise SystemExit(f"{N} pairs do not split evenly over {world} ranks")
-    per = N // world
-    p_begin, p_end = min(N, rank * per), min(N, (rank + 1) * per)
-    fit_local = torch.zeros(2 * per, dtype=torch.float64, device="cuda")
-    fit_all = torch.zeros(2 * per * world, dtype=torch.float64, device="cuda")
+    from neural_block_textures_b200.shard import ShardedES, pair_range
+    per = pair_range(N, world, rank)[1] - pair_range(N, world, rank)[0]
+    sharded = ShardedES(tr, dist, N, device="cuda", stream=stream) if world > 1 else None
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     dec = cfg.decodes_per_iter()
     decodes = sum(dec.values())
 
     def step(it):
-        if world == 1:
+        if sharded is None:
             tr.mlp_step(it, cfg.mlp_sigma, cfg.mlp_lr, N, M)
         else:
-            tr.shard_mlp_eval(it, cfg.mlp_sigma, N, M, p_begin, p_end, fit_local.data_ptr())
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(fit_all, fit_local)
-            tr.shard_mlp_apply(it, cfg.mlp_sigma, cfg.mlp_lr, N, M, fit_all.data_ptr())
+            sharded.step(it, cfg.mlp_sigma, cfg.mlp_lr, M)
         tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
         tr.qat_search()
 

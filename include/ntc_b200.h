@@ -140,6 +140,10 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
  * u32_host[i] for index index0 + i of (seed, stream, step, pair); either pointer may be NULL. For tests. */
 void ntcb_noise_fill(uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, size_t n,
                      float* gauss_host, uint32_t* u32_host);
+/* Host-only: the per-texel pixel range [lo[t], hi[t]) along one axis of a level with ntex texels over npx
+ * pixels, with the nearest-cell rule or the bilinear distinct-texel rule the latent gradient gathers with.
+ * Returns 1 when every texel's pixels form one contiguous range (the gather's precondition), else 0. */
+int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi);
 /* Measured FP32 FMA throughput of the current device in TFLOP/s (the roofline of the population kernels). */
 double ntcb_fp32_peak_tflops(void);
 /* Number of kernels this trainer has launched since creation. */

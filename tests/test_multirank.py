@@ -1,0 +1,85 @@
+"""The N > 1 host logic on CPU: two gloo ranks shard the ES population with ShardedES (the code bench.py
+runs over NCCL on GPUs), all-gather the per-pair fitness and apply identical updates. The per-rank
+evaluator here is the oracle (test infrastructure standing in for the GPU kernels); the test checks the
+pair split, the gather order and that every rank ends with the single-process weights, bit for bit."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from neural_block_textures_b200.shard import ShardedES, pair_range
+
+from .helpers import spec_named, target_for
+
+N, M, SIGMA, LR, STEPS = 8, 128, 0.02, 0.005, 2
+
+
+class OracleEvaluator:
+    """shard_mlp_eval / shard_mlp_apply with the libntc_b200 contract, computed by the oracle on CPU."""
+
+    def __init__(self, name):
+        from oracle.oracle import Oracle
+        self.spec = spec_named(name)
+        self.z, self.p = self.spec.init_params()
+        self.orc = Oracle(self.spec, target_for(self.spec))
+        self.m = np.zeros_like(self.p); self.v = np.zeros_like(self.p); self.t = 0
+
+    def shard_mlp_eval(self, it, sigma, N_, M_, p0, p1, fit):
+        idx = self.orc.draw_batch(self.spec.seed, it, M_)
+        lp, lm = self.orc.es_fitness(self.p, self.z, self.spec.seed, it, sigma, p0, p1 - p0, idx)
+        fit[0::2] = torch.from_numpy(lp); fit[1::2] = torch.from_numpy(lm)
+
+    def shard_mlp_apply(self, it, sigma, lr, N_, M_, fit_all):
+        f = fit_all.numpy()
+        g = self.orc.es_grad(self.spec.seed, it, sigma, f[0::2] - f[1::2])
+        self.t += 1
+        self.p, self.m, self.v = self.orc.adam(self.p, g, self.m, self.v, lr, self.t)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ev = OracleEvaluator("cfg2")
+        es = ShardedES(ev, dist, N, device="cpu")
+        for it in range(1, STEPS + 1):
+            es.step(it, SIGMA, LR, M)
+        np.save(os.path.join(out_dir, f"p{rank}.npy"), ev.p)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_pair_range():
+    assert [pair_range(16, 4, r) for r in range(4)] == [(0, 4), (4, 8), (8, 12), (12, 16)]
+    with pytest.raises(ValueError):
+        pair_range(10, 4, 0)
+
+
+def test_two_gloo_ranks_match_single_process(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    p0, p1 = np.load(tmp_path / "p0.npy"), np.load(tmp_path / "p1.npy")
+    assert np.array_equal(p0, p1), "replicas stay bit-identical"
+    ev = OracleEvaluator("cfg2")
+    for it in range(1, STEPS + 1):
+        fit = torch.zeros(2 * N, dtype=torch.float64)
+        ev.shard_mlp_eval(it, SIGMA, N, M, 0, N, fit)
+        ev.shard_mlp_apply(it, SIGMA, LR, N, M, fit)
+    assert np.array_equal(p0, ev.p), "sharded == single process"
+    assert not np.array_equal(p0, spec_named("cfg2").init_params()[1])
