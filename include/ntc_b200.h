@@ -140,6 +140,21 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
  * u32_host[i] for index index0 + i of (seed, stream, step, pair); either pointer may be NULL. For tests. */
 void ntcb_noise_fill(uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, size_t n,
                      float* gauss_host, uint32_t* u32_host);
+/* No counterpart in the reference. The per-pair ES fitness of mlp_step (L(w + sigma eps_i), L(w - sigma eps_i)
+ * for pairs pair_begin .. pair_begin + npairs - 1 of iteration `it`, hash noise keyed by d->seed, normalised
+ * like loss_subset) for callers that cannot allocate device memory where they run — a host engine whose device
+ * memory is fixed after start-up, or a plugin that may only use memory it is handed; cudaMalloc can also block
+ * and synchronise the device. It allocates nothing: its scratch is one file-scope device array of
+ * NTCB_STATIC_SCRATCH_BYTES per GPU, held until exit. Inputs are host arrays: w (the flat MLP), feat (M rows of
+ * d->nin features, the minibatch pixels' MLP inputs), tgt (M rows of d->nout targets); fit receives 2 * npairs
+ * doubles (L+, L- per pair). Returns 1, or 0 with a reason in why when the sizes need more than the static
+ * maximum or the model is outside the envelope. The first call on a device looks up the array's device address
+ * (make it before any stream capture). Calls in one process share the array: concurrent calls race and must be
+ * serialised by the caller. Synchronous on the legacy default stream. */
+#define NTCB_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+int ntcb_es_fitness_noalloc(const ntcb_model_desc* d, int it, float sigma, int pair_begin, int npairs,
+                            const float* w, const float* feat, const float* tgt, int M, double* fit,
+                            char* why, size_t why_cap);
 /* Host-only: the per-texel pixel range [lo[t], hi[t]) along one axis of a level with ntex texels over npx
  * pixels, with the nearest-cell rule or the bilinear distinct-texel rule the latent gradient gathers with.
  * Returns 1 when every texel's pixels form one contiguous range (the gather's precondition), else 0. */

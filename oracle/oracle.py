@@ -101,7 +101,7 @@ class Oracle:
 
     def features(self, z, px, py):
         f = np.zeros(128, np.float32)
-        self.lib.or_features(self.mp, f32p(z), px, py, f.ctypes.data_as(_fp))
+        self.lib.or_features(self.mp, f32p(z), C.c_int(int(px)), C.c_int(int(py)), f.ctypes.data_as(_fp))
         return f[: self.spec.nin].copy()
 
     def decode_full(self, p, z):
