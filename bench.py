@@ -9,8 +9,9 @@ level 0 = 512x512x1 2-bit --qat selector plane, level 1 = 128x128x2 bilinear, 24
 
 --impl ours (default): the CUDA backend. N > 1 (torchrun, one process per GPU): the ES population is sharded
 over the ranks (each evaluates its pairs, regenerating their noise from the counter); one NCCL all-gather of
-the per-pair fitness (2 doubles per pair) feeds the identical gradient + Adam on every rank; the latent step
-and the selector search run as replicas.
+the per-pair fitness (2 doubles per pair) feeds the identical gradient + Adam on every rank; the latent step is
+sharded by image rows (all-gather of the per-pixel loss differences) and the selector search by level-0 texel
+rows (all-gather of level 0), with identical gathers / Adam / snap on every rank (neural_block_textures_b200/shard.py).
 --impl reference: the reference's own CPU trainer (main.cpp compiled from source, OpenMP on every host
 thread) timed on a bounded sample of the same iteration (rank 0 only).
 """
@@ -43,6 +44,7 @@ def parse():
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true", help="skip timing the reference's own CUDA backend (oracle/_ref/ntc_ref)")
     return ap.parse_args()
 
 
@@ -172,6 +174,50 @@ def cpu_baseline_leg(cfg, budget_s=12.0):
                       f"and selector search): {dec / 1e6:.2f} M decodes each, {t_all:.1f} s"}
 
 
+def ref_cuda_leg(cfg, n1=20, n2=120):
+    """The reference's own CUDA backend (cuda/ntc_cuda.cu built unmodified for sm_100a, linked into the reference
+    CLI as oracle/_ref/ntc_ref) on the same configuration and GPU. Two runs of n1 and n2 ES iterations with no
+    intermediate prints: the CLI reports the elapsed time at the last iteration before its final print, so
+    (t(n2) - t(n1)) / (n2 - n1) is the per-iteration time without initialisation or printing."""
+    import re
+    import tempfile
+    from neural_block_textures_b200 import synth
+    exe = ROOT / "oracle" / "_ref" / "ntc_ref"
+    if not exe.exists():
+        return None
+    with tempfile.TemporaryDirectory() as d:
+        imgs = cfg.images()
+        paths = []
+        for t, im in enumerate(imgs):
+            p = Path(d) / f"in{t}.png"
+            synth.write_png(p, im)
+            paths.append(str(p))
+        flags = [f for f in cfg.cli.replace("--write-ntcb", "").split()]
+        # ES phase only (the bench step): drop --mlp-fd and its value, and the iteration count
+        out = []
+        skip = 0
+        for f in flags:
+            if skip:
+                skip -= 1; continue
+            if f in ("--mlp-fd", "--iters"):
+                skip = 1; continue
+            out.append(f)
+        ts = {}
+        for n in (n1, n2):
+            r = subprocess.run([str(exe), *paths, *out, "--iters", str(n), "--print-every", "100000000", "--rng", "hash", "--cuda",
+                                "--out", str(Path(d) / f"o{n}")], capture_output=True, text=True, timeout=900)
+            if r.returncode != 0:
+                return {"unavailable": f"ntc_ref exited {r.returncode}: {(r.stdout + r.stderr)[-300:]}"}
+            m = re.findall(rf"iter\s+{n}\s.*\|\s+([0-9.]+)s \(", r.stdout)
+            if not m:
+                return {"unavailable": "could not parse the reference CLI's timing line"}
+            ts[n] = float(m[-1])
+    ms = 1e3 * (ts[n2] - ts[n1]) / (n2 - n1)
+    dec = sum(cfg.decodes_per_iter().values())
+    return {"value": dec / (ms * 1e-3), "unit": "decodes/s", "ms_per_step": ms, "kind": "reference CUDA backend (ntc_ref, sm_100a)",
+            "method": f"wall clock of the reference CLI, ({n2} - {n1}) ES iterations, same synthetic input"}
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
@@ -200,7 +246,12 @@ def main():
     N, M, K = cfg.pairs, cfg.batch, cfg.lat_pairs
     from neural_block_textures_b200.shard import ShardedES, pair_range
     per = pair_range(N, world, rank)[1] - pair_range(N, world, rank)[0]
-    sharded = ShardedES(tr, dist, N, device="cuda", stream=stream) if world > 1 else None
+    L0 = spec.levels[0]
+    has_lat = len(spec.levels) > 1 or not spec.qat_bits
+    sharded = None
+    if world > 1:
+        sharded = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K if has_lat else 0, image=(spec.W, spec.H),
+                            level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     dec = cfg.decodes_per_iter()
     decodes = sum(dec.values())
@@ -208,10 +259,16 @@ def main():
     def step(it):
         if sharded is None:
             tr.mlp_step(it, cfg.mlp_sigma, cfg.mlp_lr, N, M)
+            if has_lat:
+                tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
+            if spec.qat_bits:
+                tr.qat_search()
         else:
             sharded.step(it, cfg.mlp_sigma, cfg.mlp_lr, M)
-        tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
-        tr.qat_search()
+            if has_lat:
+                sharded.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
+            if spec.qat_bits:
+                sharded.qat_search()
 
     it = 1
     for _ in range(args.warmup):
@@ -308,6 +365,9 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_leg(cfg)
+        if world == 1 and not args.no_ref_cuda:
+            tr.close()
+            line["ref_cuda_backend"] = ref_cuda_leg(cfg)
         print(json.dumps(line))
     tr.close()
     if dist:

@@ -172,6 +172,17 @@ long long ntcb_launch_count(const ntcb_trainer* t);
  * step; every rank computes the identical update, so the replicas stay bit-identical. */
 void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, double* fit_dev);
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev);
+/* The latent ES step sharded by pixel rows: a rank writes the per-pixel loss differences of image rows
+ * [row_begin, row_end) for all K pairs into dpix_dev, a DEVICE buffer laid out [K][W * H] (each pair's plane is
+ * row-major, so a rank's rows are one contiguous range per plane); after the caller all-gathers every plane,
+ * ntcb_shard_lat_apply runs the footprint gathers, Adam and the snap identically on every rank. */
+void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* dpix_dev);
+void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* dpix_all_dev);
+/* The selector search sharded by level-0 texel rows: a rank searches rows [trow_begin, trow_end) and copies
+ * their level-0 values into level0_dev (a DEVICE buffer of the level's W * H * C floats, rows contiguous);
+ * after the caller's all-gather, ntcb_shard_qat_apply installs the full level 0 on every rank. */
+void ntcb_shard_qat(ntcb_trainer* t, int trow_begin, int trow_end, float* level0_dev);
+void ntcb_shard_qat_apply(ntcb_trainer* t, const float* level0_all_dev);
 
 #ifdef __cplusplus
 }

@@ -118,6 +118,10 @@ SIGNATURES = {
     "ntcb_noise_fill": (None, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_size_t, _fp, C.POINTER(C.c_uint32)]),
     "ntcb_shard_mlp_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "ntcb_shard_mlp_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_lat_eval": (None, [_vp, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_lat_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, _vp]),
+    "ntcb_shard_qat": (None, [_vp, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_qat_apply": (None, [_vp, _vp]),
 }
 
 _lib = None

@@ -534,27 +534,37 @@ void mlp_stats_impl(Impl& I, double& batch_loss, double& diff_std) {
     }
 }
 
-void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
-    (void)it;
-    require_ready(I); set_device(I);
-    if (K < 1) die("lat_step needs K >= 1 pairs");
+unsigned lat_mask(const Impl& I) {
     const bool qat = I.d.qat > 0;
     unsigned mask = 0;
     for (int l = 0; l < I.d.nlev; l++) if (!(qat && l == 0)) mask |= 1u << l;
+    return mask;
+}
+
+// The first half of a latent ES step: the noise of every ES-trained texel for the K pairs of this step, and
+// the per-pixel loss differences of pixels [p_begin, p_end) written into dpix ([K][W H]).
+void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_end, float* dpix) {
+    const unsigned mask = lat_mask(I);
+    if (!mask) return;
+    ensure_lat(I, K);
+    int nact = 0;
+    for (int l = 0; l < I.d.nlev; l++) if (mask & (1u << l)) nact++;
+    const int step = I.lat_step_no;
+    timed(I, "lat_noise", nact, [&] { ntcb::launch_lat_noise(I.stream, I.d.seed, step, K, I.dm, mask, I.nz, I.lat_eps); });
+    const float inv_px = 1.0f / (3.0f * I.d.wsum * (float)I.d.W * (float)I.d.H);
+    timed(I, "lat_eval", 1, [&] {
+        ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, dpix, p_begin, p_end);
+    });
+}
+
+// The second half: the DCT rate pass, the footprint gathers of every pixel's dpix, Adam, the snap.
+void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix) {
+    const unsigned mask = lat_mask(I);
     NTCB_CHECK(cudaMemsetAsync(I.zgrad, 0, I.nz * sizeof(float), I.stream));
     const bool rate = I.dct_live && I.rate_es;
     if (rate) NTCB_CHECK(cudaMemsetAsync(I.dcnt + 2, 0, sizeof(int), I.stream));
     I.dct_evals = rate ? (int)(I.dct_n * K) : 0;
-    const int step = I.lat_step_no;
     if (mask) {
-        ensure_lat(I, K);
-        int nact = 0;
-        for (int l = 0; l < I.d.nlev; l++) if (mask & (1u << l)) nact++;
-        timed(I, "lat_noise", nact, [&] { ntcb::launch_lat_noise(I.stream, I.d.seed, step, K, I.dm, mask, I.nz, I.lat_eps); });
-        const float inv_px = 1.0f / (3.0f * I.d.wsum * (float)I.d.W * (float)I.d.H);
-        timed(I, "lat_eval", 1, [&] {
-            ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, I.dpix);
-        });
         ntcb::RateTerm rt{nullptr, 0.0f, 0, 0};
         if (rate) {
             timed(I, "dct_rate", 1, [&] {
@@ -568,7 +578,7 @@ void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
             if (!(mask & (1u << l))) continue;
             const ntcb::RateTerm r = (l == 0) ? rt : ntcb::RateTerm{nullptr, 0.0f, 0, 0};
             timed(I, "lat_gather", 1, [&] {
-                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], I.dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad);
+                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad);
             });
         }
     }
@@ -581,14 +591,33 @@ void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
     I.lat_step_no++;
 }
 
-void qat_search_impl(Impl& I) {
+void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
+    (void)it;
     require_ready(I); set_device(I);
+    if (K < 1) die("lat_step needs K >= 1 pairs");
+    if (lat_mask(I)) {
+        ensure_lat(I, K);
+        lat_eval_part(I, sigma, K, 0, I.npix, I.dpix);
+    }
+    lat_apply_part(I, sigma, lr, K, I.dpix);
+}
+
+// Level-0 texels [t_begin, t_end) (row-major over the level) searched in place on the decode buffer.
+void qat_rows_part(Impl& I, long long t_begin, long long t_end) {
     if (I.d.qat <= 0) die("qat_search without --qat in the model description");
     timed(I, "qat", 1, [&] {
-        ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits);
+        ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits, t_begin, t_end);
     });
+}
+void qat_copy_back(Impl& I) {
     if (I.zdec != I.z)
         NTCB_CHECK(cudaMemcpyAsync(I.z + I.dm.lv[0].off, I.zdec + I.dm.lv[0].off, I.n0 * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+}
+
+void qat_search_impl(Impl& I) {
+    require_ready(I); set_device(I);
+    qat_rows_part(I, 0, (long long)I.d.lv[0].W * I.d.lv[0].H);
+    qat_copy_back(I);
 }
 
 void decode_full_impl(Impl& I, const float* z_host, float* img) {
@@ -823,6 +852,36 @@ void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int
         die("shard_mlp_eval: pair range or sizes outside the buffers sized at init");
     draw_batch(I, it, M);
     es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit_dev);
+}
+void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* dpix_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (K < 1 || row_begin < 0 || row_end > I.d.H || row_begin > row_end) die("shard_lat_eval: bad pair count or row range");
+    lat_eval_part(I, sigma, K, (long long)row_begin * I.d.W, (long long)row_end * I.d.W, dpix_dev);
+}
+void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* dpix_all_dev) {
+    (void)it;
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (K < 1) die("shard_lat_apply needs K >= 1 pairs");
+    if (lat_mask(I)) ensure_lat(I, K);
+    lat_apply_part(I, sigma, lr, K, dpix_all_dev);
+}
+void ntcb_shard_qat(ntcb_trainer* t, int trow_begin, int trow_end, float* level0_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    const int LW = I.d.lv[0].W, LH = I.d.lv[0].H, LC = I.d.lv[0].C;
+    if (trow_begin < 0 || trow_end > LH || trow_begin > trow_end) die("shard_qat: bad texel row range");
+    qat_rows_part(I, (long long)trow_begin * LW, (long long)trow_end * LW);
+    const long long off = (long long)trow_begin * LW * LC, n = (long long)(trow_end - trow_begin) * LW * LC;
+    if (n > 0)
+        NTCB_CHECK(cudaMemcpyAsync(level0_dev + off, I.zdec + I.dm.lv[0].off + off, n * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+}
+void ntcb_shard_qat_apply(ntcb_trainer* t, const float* level0_all_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    NTCB_CHECK(cudaMemcpyAsync(I.zdec + I.dm.lv[0].off, level0_all_dev, I.n0 * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+    qat_copy_back(I);
 }
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev) {
     Impl& I = t->impl;

@@ -58,7 +58,8 @@ void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w,
 // ---- latent ES and selector search (kernels_latent.cu) ----
 void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevModel& m, unsigned active_mask, long long nz, float* eps);
 void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
-                     long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix);
+                     long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
+                     long long p_begin, long long p_end);   // pixels [p_begin, p_end) of every pair
 struct RateTerm {              // DCT rate term of the latent gradient (level 0), null dbits = off
     const int* dbits;          // [K][nblk * C]
     float rate_scale;
@@ -67,6 +68,6 @@ struct RateTerm {              // DCT rate term of the latent gradient (level 0)
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad);
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
-                const int* xr0, const int* yr0, const float* grid, const int* bits);
+                const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end);
 
 }  // namespace ntcb

@@ -68,66 +68,105 @@ __device__ __forceinline__ void perturbed_features(const DevModel& m, const floa
     pos_encode(m, u, v, t1, f + slot);
 }
 
+// The + and - features of one pixel for pair k in one pass (taps, latent and noise loads shared).
+__device__ __forceinline__ void perturbed_features_pm(const DevModel& m, const float* __restrict__ z, const float* __restrict__ ek,
+                                                      unsigned active, float sg, int px, int py, float* fp, float* fm) {
+    const float u = pix_u(m, px), v = pix_v(m, py);
+    Tap t1 = {0, 0, 0, 0, 0.0f, 0.0f};
+    int slot = 0;
+    for (int l = 0; l < m.nlev; l++) {
+        const DevLevel& L = m.lv[l];
+        const Tap t = level_tap(L, u, v);
+        if (l == 1) t1 = t;
+        const float* zl = z + L.off;
+        if (!(active & (1u << l))) {
+            sample_level(L, zl, t, fp + slot);
+            for (int c = 0; c < L.C; c++) fm[slot + c] = fp[slot + c];
+        } else {
+            const float* el = ek + L.off;
+            const long long ia = ((long long)t.y0 * L.W + t.x0) * L.C;
+            if (L.nearest) {
+                for (int c = 0; c < L.C; c++) {
+                    const float e = el[ia + c], zz = zl[ia + c];
+                    fp[slot + c] = fmaf(sg, e, zz); fm[slot + c] = fmaf(-sg, e, zz);
+                }
+            } else {
+                const long long ib = ((long long)t.y0 * L.W + t.x1) * L.C;
+                const long long ic = ((long long)t.y1 * L.W + t.x0) * L.C;
+                const long long id = ((long long)t.y1 * L.W + t.x1) * L.C;
+                const TapW w = tap_weights(t);
+                for (int c = 0; c < L.C; c++) {
+                    const float ea = el[ia + c], eb = el[ib + c], ec = el[ic + c], ed = el[id + c];
+                    const float za = zl[ia + c], zb = zl[ib + c], zc = zl[ic + c], zd = zl[id + c];
+                    fp[slot + c] = blend4(w, fmaf(sg, ea, za), fmaf(sg, eb, zb), fmaf(sg, ec, zc), fmaf(sg, ed, zd));
+                    fm[slot + c] = blend4(w, fmaf(-sg, ea, za), fmaf(-sg, eb, zb), fmaf(-sg, ec, zc), fmaf(-sg, ed, zd));
+                }
+            }
+        }
+        slot += L.C;
+    }
+    pos_encode(m, u, v, t1, fp + slot);
+    for (int q = slot; q < m.nin; q++) fm[q] = fp[q];
+}
+
 // One thread per (pixel, group of kLatPairs pairs): the 2 x kLatPairs perturbed decodes of the pixel run
-// as one register tile; dpix[k][p] = (e+ - e-) * inv_px with the float per-pixel error of decode_err
-// (main.cpp:1722-1735, 2015). The reference launches one kernel per pair and regenerates the noise of
-// every tap (cuda/ntc_cuda.cu:358-409, 1124-1144).
+// as one register tile on the packed FP32 pipe, each latent pair's (+, -) decodes forming one row pair;
+// dpix[k][p] = (e+ - e-) * inv_px with the float per-pixel error of decode_err (main.cpp:1722-1735, 2015).
+// The reference launches one kernel per pair and regenerates the noise of every tap
+// (cuda/ntc_cuda.cu:358-409, 1124-1144).
 template <class S, int TPB>
 __global__ void __launch_bounds__(TPB) k_lat_eval_fixed(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                         const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
-                                                        int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix) {
-    constexpr int R = 2 * kLatPairs;
+                                                        int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
+                                                        long long p_begin, long long p_end) {
+    constexpr int R2 = kLatPairs;
     extern __shared__ __align__(16) float ws[];
-    for (int k = threadIdx.x; k < S::SIZE; k += TPB) ws[k] = 0.0f;
-    __syncthreads();
-    for (int k = threadIdx.x; k < m.P; k += TPB) ws[S::slot(k)] = wg[k];
-    __syncthreads();
+    load_weights_x2<S>(wg, m.P, ws);
     const long long npix = (long long)m.W * m.H;
-    const long long p = (long long)blockIdx.x * TPB + threadIdx.x;
-    const long long pc = p < npix ? p : npix - 1;
+    const long long p = p_begin + (long long)blockIdx.x * TPB + threadIdx.x;
+    const long long pc = p < p_end ? p : p_end - 1;
     const int px = (int)(pc % m.W), py = (int)(pc / m.W);
     const int k0 = blockIdx.y * kLatPairs;
-    float x[R][S::NIN];
+    float2 x[R2][S::NIN];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        const int k = min(k0 + r / 2, K - 1);
-        float f[kMaxIn];
-        perturbed_features(m, z, eps + (long long)k * nz, active, (r & 1) ? -sg : sg, px, py, f);
+    for (int q = 0; q < R2; q++) {
+        const int k = min(k0 + q, K - 1);
+        float fp[kMaxIn], fm[kMaxIn];
+        perturbed_features_pm(m, z, eps + (long long)k * nz, active, sg, px, py, fp, fm);
 #pragma unroll
-        for (int i = 0; i < S::NIN; i++) x[r][i] = f[i];
+        for (int i = 0; i < S::NIN; i++) x[q][i] = make_float2(fp[i], fm[i]);
     }
-    float o[R][S::NOUT];
-    fixed_forward<S, R>(ws, x, o, m.leak, m.clamp_out);
-    if (p >= npix) return;
+    float2 o[R2][S::NOUT];
+    fixed_forward_x2<S, R2>(ws, x, o, m.leak, m.clamp_out);
+    if (p >= p_end) return;
     const float* t = tgt + pc * S::NOUT;
     float tv[S::NOUT];
 #pragma unroll
     for (int c = 0; c < S::NOUT; c++) tv[c] = t[c];
 #pragma unroll
-    for (int j = 0; j < kLatPairs; j++) {
-        const int k = k0 + j;
-        float e[2];
+    for (int q = 0; q < R2; q++) {
+        const int k = k0 + q;
+        float ep = 0.0f, em = 0.0f;
 #pragma unroll
-        for (int sgn = 0; sgn < 2; sgn++) {
-            float acc = 0.0f;
-#pragma unroll
-            for (int c = 0; c < S::NOUT; c++) { const float d = o[2 * j + sgn][c] - tv[c]; acc += m.cw[c] * (d * d); }
-            e[sgn] = acc;
+        for (int c = 0; c < S::NOUT; c++) {
+            const float dp = o[q][c].x - tv[c], dm = o[q][c].y - tv[c];
+            ep += m.cw[c] * (dp * dp);
+            em += m.cw[c] * (dm * dm);
         }
-        if (k < K) dpix[(long long)k * npix + p] = (e[0] - e[1]) * inv_px;
+        if (k < K) dpix[(long long)k * npix + p] = (ep - em) * inv_px;
     }
 }
 
 __global__ void k_lat_eval_generic(DevModel m, const float* __restrict__ wg, const float* __restrict__ z, const float* __restrict__ eps,
                                    long long nz, const float* __restrict__ tgt, int K, unsigned active, float sg, float inv_px,
-                                   float* __restrict__ dpix) {
+                                   float* __restrict__ dpix, long long p_begin, long long p_end) {
     extern __shared__ __align__(16) float ws[];
     for (int k = threadIdx.x; k < m.P; k += blockDim.x) ws[k] = wg[k];
     __syncthreads();
     const long long npix = (long long)m.W * m.H;
-    const long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long p = p_begin + (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int k = blockIdx.y;
-    if (p >= npix) return;
+    if (p >= p_end) return;
     const int px = (int)(p % m.W), py = (int)(p / m.W);
     float f[kMaxIn], o[kMaxOut];
     const float* t = tgt + p * m.nout;
@@ -141,17 +180,20 @@ __global__ void k_lat_eval_generic(DevModel m, const float* __restrict__ wg, con
 }
 
 void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
-                     long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix) {
-    const long long npix = (long long)m.W * m.H;
+                     long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
+                     long long p_begin, long long p_end) {
+    const long long n = p_end - p_begin;
+    if (n <= 0) return;
     switch (shape) {
 #define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: { using S = FixedShape<NIN, H1, H2, NOUT>; \
-        dim3 grid(blocks_for(npix, kLatTPB), (unsigned)((K + kLatPairs - 1) / kLatPairs)); \
-        k_lat_eval_fixed<S, kLatTPB><<<grid, kLatTPB, S::SIZE * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix); break; }
+        dim3 grid(blocks_for(n, kLatTPB), (unsigned)((K + kLatPairs - 1) / kLatPairs)); \
+        k_lat_eval_fixed<S, kLatTPB><<<grid, kLatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, \
+                                                                                     p_begin, p_end); break; }
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: {
-            dim3 grid(blocks_for(npix, 128), (unsigned)K);
-            k_lat_eval_generic<<<grid, 128, m.P * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix);
+            dim3 grid(blocks_for(n, 128), (unsigned)K);
+            k_lat_eval_generic<<<grid, 128, m.P * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, p_begin, p_end);
         }
     }
     NTCB_CHECK(cudaGetLastError());
@@ -212,16 +254,13 @@ template <class S, int TPB>
 __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __restrict__ wg, float* __restrict__ z,
                                                    const float* __restrict__ tgt, const int* __restrict__ xr,
                                                    const int* __restrict__ yr, const float* __restrict__ grid,
-                                                   const int* __restrict__ bits_c) {
-    constexpr int R = kQatRows;
+                                                   const int* __restrict__ bits_c, long long t_begin, long long t_end) {
+    constexpr int R = kQatRows, R2 = kQatRows / 2;
     extern __shared__ __align__(16) float ws[];
-    for (int k = threadIdx.x; k < S::SIZE; k += TPB) ws[k] = 0.0f;
-    __syncthreads();
-    for (int k = threadIdx.x; k < m.P; k += TPB) ws[S::slot(k)] = wg[k];
-    __syncthreads();
+    load_weights_x2<S>(wg, m.P, ws);
     const DevLevel& L = m.lv[0];
-    const long long t = (long long)blockIdx.x * TPB + threadIdx.x;
-    if (t >= (long long)L.W * L.H) return;   // no barrier below
+    const long long t = t_begin + (long long)blockIdx.x * TPB + threadIdx.x;
+    if (t >= t_end) return;   // no barrier below
     const int tx = (int)(t % L.W), ty = (int)(t / L.W);
     const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
     if (x0 >= x1 || y0 >= y1) return;
@@ -238,20 +277,24 @@ __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __re
                 for (int px = x0; px < x1; px++) {
                     float f[kMaxIn];
                     pixel_features(m, z, px, py, f);
-                    float x[R][S::NIN];
+                    float2 x[R2][S::NIN];
 #pragma unroll
-                    for (int r = 0; r < R; r++) {
-                        const float val = gv[min(kg + r, n - 1)];
+                    for (int h = 0; h < R2; h++) {
+                        const float va = gv[min(kg + 2 * h, n - 1)], vb = gv[min(kg + 2 * h + 1, n - 1)];
 #pragma unroll
-                        for (int i = 0; i < S::NIN; i++) x[r][i] = (i == c) ? val : f[i];
+                        for (int i = 0; i < S::NIN; i++) x[h][i] = (i == c) ? make_float2(va, vb) : make_float2(f[i], f[i]);
                     }
-                    float o[R][S::NOUT];
-                    fixed_forward<S, R>(ws, x, o, m.leak, m.clamp_out);
+                    float2 o[R2][S::NOUT];
+                    fixed_forward_x2<S, R2>(ws, x, o, m.leak, m.clamp_out);
                     const float* tp = tgt + ((long long)py * m.W + px) * S::NOUT;
 #pragma unroll
-                    for (int r = 0; r < R; r++)
+                    for (int h = 0; h < R2; h++)
 #pragma unroll
-                        for (int q = 0; q < S::NOUT; q++) { const float d = o[r][q] - tp[q]; acc[r] += (double)(m.cw[q] * (d * d)); }
+                        for (int q = 0; q < S::NOUT; q++) {
+                            const float da = o[h][q].x - tp[q], db = o[h][q].y - tp[q];
+                            acc[2 * h] += (double)(m.cw[q] * (da * da));
+                            acc[2 * h + 1] += (double)(m.cw[q] * (db * db));
+                        }
                 }
 #pragma unroll
             for (int r = 0; r < R; r++) if (kg + r < n) loss[kg + r] = acc[r];
@@ -268,13 +311,13 @@ __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __re
 
 __global__ void k_qat_generic(DevModel m, const float* __restrict__ wg, float* __restrict__ z, const float* __restrict__ tgt,
                               const int* __restrict__ xr, const int* __restrict__ yr, const float* __restrict__ grid,
-                              const int* __restrict__ bits_c) {
+                              const int* __restrict__ bits_c, long long t_begin, long long t_end) {
     extern __shared__ __align__(16) float ws[];
     for (int k = threadIdx.x; k < m.P; k += blockDim.x) ws[k] = wg[k];
     __syncthreads();
     const DevLevel& L = m.lv[0];
-    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= (long long)L.W * L.H) return;
+    const long long t = t_begin + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= t_end) return;
     const int tx = (int)(t % L.W), ty = (int)(t / L.W);
     const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
     if (x0 >= x1 || y0 >= y1) return;
@@ -306,14 +349,16 @@ __global__ void k_qat_generic(DevModel m, const float* __restrict__ wg, float* _
 }
 
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
-                const int* xr0, const int* yr0, const float* grid, const int* bits) {
-    const long long ntx = (long long)m.lv[0].W * m.lv[0].H;
+                const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end) {
+    const long long ntx = t_end - t_begin;
+    if (ntx <= 0) return;
     switch (shape) {
 #define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: { using S = FixedShape<NIN, H1, H2, NOUT>; \
-        k_qat_fixed<S, kQatTPB><<<blocks_for(ntx, kQatTPB), kQatTPB, S::SIZE * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits); break; }
+        k_qat_fixed<S, kQatTPB><<<blocks_for(ntx, kQatTPB), kQatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits, \
+                                                                                                      t_begin, t_end); break; }
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
-        default: k_qat_generic<<<blocks_for(ntx, 128), 128, m.P * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits);
+        default: k_qat_generic<<<blocks_for(ntx, 128), 128, m.P * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits, t_begin, t_end);
     }
     NTCB_CHECK(cudaGetLastError());
 }

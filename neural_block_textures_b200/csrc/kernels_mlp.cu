@@ -100,91 +100,27 @@ __device__ __forceinline__ double cta_sum(double v, double* red) {
     return r;   // valid in thread 0
 }
 
-template <class S>
-constexpr int shape_size() {
-    if constexpr (S::kFixed) return S::SIZE;
-    else return 0;
+// The perturbed weight of slot k for sign +/- : ES w0 +- sigma eps with each perturbed weight rounded once,
+// fma(+-sigma, eps, w0) (MlpTrainer::step, main.cpp:1856); FD: w0 except weight j at the float-realised
+// w0[j] + h / w0[j] - h (main.cpp:1906-1910).
+__device__ __forceinline__ void perturbed_weight(const PopArgs& a, const float* e, int k, int cand, float& wp, float& wm) {
+    const float w0 = a.w0[k];
+    wp = w0; wm = w0;
+    if (e) { const float ek = e[k]; wp = fmaf(a.sigma, ek, w0); wm = fmaf(-a.sigma, ek, w0); }
+    else if (a.mode == 1 && k == cand) { wp = w0 + a.fd_h; wm = w0 - a.fd_h; }
 }
 
-// Builds the CTA's two weight sets (+ and -) in shared memory from the base weights. ES: w0 +- sigma
-// eps with each perturbed weight rounded once, fma(+-sigma, eps, w0) (MlpTrainer::step, main.cpp:1856).
-// FD: both sets equal w0 except weight j at the float-realised w0[j] + h / w0[j] - h (main.cpp:1906-1910).
-template <class S>
-__device__ __forceinline__ void build_weight_pair(const DevModel& m, const PopArgs& a, int cand, float* ws) {
-    constexpr int kSize = shape_size<S>();
-    const int setsz = S::kFixed ? kSize : m.P;
+// Runtime-shaped kernels: both weight sets in the reference's flat layout.
+__device__ __forceinline__ void build_weight_pair_flat(const DevModel& m, const PopArgs& a, int cand, float* ws) {
     const float* e = (a.mode == 0 && a.sigma != 0.0f) ? a.eps + (long long)(cand - a.cand_begin) * m.P : nullptr;
-    if constexpr (S::kFixed) {
-        for (int k = threadIdx.x; k < kSize; k += blockDim.x) { ws[k] = 0.0f; ws[kSize + k] = 0.0f; }
-        __syncthreads();
-    }
-    for (int k = threadIdx.x; k < m.P; k += blockDim.x) {
-        const float w0 = a.w0[k];
-        float wp = w0, wm = w0;
-        if (e) { const float ek = e[k]; wp = fmaf(a.sigma, ek, w0); wm = fmaf(-a.sigma, ek, w0); }
-        else if (a.mode == 1 && k == cand) { wp = w0 + a.fd_h; wm = w0 - a.fd_h; }
-        int sl = k;
-        if constexpr (S::kFixed) sl = S::slot(k);
-        ws[sl] = wp; ws[setsz + sl] = wm;
-    }
+    for (int k = threadIdx.x; k < m.P; k += blockDim.x) perturbed_weight(a, e, k, cand, ws[k], ws[m.P + k]);
     __syncthreads();
 }
 
 // One CTA per (candidate pair, batch chunk): the + and - weight sets are evaluated over the chunk's
-// minibatch rows; the per-row weighted squared errors are accumulated in double (loss_subset,
-// main.cpp:1739-1750) and reduced in a fixed order into part[cand][sign][chunk].
-template <class S, int TPB, int R>
-__global__ void __launch_bounds__(TPB) k_pop_eval_fixed(DevModel m, PopArgs a, int chunks) {
-    extern __shared__ __align__(16) float ws[];
-    __shared__ double red[TPB / 32];
-    const int cand = a.cand_begin + blockIdx.x;
-    const int chunk = blockIdx.y;
-    build_weight_pair<S>(m, a, cand, ws);
-    const int row0 = chunk * a.chunk;
-    const int row1 = min(a.M, row0 + a.chunk);
-    double acc[2] = {0.0, 0.0};
-#pragma unroll 1
-    for (int sg = 0; sg < 2; sg++) {
-        const float* w = ws + sg * S::SIZE;
-#pragma unroll 1
-        for (int base = row0; base < row1; base += TPB * R) {
-            float x[R][S::NIN];
-            int rows[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int s = base + r * TPB + threadIdx.x;
-                rows[r] = s;
-                const int sc = min(s, a.M - 1);
-#pragma unroll
-                for (int i = 0; i < S::NIN; i++) x[r][i] = __ldg(a.feat_t + (long long)i * a.mstride + sc);
-            }
-            float o[R][S::NOUT];
-            fixed_forward<S, R>(w, x, o, m.leak, m.clamp_out);
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                if (rows[r] < row1) {
-                    double e = 0.0;
-#pragma unroll
-                    for (int c = 0; c < S::NOUT; c++) {
-                        const float d = o[r][c] - __ldg(a.tgt_t + (long long)c * a.mstride + rows[r]);
-                        e += (double)(m.cw[c] * (d * d));
-                    }
-                    acc[sg] += e;
-                }
-            }
-        }
-    }
-    const double sp = cta_sum<TPB>(acc[0], red);
-    const double sm = cta_sum<TPB>(acc[1], red);
-    if (threadIdx.x == 0) {
-        double* dst = a.part + (long long)blockIdx.x * 2 * chunks;
-        dst[chunk] = sp;
-        dst[chunks + chunk] = sm;
-    }
-}
-
-// The same evaluation on the packed FP32 pipe: rows in pairs (R2 pairs = 2 R2 rows per thread), weight sets
-// stored duplicated ({w, w} per slot, 2 * S::SIZE floats per set). Values are bit-identical to k_pop_eval_fixed.
+// minibatch rows on the packed FP32 pipe (R2 row pairs per thread per pass, weight sets stored duplicated:
+// {w, w} per slot, 2 * S::SIZE floats per set); the per-row weighted squared errors are accumulated in
+// double (loss_subset, main.cpp:1739-1750) and reduced in a fixed order into part[cand][sign][chunk].
 template <class S>
 __device__ __forceinline__ void build_weight_pair_x2(const DevModel& m, const PopArgs& a, int cand, float* ws) {
     constexpr int kSet = 2 * S::SIZE;
@@ -192,10 +128,8 @@ __device__ __forceinline__ void build_weight_pair_x2(const DevModel& m, const Po
     for (int k = threadIdx.x; k < 2 * kSet; k += blockDim.x) ws[k] = 0.0f;
     __syncthreads();
     for (int k = threadIdx.x; k < m.P; k += blockDim.x) {
-        const float w0 = a.w0[k];
-        float wp = w0, wm = w0;
-        if (e) { const float ek = e[k]; wp = fmaf(a.sigma, ek, w0); wm = fmaf(-a.sigma, ek, w0); }
-        else if (a.mode == 1 && k == cand) { wp = w0 + a.fd_h; wm = w0 - a.fd_h; }
+        float wp, wm;
+        perturbed_weight(a, e, k, cand, wp, wm);
         const int sl = 2 * S::slot(k);
         *reinterpret_cast<float2*>(ws + sl) = make_float2(wp, wp);
         *reinterpret_cast<float2*>(ws + kSet + sl) = make_float2(wm, wm);
@@ -204,7 +138,7 @@ __device__ __forceinline__ void build_weight_pair_x2(const DevModel& m, const Po
 }
 
 template <class S, int TPB, int R2>
-__global__ void __launch_bounds__(TPB) k_pop_eval_x2(DevModel m, PopArgs a, int chunks) {
+__global__ void __launch_bounds__(TPB, S::kPopMinBlocks) k_pop_eval_x2(DevModel m, PopArgs a, int chunks) {
     extern __shared__ __align__(16) float ws[];
     __shared__ double red[TPB / 32];
     constexpr int R = 2 * R2;
@@ -267,7 +201,7 @@ __global__ void __launch_bounds__(TPB) k_pop_eval_generic(DevModel m, PopArgs a,
     __shared__ double red[TPB / 32];
     const int cand = a.cand_begin + blockIdx.x;
     const int chunk = blockIdx.y;
-    build_weight_pair<GenericShape>(m, a, cand, ws);
+    build_weight_pair_flat(m, a, cand, ws);
     const int row0 = chunk * a.chunk;
     const int row1 = min(a.M, row0 + a.chunk);
     double acc[2] = {0.0, 0.0};
@@ -294,14 +228,7 @@ template <class S>
 static void launch_pop_fixed(cudaStream_t s, const DevModel& m, const PopArgs& a) {
     const int chunks = pop_chunks(a.M, a.chunk);
     dim3 grid((unsigned)a.ncand, (unsigned)chunks);
-    static const int variant = [] { const char* e = getenv("NTCB_POP_VARIANT"); return (e && e[0] == 's') ? 0 : 1; }();
-    if (variant == 1) {
-        const size_t smem = 4 * S::SIZE * sizeof(float);
-        k_pop_eval_x2<S, kPopTPB, kPopRows / 2><<<grid, kPopTPB, smem, s>>>(m, a, chunks);
-    } else {
-        const size_t smem = 2 * S::SIZE * sizeof(float);
-        k_pop_eval_fixed<S, kPopTPB, kPopRows><<<grid, kPopTPB, smem, s>>>(m, a, chunks);
-    }
+    k_pop_eval_x2<S, kPopTPB, kPopRows / 2><<<grid, kPopTPB, 4 * S::SIZE * sizeof(float), s>>>(m, a, chunks);
 }
 
 void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a) {
@@ -454,31 +381,34 @@ void launch_adam(cudaStream_t s, float* theta, const float* g, float* m, float* 
 template <class S, int TPB, int R>
 __global__ void __launch_bounds__(TPB) k_decode_fixed(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                       float* __restrict__ img) {
+    constexpr int R2 = R / 2;
     extern __shared__ __align__(16) float ws[];
-    for (int k = threadIdx.x; k < S::SIZE; k += TPB) ws[k] = 0.0f;
-    __syncthreads();
-    for (int k = threadIdx.x; k < m.P; k += TPB) ws[S::slot(k)] = wg[k];
-    __syncthreads();
+    load_weights_x2<S>(wg, m.P, ws);
     const long long npix = (long long)m.W * m.H;
     const long long base = (long long)blockIdx.x * TPB * R;
-    float x[R][S::NIN];
+    float2 x[R2][S::NIN];
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        long long p = base + r * TPB + threadIdx.x;
-        if (p >= npix) p = npix - 1;
-        float f[kMaxIn];
-        pixel_features(m, z, (int)(p % m.W), (int)(p / m.W), f);
+    for (int h = 0; h < R2; h++) {
+        long long pa = base + (2 * h) * TPB + threadIdx.x, pb = base + (2 * h + 1) * TPB + threadIdx.x;
+        if (pa >= npix) pa = npix - 1;
+        if (pb >= npix) pb = npix - 1;
+        float fa[kMaxIn], fb[kMaxIn];
+        pixel_features(m, z, (int)(pa % m.W), (int)(pa / m.W), fa);
+        pixel_features(m, z, (int)(pb % m.W), (int)(pb / m.W), fb);
 #pragma unroll
-        for (int i = 0; i < S::NIN; i++) x[r][i] = f[i];
+        for (int i = 0; i < S::NIN; i++) x[h][i] = make_float2(fa[i], fb[i]);
     }
-    float o[R][S::NOUT];
-    fixed_forward<S, R>(ws, x, o, m.leak, m.clamp_out);
+    float2 o[R2][S::NOUT];
+    fixed_forward_x2<S, R2>(ws, x, o, m.leak, m.clamp_out);
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        const long long p = base + r * TPB + threadIdx.x;
-        if (p < npix)
+    for (int h = 0; h < R2; h++) {
+        const long long pa = base + (2 * h) * TPB + threadIdx.x, pb = base + (2 * h + 1) * TPB + threadIdx.x;
+        if (pa < npix)
 #pragma unroll
-            for (int c = 0; c < S::NOUT; c++) img[p * S::NOUT + c] = o[r][c];
+            for (int c = 0; c < S::NOUT; c++) img[pa * S::NOUT + c] = o[h][c].x;
+        if (pb < npix)
+#pragma unroll
+            for (int c = 0; c < S::NOUT; c++) img[pb * S::NOUT + c] = o[h][c].y;
     }
 }
 
@@ -498,7 +428,7 @@ void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w,
     const long long npix = (long long)m.W * m.H;
     switch (shape) {
 #define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: { using S = FixedShape<NIN, H1, H2, NOUT>; \
-        k_decode_fixed<S, kDecTPB, kDecRows><<<blocks_for(npix, kDecTPB * kDecRows), kDecTPB, S::SIZE * sizeof(float), s>>>(m, w, z, img); break; }
+        k_decode_fixed<S, kDecTPB, kDecRows><<<blocks_for(npix, kDecTPB * kDecRows), kDecTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, z, img); break; }
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: k_decode_generic<<<blocks_for(npix, 128), 128, m.P * sizeof(float), s>>>(m, w, z, img);

@@ -1,18 +1,22 @@
-// Register-tiled MLP forward for the population kernels.
+// Register-tiled MLP forward on the packed FP32 pipe, for the population kernels.
 //
 // The reference evaluates one pixel per thread and reads every weight from shared memory once per
-// FFMA (cuda/ntc_cuda.cu:164-194, loops predicated to a 32/64 maximum width). Here a thread owns R
-// rows (R pixels, or R candidates of one pixel) whose activations live in registers; each broadcast
-// LDS.128 of four weights feeds 4R FFMAs. The hidden layer 2 -> output layer product is streamed:
-// hidden unit j is computed, activated and immediately folded into the output accumulators, so only
-// the layer-1 activations (R x H1) and the outputs (R x NOUT) are register-resident.
+// FFMA (cuda/ntc_cuda.cu:164-194, loops predicated to a 32/64 maximum width). Here a thread owns R2 row
+// pairs (two pixels, or two candidates of one pixel, per pair) whose activations live in registers as
+// float2 (.x = first row, .y = second row). sm_100's FFMA2 (__ffma2_rn) performs two independent
+// round-to-nearest FMAs per instruction, so every value is bit-identical to a scalar FMA chain while the
+// FMA issue count halves. Weight sets are stored in shared memory with every weight duplicated, {w, w},
+// so one broadcast LDS.128 delivers two weight pairs with no register moves. The hidden layer 2 ->
+// output layer product is streamed: hidden unit j is computed, activated and immediately folded into
+// the output accumulators, so only the layer-1 activations and the outputs are register-resident.
 //
 // Evaluation order per unit is the reference's (mlp_forward, main.cpp:603-627): s = bias, then
 // s += w[i] * a[i] for i ascending (one FMA each), so every unit's value is the same FMA chain the
 // reference CUDA backend computes. The output layer's chain over hidden units j also starts from its
 // bias and runs j ascending, exactly as a separate pass would.
 //
-// Shared-memory layout of one weight set for a FixedShape (floats):
+// Shared-memory layout of one weight set for a FixedShape, in floats before the duplication (each slot
+// then occupies two floats, so every offset doubles):
 //   W0T [NIN][H1]   layer-1 weights transposed (column i of W0 contiguous)
 //   b0  [H1]
 //   W1  [H2][H1]    layer-2 weights, row j contiguous
@@ -37,8 +41,11 @@ struct FixedShape {
     static constexpr int oB1 = oW1 + H2 * H1;
     static constexpr int oW2T = (oB1 + H2 + 3) / 4 * 4;
     static constexpr int oB2 = oW2T + H2 * NOUTP;
-    static constexpr int SIZE = (oB2 + NOUTP + 3) / 4 * 4;
+    static constexpr int SIZE = (oB2 + NOUTP + 3) / 4 * 4;   // slots per set (2 * SIZE floats in shared memory)
     static constexpr int P = H1 * NIN + H1 + H2 * H1 + H2 + NOUT * H2 + NOUT;
+    // Register bound of the population kernel: 4 resident CTAs of 128 threads (128 registers) when the
+    // tile fits without spilling, 2 otherwise (the 12-output material shape).
+    static constexpr int kPopMinBlocks = NOUT <= 3 ? 4 : 2;
     static_assert(H1 % 4 == 0 && H2 % 4 == 0, "hidden widths of a fixed shape are multiples of 4");
 
     __host__ __device__ static int slot(int k) {
@@ -65,86 +72,8 @@ struct GenericShape {
 };
 
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-
-// Forward of R rows through a FixedShape weight set `w` (shared memory). x: inputs, o: outputs.
-template <class S, int R>
-__device__ __forceinline__ void fixed_forward(const float* __restrict__ w, const float (&x)[R][S::NIN],
-                                              float (&o)[R][S::NOUT], float leak, int clamp_out) {
-    float a[R][S::H1];
-#pragma unroll
-    for (int j = 0; j < S::H1; j += 4) {
-        const float4 b = lds4(w + S::oB0 + j);
-#pragma unroll
-        for (int r = 0; r < R; r++) { a[r][j] = b.x; a[r][j + 1] = b.y; a[r][j + 2] = b.z; a[r][j + 3] = b.w; }
-    }
-#pragma unroll
-    for (int i = 0; i < S::NIN; i++) {
-#pragma unroll
-        for (int j = 0; j < S::H1; j += 4) {
-            const float4 c = lds4(w + S::oW0T + i * S::H1 + j);
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                a[r][j] = fmaf(c.x, x[r][i], a[r][j]);
-                a[r][j + 1] = fmaf(c.y, x[r][i], a[r][j + 1]);
-                a[r][j + 2] = fmaf(c.z, x[r][i], a[r][j + 2]);
-                a[r][j + 3] = fmaf(c.w, x[r][i], a[r][j + 3]);
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int j = 0; j < S::H1; j++) a[r][j] = leaky(a[r][j], leak);
-
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int k = 0; k < S::NOUT; k++) o[r][k] = w[S::oB2 + k];
-
-#pragma unroll 2
-    for (int j = 0; j < S::H2; j++) {
-        float s[R];
-        const float bj = w[S::oB1 + j];
-#pragma unroll
-        for (int r = 0; r < R; r++) s[r] = bj;
-        const float* wr = w + S::oW1 + j * S::H1;
-#pragma unroll
-        for (int i = 0; i < S::H1; i += 4) {
-            const float4 c = lds4(wr + i);
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                s[r] = fmaf(c.x, a[r][i], s[r]);
-                s[r] = fmaf(c.y, a[r][i + 1], s[r]);
-                s[r] = fmaf(c.z, a[r][i + 2], s[r]);
-                s[r] = fmaf(c.w, a[r][i + 3], s[r]);
-            }
-        }
-        float wo[S::NOUTP];
-#pragma unroll
-        for (int k = 0; k < S::NOUTP; k += 4) {
-            const float4 c = lds4(w + S::oW2T + j * S::NOUTP + k);
-            wo[k] = c.x; wo[k + 1] = c.y; wo[k + 2] = c.z; wo[k + 3] = c.w;
-        }
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            const float h = leaky(s[r], leak);
-#pragma unroll
-            for (int k = 0; k < S::NOUT; k++) o[r][k] = fmaf(wo[k], h, o[r][k]);
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int k = 0; k < S::NOUT; k++) o[r][k] = out_act(o[r][k], clamp_out);
-}
-
-// ---------------------------------------------------------------------------------------------
-// Paired-row variant on the packed FP32 pipe (sm_100 FFMA2: __ffma2_rn performs two independent
-// round-to-nearest FMAs, so every value is bit-identical to the scalar path). Rows are processed in
-// pairs (.x = row 2q, .y = row 2q + 1); the weight set is stored with every weight duplicated,
-// {w, w}, so one broadcast LDS.128 delivers two weight pairs with no register moves. Shared layout:
-// the FixedShape layout with each float slot doubled (2 * S::SIZE floats per set, offsets doubled).
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
 __device__ __forceinline__ float2 leaky2(float2 s, float leak, bool leak_unit) {
     // For 0 <= leak <= 1, max(x, leak x) equals (x > 0 ? x : leak x) for every float, signed zeros and
     // NaN included; other slopes take the select.
@@ -153,6 +82,19 @@ __device__ __forceinline__ float2 leaky2(float2 s, float leak, bool leak_unit) {
     return make_float2(s.x > 0.0f ? s.x : t.x, s.y > 0.0f ? s.y : t.y);
 }
 
+// Stage the flat weights wg (reference layout) into shared memory as one duplicated FixedShape set.
+template <class S>
+__device__ __forceinline__ void load_weights_x2(const float* __restrict__ wg, int P, float* ws) {
+    for (int k = threadIdx.x; k < 2 * S::SIZE; k += blockDim.x) ws[k] = 0.0f;
+    __syncthreads();
+    for (int k = threadIdx.x; k < P; k += blockDim.x) {
+        const float v = wg[k];
+        *reinterpret_cast<float2*>(ws + 2 * S::slot(k)) = make_float2(v, v);
+    }
+    __syncthreads();
+}
+
+// Forward of R2 row pairs through one duplicated weight set `w` (shared memory). x: inputs, o: outputs.
 template <class S, int R2>
 __device__ __forceinline__ void fixed_forward_x2(const float* __restrict__ w, const float2 (&x)[R2][S::NIN],
                                                  float2 (&o)[R2][S::NOUT], float leak, int clamp_out) {

@@ -1,35 +1,44 @@
-"""Population sharding of the MLP ES step over G ranks (one process and one GPU per rank).
+"""Sharding one ES training iteration over G ranks (one process and one GPU per rank).
 
-Rank r evaluates the antithetic pairs [r N / G, (r + 1) N / G) of every step, regenerating their noise from
-the counter (no noise crosses the wire), and contributes 2 doubles per pair (L+, L-). One all-gather
-(NCCL over NVLink on GPUs, gloo in the CPU tests) gives every rank the fitness of all N pairs in pair order,
-from which each rank computes the identical ES gradient and Adam step, so the weight replicas stay
-bit-identical without exchanging weights. The latent ES step and the selector search run as replicas.
+* MLP ES step — the population: rank r evaluates the antithetic pairs [r N / G, (r + 1) N / G), regenerating
+  their noise from the counter (no noise crosses the wire), and contributes 2 doubles per pair (L+, L-). One
+  all-gather gives every rank the fitness of all N pairs in pair order; each rank computes the identical ES
+  gradient and Adam step, so the weight replicas stay bit-identical without exchanging weights.
+* Latent ES step — the image: rank r evaluates the K pairs' per-pixel loss differences for image rows
+  [r H / G, (r + 1) H / G); one in-place all-gather per pair plane gives every rank the full [K][W H] array,
+  from which each rank runs the identical footprint gathers, Adam and snap.
+* Selector search — level-0 texel rows: rank r searches rows [r LH / G, (r + 1) LH / G) (texels are
+  independent); one all-gather of the level installs every rank's result everywhere.
+
+The exchanges run over NCCL (NVLink) on GPUs, over gloo in the CPU tests.
 """
 from __future__ import annotations
 
+import contextlib
+
 
 def pair_range(N: int, world: int, rank: int) -> tuple[int, int]:
+    return even_range(N, world, rank, "pairs")
+
+
+def even_range(n: int, world: int, rank: int, what: str = "items") -> tuple[int, int]:
     if world < 1 or not 0 <= rank < world:
         raise ValueError("bad rank / world size")
-    if N % world:
-        raise ValueError(f"{N} pairs do not split evenly over {world} ranks")
-    per = N // world
+    if n % world:
+        raise ValueError(f"{n} {what} do not split evenly over {world} ranks")
+    per = n // world
     return rank * per, (rank + 1) * per
 
 
-def _ptr(x):
-    return x if isinstance(x, int) else x.data_ptr()
-
-
 class ShardedES:
-    """Drives trainer.shard_mlp_eval / shard_mlp_apply around one all-gather of the per-pair fitness.
+    """Drives a trainer's ntcb_shard_* entry points around the all-gathers.
 
-    `trainer` is a neural_block_textures_b200.Trainer (or any object with the same two methods); `dist` is
-    torch.distributed with an initialised process group; `device` is where the fitness buffers live (the
-    trainer's GPU, or "cpu" for a gloo group)."""
+    `trainer` is a neural_block_textures_b200.Trainer (or any object with the same methods); `dist` is
+    torch.distributed with an initialised process group; `device` is where the exchange buffers live (the
+    trainer's GPU, or "cpu" for a gloo group); `stream` (optional) is the CUDA stream the trainer launches on.
+    `image` = (W, H) and `level0` = (LW, LH, LC) enable the sharded latent step and selector search."""
 
-    def __init__(self, trainer, dist, N: int, device="cuda", stream=None):
+    def __init__(self, trainer, dist, N: int, device="cuda", stream=None, K: int = 0, image=None, level0=None):
         import torch
         self.t, self.dist, self.N = trainer, dist, N
         self.world, self.rank = dist.get_world_size(), dist.get_rank()
@@ -38,12 +47,45 @@ class ShardedES:
         self.fit_local = torch.zeros(2 * per, dtype=torch.float64, device=device)
         self.fit_all = torch.zeros(2 * N, dtype=torch.float64, device=device)
         self.stream = stream
+        self.dpix = None
+        if image is not None and K > 0:
+            W, H = image
+            self.W = W
+            self.r0, self.r1 = even_range(H, self.world, self.rank, "image rows")
+            self.dpix = torch.zeros(K, W * H, dtype=torch.float32, device=device)
+        self.l0 = None
+        if level0 is not None:
+            LW, LH, LC = level0
+            self.tr0, self.tr1 = even_range(LH, self.world, self.rank, "level-0 texel rows")
+            self.row_floats = LW * LC
+            self.l0 = torch.zeros(LW * LH * LC, dtype=torch.float32, device=device)
+
+    def _ctx(self):
+        import torch
+        return torch.cuda.stream(self.stream) if self.stream is not None else contextlib.nullcontext()
 
     def step(self, it: int, sigma: float, lr: float, M: int) -> None:
-        import contextlib
-        import torch
+        """One MLP ES step (mlp_step)."""
         self.t.shard_mlp_eval(it, sigma, self.N, M, self.p0, self.p1, self.fit_local)
-        ctx = torch.cuda.stream(self.stream) if self.stream is not None else contextlib.nullcontext()
-        with ctx:
+        with self._ctx():
             self.dist.all_gather_into_tensor(self.fit_all, self.fit_local)
         self.t.shard_mlp_apply(it, sigma, lr, self.N, M, self.fit_all)
+
+    def lat_step(self, it: int, sigma: float, lr: float, K: int) -> None:
+        """One latent ES step (lat_step)."""
+        assert self.dpix is not None and K == self.dpix.shape[0]
+        self.t.shard_lat_eval(sigma, K, self.r0, self.r1, self.dpix)
+        a, b = self.r0 * self.W, self.r1 * self.W
+        with self._ctx():
+            for k in range(K):
+                self.dist.all_gather_into_tensor(self.dpix[k], self.dpix[k, a:b])
+        self.t.shard_lat_apply(it, sigma, lr, K, self.dpix)
+
+    def qat_search(self) -> None:
+        """One selector search (qat_search)."""
+        assert self.l0 is not None
+        self.t.shard_qat(self.tr0, self.tr1, self.l0)
+        a, b = self.tr0 * self.row_floats, self.tr1 * self.row_floats
+        with self._ctx():
+            self.dist.all_gather_into_tensor(self.l0, self.l0[a:b])
+        self.t.shard_qat_apply(self.l0)

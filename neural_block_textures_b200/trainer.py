@@ -187,3 +187,22 @@ class Trainer:
         """fit_all_dev: a CUDA tensor (or device pointer) with all N pairs' (L+, L-) in pair order."""
         ptr = fit_all_dev if isinstance(fit_all_dev, int) else fit_all_dev.data_ptr()
         self.lib.ntcb_shard_mlp_apply(self.h, it, sigma, lr, N, M, C.c_void_p(ptr))
+
+    def shard_lat_eval(self, sigma: float, K: int, row_begin: int, row_end: int, dpix_dev) -> None:
+        """dpix_dev: a CUDA tensor [K, W * H] of float32; rows [row_begin, row_end) of every plane are written."""
+        self.lib.ntcb_shard_lat_eval(self.h, sigma, K, row_begin, row_end, C.c_void_p(_dptr(dpix_dev)))
+
+    def shard_lat_apply(self, it: int, sigma: float, lr: float, K: int, dpix_all_dev) -> None:
+        self.lib.ntcb_shard_lat_apply(self.h, it, sigma, lr, K, C.c_void_p(_dptr(dpix_all_dev)))
+
+    def shard_qat(self, trow_begin: int, trow_end: int, level0_dev) -> None:
+        """level0_dev: a CUDA tensor of the level-0 W * H * C floats; the searched rows are written into it."""
+        self.lib.ntcb_shard_qat(self.h, trow_begin, trow_end, C.c_void_p(_dptr(level0_dev)))
+
+    def shard_qat_apply(self, level0_all_dev) -> None:
+        self.lib.ntcb_shard_qat_apply(self.h, C.c_void_p(_dptr(level0_all_dev)))
+
+
+def _dptr(x) -> int:
+    return x if isinstance(x, int) else x.data_ptr()
+

@@ -59,6 +59,60 @@ def _rank_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
+class PlumbingTrainer:
+    """Writes known values into its own rows / texel rows and records what the exchange delivered."""
+    W, H, LW, LH, LC, K = 12, 8, 6, 4, 2, 3
+
+    def shard_lat_eval(self, sigma, K, r0, r1, dpix):
+        for k in range(K):
+            for p in range(r0 * self.W, r1 * self.W):
+                dpix[k, p] = 1000.0 * k + p
+
+    def shard_lat_apply(self, it, sigma, lr, K, dpix_all):
+        self.dpix = dpix_all.clone()
+
+    def shard_qat(self, t0, t1, l0):
+        n = self.LW * self.LC
+        for i in range(t0 * n, t1 * n):
+            l0[i] = -1.0 - i
+
+    def shard_qat_apply(self, l0_all):
+        self.l0 = l0_all.clone()
+
+
+def _plumbing_main(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        t = PlumbingTrainer()
+        es = ShardedES(t, dist, 4, device="cpu", K=t.K, image=(t.W, t.H), level0=(t.LW, t.LH, t.LC))
+        es.lat_step(1, 0.05, 0.0, t.K)
+        es.qat_search()
+        np.save(os.path.join(out_dir, f"d{rank}.npy"), t.dpix.numpy())
+        np.save(os.path.join(out_dir, f"l{rank}.npy"), t.l0.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_latent_and_qat_row_sharding_plumbing(tmp_path):
+    """Two gloo ranks: each fills only its own image rows / level-0 texel rows; after the all-gathers every rank
+    holds the whole arrays in row order."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_plumbing_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    T = PlumbingTrainer
+    want_d = np.array([[1000.0 * k + p for p in range(T.W * T.H)] for k in range(T.K)], np.float32)
+    want_l = np.array([-1.0 - i for i in range(T.LW * T.LH * T.LC)], np.float32)
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"d{r}.npy"), want_d)
+        assert np.array_equal(np.load(tmp_path / f"l{r}.npy"), want_l)
+
+
 def test_pair_range():
     assert [pair_range(16, 4, r) for r in range(4)] == [(0, 4), (4, 8), (8, 12), (12, 16)]
     with pytest.raises(ValueError):
