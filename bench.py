@@ -141,6 +141,8 @@ def reference_arm(args, world, rank):
 def _ref_sample_setup(cfg):
     from oracle.oracle import RefSession, refcpu_lib
     lib = refcpu_lib()
+    # torchrun exports OMP_NUM_THREADS=1 to every rank; the reference CPU path gets every core this process may use.
+    lib.ref_set_threads(len(os.sched_getaffinity(0)))
     cores = int(lib.ref_max_threads())
     spec = cfg.spec
     sess = RefSession(spec, cfg.target())

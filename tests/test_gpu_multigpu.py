@@ -1,0 +1,92 @@
+"""Population / image / texel-row sharding on 2 GPUs over NCCL (neural_block_textures_b200.shard.ShardedES, the code
+bench.py runs with torchrun): two ranks must end with the same weights and latent as one GPU running the plain
+Trainer steps, bit for bit (every per-pair, per-pixel and per-texel value is computed by the same kernels
+whichever rank computes it, and the gradient sums keep their order). Needs >= 2 GPUs; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+N, M, K, ITERS = 32, 256, 4, 3
+
+
+def _spec():
+    from neural_block_textures_b200.model import LevelSpec, ModelSpec
+    return ModelSpec(64, 64, [LevelSpec(64, 64, 1, True), LevelSpec(16, 16, 2)], qat_bits=(2,), max_pairs=N, max_batch=M, seed=21)
+
+
+def _target(spec):
+    from neural_block_textures_b200 import synth
+    return synth.to_target([synth.synth_rgb8(spec.W, spec.H, 9)])
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from neural_block_textures_b200 import Trainer
+    from neural_block_textures_b200.shard import ShardedES
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        spec = _spec()
+        z, p = spec.init_params()
+        tr = Trainer()
+        ok, why = tr.init(spec.model_desc(), z, p, _target(spec))
+        assert ok, why
+        stream = torch.cuda.Stream()
+        tr.set_stream(stream.cuda_stream)
+        L0 = spec.levels[0]
+        es = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K, image=(spec.W, spec.H), level0=(L0.W, L0.H, L0.C))
+        for it in range(1, ITERS + 1):
+            es.step(it, 0.02, 0.005, M)
+            es.lat_step(it, 0.05, 0.02, K)
+            es.qat_search()
+        zz, pp = tr.download_model()
+        np.save(os.path.join(out_dir, f"z{rank}.npy"), zz)
+        np.save(os.path.join(out_dir, f"p{rank}.npy"), pp)
+        tr.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=300)
+        assert pr.exitcode == 0
+    from neural_block_textures_b200 import Trainer
+    spec = _spec()
+    z, p = spec.init_params()
+    with Trainer() as tr:
+        ok, why = tr.init(spec.model_desc(), z, p, _target(spec))
+        assert ok, why
+        for it in range(1, ITERS + 1):
+            tr.mlp_step(it, 0.02, 0.005, N, M)
+            tr.lat_step(it, 0.05, 0.02, K)
+            tr.qat_search()
+        z1, p1 = tr.download_model()
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"p{r}.npy"), p1), f"rank {r} weights"
+        assert np.array_equal(np.load(tmp_path / f"z{r}.npy"), z1), f"rank {r} latent"
+    assert not np.array_equal(p1, p)
