@@ -43,8 +43,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--fd-steps", type=int, default=100, help="FD-phase iterations timed after the ES ones (0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-cuda", action="store_true", help="skip timing the reference's own CUDA backend (oracle/_ref/ntc_ref)")
+    ap.add_argument("--pop-kernel", default="tensor", choices=["tensor", "ffma"],
+                    help="ES population kernel: tcgen05 3xTF32 (default) or the bit-exact packed-FP32 one")
     return ap.parse_args()
 
 
@@ -176,6 +179,52 @@ def cpu_baseline_leg(cfg, budget_s=12.0):
                       f"and selector search): {dec / 1e6:.2f} M decodes each, {t_all:.1f} s"}
 
 
+def tf32_peak_tflops(n=8192, reps=20):
+    """cuBLAS TF32 GEMM throughput on this GPU (the denominator for the tensor-core population kernel)."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(n, n, device="cuda"); b = torch.randn(n, n, device="cuda"); c = torch.empty(n, n, device="cuda")
+    for _ in range(3):
+        torch.matmul(a, b, out=c)
+    e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        torch.matmul(a, b, out=c)
+    e1.record(); e1.synchronize()
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    return 2.0 * n ** 3 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
+def tc_issued_flops_per_decode(spec) -> int:
+    """Tensor FLOPs the 3xTF32 kernel issues per decode: 3 products x padded K x padded N for the two hidden
+    layers (the output layer runs on the FP32 pipe)."""
+    w = spec.widths
+    up = lambda x, m: (x + m - 1) // m * m
+    k1, n1, n2 = up(w[0] + 1, 8), up(w[1], 16), up(w[2], 16)
+    return 3 * 2 * (k1 * n1 + w[1] * n2)
+
+
+def pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks):
+    base = {"kernel": "k_pop_eval_tc (tcgen05 3xTF32)" if kernel == "tensor" else "k_pop_eval_x2 (packed FP32)",
+            "achieved": achieved, "unit": "TFLOP/s", "traffic": traffic, "flops_per_launch": eval_flops,
+            "avg_launch_ms": eval_avg_s * 1e3, "fp32_ffma_peak": ffma,
+            "frac_of_fp32_ffma_peak": (achieved / ffma) if achieved else None}
+    if kernel == "tensor" and achieved and tf32:
+        issued = achieved * tc_issued_flops_per_decode(cfg.spec) / cfg.flops_per_decode()
+        base.update({"bound": "tensor", "peak": tf32, "frac": achieved / tf32,
+                     "peak_source": "cuBLAS TF32 GEMM (8192^3) measured in bench.py on this GPU",
+                     "issued_tensor_tflops": issued, "issued_frac_of_tf32_peak": issued / tf32,
+                     "note": "achieved counts algorithmic FLOPs (2 sum n_in n_out per decode); the kernel issues "
+                             f"{tc_issued_flops_per_decode(cfg.spec)} tensor FLOPs per decode (3xTF32, padded K/N)"})
+    else:
+        base.update({"bound": "fp32", "peak": ffma, "frac": (achieved / ffma) if achieved else None,
+                     "peak_source": "FP32 FFMA throughput measured on this GPU by ntcb_fp32_peak_tflops"})
+    if achieved and "bf16_tflops" in peaks:
+        base["frac_of_measured_bf16_tensor"] = achieved / peaks["bf16_tflops"]
+    return base
+
+
 def ref_cuda_leg(cfg, n1=20, n2=120):
     """The reference's own CUDA backend (cuda/ntc_cuda.cu built unmodified for sm_100a, linked into the reference
     CLI as oracle/_ref/ntc_ref) on the same configuration and GPU. Two runs of n1 and n2 ES iterations with no
@@ -245,6 +294,7 @@ def main():
         raise SystemExit(f"init failed: {why}")
     stream = torch.cuda.Stream()
     tr.set_stream(stream.cuda_stream)
+    tr.set_pop_kernel(args.pop_kernel == "tensor")
     N, M, K = cfg.pairs, cfg.batch, cfg.lat_pairs
     from neural_block_textures_b200.shard import ShardedES, pair_range
     per = pair_range(N, world, rank)[1] - pair_range(N, world, rank)[0]
@@ -253,7 +303,7 @@ def main():
     sharded = None
     if world > 1:
         sharded = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K if has_lat else 0, image=(spec.W, spec.H),
-                            level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None)
+                            level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None, P=spec.P)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     dec = cfg.decodes_per_iter()
     decodes = sum(dec.values())
@@ -267,6 +317,20 @@ def main():
                 tr.qat_search()
         else:
             sharded.step(it, cfg.mlp_sigma, cfg.mlp_lr, M)
+            if has_lat:
+                sharded.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
+            if spec.qat_bits:
+                sharded.qat_search()
+
+    def fd_step(it):
+        if sharded is None:
+            tr.mlp_step_fd(it, cfg.fd_h, cfg.mlp_lr, M)
+            if has_lat:
+                tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
+            if spec.qat_bits:
+                tr.qat_search()
+        else:
+            sharded.fd_step(it, cfg.fd_h, cfg.mlp_lr, M)
             if has_lat:
                 sharded.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
             if spec.qat_bits:
@@ -307,6 +371,35 @@ def main():
         ms = float(t.item())
     value = decodes * args.steps / (ms * 1e-3)
 
+    # ---- FD-phase iterations (mlp_step_fd + lat_step + qat_search), same timing rules
+    fd_line = None
+    if args.fd_steps > 0:
+        for _ in range(3):
+            fd_step(it); it += 1
+        stream.synchronize()
+        if dist:
+            dist.barrier()
+        fevs = []
+        for _ in range(args.fd_steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+                e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            fd_step(it); it += 1
+            with torch.cuda.stream(stream):
+                e1.record(stream)
+            fevs.append((e0, e1))
+        stream.synchronize()
+        fms = sum(a.elapsed_time(b) for a, b in fevs)
+        if dist:
+            t = torch.tensor([fms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            fms = float(t.item())
+        fdec = cfg.decodes_per_iter(fd=True)
+        fd_line = {"steps": args.fd_steps, "ms_per_step": fms / args.fd_steps, "decodes_per_step": fdec,
+                   "value": sum(fdec.values()) * args.fd_steps / (fms * 1e-3), "unit": "decodes/s",
+                   "kernel": "k_pop_eval_x2 (packed FP32, exact) for the 2P + 2 FD candidates"}
+
     # ---- end to end through the public API with host buffers (pinned), copies inside the timed region
     zh = torch.empty(spec.nz, dtype=torch.float32, pin_memory=True).numpy()
     ph = torch.empty(spec.P, dtype=torch.float32, pin_memory=True).numpy()
@@ -335,6 +428,8 @@ def main():
     if rank == 0:
         lib = load_library()
         ffma = float(lib.ntcb_fp32_peak_tflops())
+        kernel = tr.pop_kernel()
+        tf32 = tf32_peak_tflops() if kernel == "tensor" else None
         fpd = cfg.flops_per_decode()
         eval_flops = 2 * per * M * fpd if world > 1 else 2 * N * M * fpd
         eval_avg_s = (eval_ms / max(eval_n, 1)) * 1e-3
@@ -352,17 +447,14 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg.name, "cli": cfg.cli, "decodes_per_step": dec, "parallelism": f"population x{world}",
+                       "pop_kernel": kernel,
                        "l2": "flushed between steps (256 MiB memset outside the timed events)"},
-            "roofline": {"kernel": "k_pop_eval_fixed (MLP ES population evaluation)", "bound": "fp32",
-                         "achieved": achieved, "peak": ffma, "unit": "TFLOP/s",
-                         "frac": (achieved / ffma) if achieved else None, "traffic": traffic,
-                         "peak_source": "FP32 FFMA throughput measured on this GPU by ntcb_fp32_peak_tflops",
-                         "flops_per_launch": eval_flops, "avg_launch_ms": eval_avg_s * 1e3,
-                         "frac_of_measured_bf16_tensor": (achieved / peaks["bf16_tflops"]) if (achieved and "bf16_tflops" in peaks) else None},
+            "roofline": pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks),
             "phase_ms_per_step": {"mlp_eval": eval_ms / args.steps, "lat_eval": lat_ms / args.steps, "qat": qat_ms / args.steps},
             "e2e": {"value": e2e_value, "unit": "decodes/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
             "gpu_launches": launches,
+            "fd_phase": fd_line,
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

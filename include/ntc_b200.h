@@ -163,6 +163,15 @@ int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi);
 double ntcb_fp32_peak_tflops(void);
 /* Number of kernels this trainer has launched since creation. */
 long long ntcb_launch_count(const ntcb_trainer* t);
+/* Which kernel evaluates ES pairs (mlp_step, ntcb_shard_mlp_eval). tensor = 1 (the default): tcgen05 MMAs with
+ * 3xTF32 products, FP32-level accuracy (fitness within ~1e-6 relative of the exact kernel); tensor = 0: the
+ * packed-FP32 kernel, bit-identical per unit to the reference CUDA backend (cuda/ntc_cuda.cu:164-194). The FD
+ * step always uses the exact kernel, and runtime-shaped models (no fixed-shape kernel) always do too. The
+ * environment variable NTCB_POP_KERNEL=ffma selects 0 at init for callers of the C++ Trainer.
+ * No counterpart in the reference. */
+void ntcb_set_pop_kernel(ntcb_trainer* t, int tensor);
+/* 1 when ES pairs currently run on the tensor-core kernel, else 0. */
+int ntcb_pop_kernel(const ntcb_trainer* t);
 
 /* Population sharding over G ranks (one process and one GPU per rank). A rank evaluates only the pairs
  * [pair_begin, pair_end) of an N-pair ES step, regenerating their noise from the counter, and writes the
@@ -172,6 +181,13 @@ long long ntcb_launch_count(const ntcb_trainer* t);
  * step; every rank computes the identical update, so the replicas stay bit-identical. */
 void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, double* fit_dev);
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev);
+/* The FD step (mlp_step_fd) sharded by weight: a rank draws the step's minibatch, evaluates the unperturbed
+ * stats pair and the central differences of weights [j_begin, j_end), and writes their (lp, lm) as 2 doubles per
+ * weight into fit_dev (DEVICE, 2 * (j_end - j_begin) doubles). After the caller gathers all P weights' pairs in
+ * weight order into a device buffer of 2 * P doubles, ntcb_shard_fd_apply runs the FD gradient and Adam
+ * identically on every rank. */
+void ntcb_shard_fd_eval(ntcb_trainer* t, int it, float h, int M, int j_begin, int j_end, double* fit_dev);
+void ntcb_shard_fd_apply(ntcb_trainer* t, float h, float lr, const double* fit_all_dev);
 /* The latent ES step sharded by pixel rows: a rank writes the per-pixel loss differences of image rows
  * [row_begin, row_end) for all K pairs into dpix_dev, a DEVICE buffer laid out [K][W * H] (each pair's plane is
  * row-major, so a rank's rows are one contiguous range per plane); after the caller all-gathers every plane,

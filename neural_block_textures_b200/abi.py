@@ -111,11 +111,15 @@ SIGNATURES = {
     "ntcb_kernel_timing": (None, [_vp, C.c_int]),
     "ntcb_kernel_time": (None, [_vp, C.c_char_p, _dp, _ip]),
     "ntcb_launch_count": (C.c_longlong, [_vp]),
+    "ntcb_set_pop_kernel": (None, [_vp, C.c_int]),
+    "ntcb_pop_kernel": (C.c_int, [_vp]),
     "ntcb_fp32_peak_tflops": (C.c_double, []),
     "ntcb_footprint_ranges": (C.c_int, [C.c_int, C.c_int, C.c_int, _ip, _ip]),
     "ntcb_es_fitness_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.c_int, C.c_float, C.c_int, C.c_int, _fp, _fp, _fp, C.c_int, _dp,
                                           C.c_char_p, C.c_size_t]),
     "ntcb_noise_fill": (None, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_size_t, _fp, C.POINTER(C.c_uint32)]),
+    "ntcb_shard_fd_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_fd_apply": (None, [_vp, C.c_float, C.c_float, _vp]),
     "ntcb_shard_mlp_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "ntcb_shard_mlp_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _vp]),
     "ntcb_shard_lat_eval": (None, [_vp, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),

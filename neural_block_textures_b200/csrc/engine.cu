@@ -73,6 +73,10 @@ struct Trainer::Impl {
     double* part = nullptr; long long part_cap = 0;
     double *fit = nullptr, *dl = nullptr, *lsum = nullptr, *hh = nullptr;
     double* fit_stats = nullptr;
+    // ES pair evaluation: true (default) = the tensor-core kernel (3xTF32) where the shape has one; false = the
+    // packed-FP32 kernel, bit-identical per unit to the reference backend. FD always uses the latter.
+    bool tensor_pop = true;
+    int* tc_err = nullptr;   // device flag the tensor-core kernel sets when an MMA completion wait times out
     float* gpart = nullptr; long long gpart_cap = 0;
     float* qat_grid = nullptr; int* qat_bits = nullptr;
     // counters
@@ -130,7 +134,17 @@ void flush_timing(Impl& I) {
     I.pending.clear();
 }
 
-void sync(Impl& I) { NTCB_CHECK(cudaStreamSynchronize(I.stream)); }
+void sync(Impl& I) {
+    NTCB_CHECK(cudaStreamSynchronize(I.stream));
+    if (I.tc_err) {
+        int e = 0;
+        NTCB_CHECK(cudaMemcpy(&e, I.tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (e) {
+            fprintf(stderr, "ntc_b200: a tensor-core population CTA timed out waiting for its MMAs\n");
+            exit(1);
+        }
+    }
+}
 void set_device(Impl& I) { if (I.device >= 0) NTCB_CHECK(cudaSetDevice(I.device)); }
 
 // Footprint rectangles of every texel of a level (per texel column [xb, xe), per texel row [yb, ye)):
@@ -229,7 +243,7 @@ void free_all(Impl& I) {
     dfree(I.dsym); dfree(I.dcode); dfree(I.dsteps); dfree(I.dlam); dfree(I.dbits); dfree(I.ddbits); dfree(I.dcnt);
     dfree(I.w); dfree(I.wgrad); dfree(I.wm); dfree(I.wv); dfree(I.tgt); dfree(I.img);
     dfree(I.bidx); dfree(I.feat_t); dfree(I.tgt_t); dfree(I.mlp_eps); dfree(I.part);
-    dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart);
+    dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart); dfree(I.tc_err);
     dfree(I.qat_grid); dfree(I.qat_bits);
     for (auto& p : I.pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     I.pending.clear();
@@ -397,6 +411,9 @@ bool init_impl(Impl& I, const ntc_cuda::ModelDesc& d, const float* z, const floa
     NTCB_CHECK(cudaMemset(I.dl, 0, cands * sizeof(double))); NTCB_CHECK(cudaMemset(I.lsum, 0, cands * sizeof(double)));
     NTCB_CHECK(cudaMemset(I.fit, 0, 2 * cands * sizeof(double)));
     I.fit_stats = dalloc<double>(2);
+    I.tc_err = dalloc<int>(1);
+    NTCB_CHECK(cudaMemset(I.tc_err, 0, sizeof(int)));
+    if (const char* e = getenv("NTCB_POP_KERNEL")) I.tensor_pop = strcmp(e, "ffma") != 0;
     ensure_part(I, (long long)cands * 2 * 8);
     ensure_gpart(I, (long long)((I.pairs_cap + 63) / 64 + 1) * I.P);
     if (d.qat > 0) {
@@ -441,11 +458,13 @@ void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* 
     ntcb::PopArgs a{};
     a.mode = 0; a.it = it; a.sigma = sigma; a.fd_h = 0.0f; a.cand_begin = p0; a.ncand = n;
     a.M = M; a.mstride = I.mstride; a.chunk = pop_chunk(I, M);
-    a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t;
+    a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t; a.tc_err = I.tc_err;
     const int chunks = ntcb::pop_chunks(M, a.chunk);
     ensure_part(I, (long long)n * 2 * chunks);
     a.part = I.part;
-    timed(I, "mlp_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
+    timed(I, "mlp_eval", 1, [&] {
+        if (!(I.tensor_pop && ntcb::launch_pop_eval_tc(I.stream, I.shape, I.dm, a))) ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a);
+    });
     timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, n, chunks, 3.0 * (double)I.d.wsum * M, fit); });
 }
 
@@ -477,14 +496,10 @@ void mlp_step_impl(Impl& I, int it, float sigma, float lr, int N, int M) {
     es_apply(I, it, sigma, lr, N, I.fit, false);
 }
 
-void mlp_step_fd_impl(Impl& I, int it, float h, float lr, int M) {
-    require_ready(I); set_device(I);
-    if (M > I.Mcap || M < 1) {
-        fprintf(stderr, "ntc_b200: FD step with %d pixels exceeds the buffers sized at init (%d)\n", M, I.Mcap);
-        exit(1);
-    }
+// FD candidates [j0, j1) of step `it` on a fresh minibatch: the unperturbed stats pair into fit_stats
+// (cuda/ntc_cuda.cu:1059-1068), then (lp, lm) of every weight j in the range (both signs in one CTA) into fit.
+void fd_eval_part(Impl& I, int it, float h, int M, int j0, int j1, double* fit) {
     draw_batch(I, it, M);
-    // the unperturbed loss for the stats line: one sigma-0 "pair" (cuda/ntc_cuda.cu:1059-1068)
     ntcb::PopArgs a{};
     a.mode = 0; a.it = it; a.sigma = 0.0f; a.cand_begin = 0; a.ncand = 1; a.M = M; a.mstride = I.mstride;
     a.chunk = pop_chunk(I, M); a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t;
@@ -494,19 +509,31 @@ void mlp_step_fd_impl(Impl& I, int it, float h, float lr, int M) {
     const double norm = 3.0 * (double)I.d.wsum * M;
     timed(I, "fd_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
     timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, 1, chunks, norm, I.fit_stats); });
-    // central differences over every weight (both signs in one CTA)
-    a.mode = 1; a.fd_h = h; a.ncand = I.P;
+    if (j1 <= j0) return;
+    a.mode = 1; a.fd_h = h; a.cand_begin = j0; a.ncand = j1 - j0;
     timed(I, "fd_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
-    timed(I, "mlp_finish", 2, [&] {
-        ntcb::launch_pop_finish(I.stream, I.part, I.P, chunks, norm, I.fit);
-        ntcb::launch_fd_reduce(I.stream, I.fit, I.w, h, I.P, I.dl, I.hh);
-    });
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, j1 - j0, chunks, norm, fit); });
+}
+
+// FD gradient from the (lp, lm) of all P weights in I.fit and the Adam step.
+void fd_apply(Impl& I, float h, float lr) {
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_fd_reduce(I.stream, I.fit, I.w, h, I.P, I.dl, I.hh); });
     timed(I, "mlp_grad", 1, [&] {
         I.mlp_t++;
         float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
         ntcb::launch_fd_grad_adam(I.stream, I.dl, I.hh, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
     });
     I.last_N = I.P; I.last_fd = true; I.last_pairs = 0;
+}
+
+void mlp_step_fd_impl(Impl& I, int it, float h, float lr, int M) {
+    require_ready(I); set_device(I);
+    if (M > I.Mcap || M < 1) {
+        fprintf(stderr, "ntc_b200: FD step with %d pixels exceeds the buffers sized at init (%d)\n", M, I.Mcap);
+        exit(1);
+    }
+    fd_eval_part(I, it, h, M, 0, I.P, I.fit);
+    fd_apply(I, h, lr);
 }
 
 void mlp_stats_impl(Impl& I, double& batch_loss, double& diff_std) {
@@ -821,6 +848,8 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
     I.totals.erase(it);
 }
 long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
+void ntcb_set_pop_kernel(ntcb_trainer* t, int tensor) { t->impl.tensor_pop = tensor != 0; }
+int ntcb_pop_kernel(const ntcb_trainer* t) { return (t->impl.tensor_pop && t->impl.shape != 0) ? 1 : 0; }
 int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi) {
     std::vector<int> l, h;
     const bool ok = axis_ranges(npx, ntex, nearest != 0, l, h);
@@ -882,6 +911,19 @@ void ntcb_shard_qat_apply(ntcb_trainer* t, const float* level0_all_dev) {
     require_ready(I); set_device(I);
     NTCB_CHECK(cudaMemcpyAsync(I.zdec + I.dm.lv[0].off, level0_all_dev, I.n0 * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
     qat_copy_back(I);
+}
+void ntcb_shard_fd_eval(ntcb_trainer* t, int it, float h, int M, int j_begin, int j_end, double* fit_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (j_begin < 0 || j_end > I.P || j_begin > j_end || M > I.Mcap || M < 1)
+        die("shard_fd_eval: weight range or batch size outside the buffers sized at init");
+    fd_eval_part(I, it, h, M, j_begin, j_end, fit_dev);
+}
+void ntcb_shard_fd_apply(ntcb_trainer* t, float h, float lr, const double* fit_all_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    NTCB_CHECK(cudaMemcpyAsync(I.fit, fit_all_dev, 2 * (size_t)I.P * sizeof(double), cudaMemcpyDeviceToDevice, I.stream));
+    fd_apply(I, h, lr);
 }
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev) {
     Impl& I = t->impl;

@@ -31,6 +31,7 @@ struct PopArgs {
     const float* feat_t;       // [nin][mstride]
     const float* tgt_t;        // [nout][mstride]
     double* part;              // [ncand][2][chunks] per-CTA partial sums
+    int* tc_err;               // tensor-core kernel: set to 1 when an MMA completion wait timed out
 };
 int pop_chunks(int M, int chunk);
 int pop_chunk_rows(int shape);                 // rows one CTA pass covers (chunk granularity)
@@ -40,6 +41,10 @@ void launch_noise_fill(cudaStream_t s, uint64_t seed, uint32_t stream, uint32_t 
                        float* gauss, uint32_t* u32);
 void launch_mlp_noise(cudaStream_t s, uint64_t seed, int it, int pair_begin, int npairs, int P, float* eps);
 void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a);
+// Tensor-core (tcgen05, 3xTF32) population evaluation for the fixed shapes; false when the shape or the
+// chunk size (a multiple of pop_tc_rows()) does not fit it, in which case nothing was launched.
+bool launch_pop_eval_tc(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a);
+int pop_tc_rows();
 // Sum the chunk partials of every candidate in order, normalise, and write (lp, lm) pairs to fit[2*i], fit[2*i+1].
 void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit);
 // ES: dl, lsum from the fitness of all N pairs; FD: dl, hh.

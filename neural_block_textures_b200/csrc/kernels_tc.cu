@@ -1,0 +1,374 @@
+// Population evaluation on the 5th-generation tensor core (tcgen05, kind::tf32, 3xTF32 products).
+//
+// The reference evaluates one pixel per thread on the FP32 pipe (k_mlp_es_eval, cuda/ntc_cuda.cu:270-291;
+// mlp_forward, main.cpp:603-627). Here one CTA of 128 threads owns one antithetic candidate pair and a
+// chunk of minibatch rows, and each 128-row tile of each sign goes through
+//
+//   D1 = X  W0^T      X  = [features | 1 | 0 pad]  (K1 = NIN + 1 rounded up to 8; b0 folded in as a column)
+//   D2 = H1 W1^T      H1 = leaky(D1)               (K2 = H1 width)
+//   o  = b2 + W2 leaky(D2 + b1)                    (packed FP32 in registers: N = NOUT is too narrow for MMAs)
+//
+// Row r of a tile is TMEM lane r, so thread t (warp w = t / 32) owns row t: it loads its accumulator row
+// from TMEM, applies bias / activation, and stores the next layer's A operand back to TMEM (A-from-TMEM
+// MMAs). The B operands (both signs' W0 | b0 and W1) sit in shared memory, K-major without swizzle.
+// Warp 0 issues the MMAs converged, one elected lane per instruction, with compile-time TMEM / shared
+// addresses (a divergent single-thread issue loop costs ~4x more per MMA), and commits them to an mbarrier.
+//
+// Schedule per CTA (u = tile x sign): L1(u) issued -> wait, load, activation, store H -> L2(u) issued ->
+// wait, load D2 -> L1(u + 1) issued (next tile's features were prefetched one tile ahead) -> the output
+// layer and error of u run on the CUDA cores while the tensor core works on L1(u + 1). Four CTAs per SM
+// (128 TMEM columns each) overlap one another's waits.
+//
+// Precision: every tensor product is formed as 3xTF32, a b = a_hi b_hi + a_hi b_lo + a_lo b_hi with x_hi the
+// top 19 bits of x and x_lo = x - x_hi (exact), accumulated in FP32 by the tensor core. The dropped a_lo b_lo
+// term and the TF32 truncation of the lo parts leave a relative error near 2^-21 per product: FP32-level, but
+// not the bit pattern of the reference's sequential FMA chain. The output sigmoid uses the fast exponential.
+// Fitness agrees with the exact kernels to ~1e-6 relative (the pinned tolerance is 1e-5); the packed-FP32
+// kernel stays available for bit-exact runs and is always used for FD.
+//
+// Every mbarrier wait is bounded: on time-out the CTA records an error flag, stops issuing, gives the
+// outstanding MMAs one more bounded wait and still frees its TMEM.
+#include "kernels.h"
+#include "mlp_tile.cuh"
+#include "pop_common.cuh"
+#include "tc.cuh"
+
+#include <algorithm>
+
+namespace ntcb {
+
+namespace {
+
+constexpr int kTcRows = 128;                  // rows per tile (= TMEM lanes = threads of one stream)
+constexpr int kTcStreams = 4;                 // independent tile streams per CTA (one CTA per SM)
+constexpr int kTcTPB = kTcRows * kTcStreams;  // 512 threads, 16 warps
+constexpr uint32_t kTcWaitPolls = 4000;       // mbarrier polls (<= 1 ms each) before a wait is declared failed
+
+__host__ __device__ constexpr int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Canonical no-swizzle K-major float offset of element (n, k) of an [N][K] B operand: 8-row x 4-float core
+// matrices, K chunks 32 floats apart (LBO = 128 B), 8-row groups K * 8 floats apart (SBO = 32 K bytes).
+__host__ __device__ constexpr int kmajor(int n, int k, int K) { return (n >> 3) * (K * 8) + (k >> 2) * 32 + (n & 7) * 4 + (k & 3); }
+
+template <class S>
+struct TcShape {
+    static constexpr int K1 = round_up(S::NIN + 1, 8);
+    static constexpr int N1 = round_up(S::H1, 16);
+    static constexpr int K2 = S::H1;
+    static constexpr int N2 = round_up(S::H2, 16);
+    static constexpr int NOUTP = round_up(S::NOUT, 4);
+    static_assert(S::H1 % 8 == 0 && S::H2 % 8 == 0, "hidden widths must be multiples of 8");
+    static_assert(N1 <= 32 && N2 <= 32, "accumulator wider than the 32 reserved TMEM columns");
+    // shared memory, floats, per sign
+    static constexpr int oB1h = 0, oB1l = oB1h + N1 * K1;
+    static constexpr int oB2h = oB1l + N1 * K1, oB2l = oB2h + N2 * K2;
+    static constexpr int ob1 = oB2l + N2 * K2;                 // b1 [H2]
+    static constexpr int oW2 = round_up(ob1 + S::H2, 4);      // W2 transposed [H2][NOUTP]
+    static constexpr int ob2 = oW2 + S::H2 * NOUTP;           // b2 [NOUTP]
+    static constexpr int SIGN = round_up(ob2 + NOUTP, 32);
+    // TMEM columns
+    static constexpr int cD = 0, cXh = 32, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
+    static constexpr int NCOLS = 128;
+    static_assert(cHl + K2 <= NCOLS, "TMEM columns");
+
+    // Where flat reference weight k goes: an MMA B-operand element (split into hi / lo) or a plain slot.
+    __device__ static void place(int k, int& off_hi, int& off_lo) {
+        if (k < S::H1 * S::NIN) { const int j = k / S::NIN, i = k - j * S::NIN; off_hi = oB1h + kmajor(j, i, K1); off_lo = oB1l + kmajor(j, i, K1); return; }
+        k -= S::H1 * S::NIN;
+        if (k < S::H1) { off_hi = oB1h + kmajor(k, S::NIN, K1); off_lo = oB1l + kmajor(k, S::NIN, K1); return; }
+        k -= S::H1;
+        if (k < S::H2 * S::H1) { const int j = k / S::H1, i = k - j * S::H1; off_hi = oB2h + kmajor(j, i, K2); off_lo = oB2l + kmajor(j, i, K2); return; }
+        k -= S::H2 * S::H1;
+        if (k < S::H2) { off_hi = ob1 + k; off_lo = -1; return; }
+        k -= S::H2;
+        if (k < S::NOUT * S::H2) { const int o = k / S::H2, j = k - o * S::H2; off_hi = oW2 + j * NOUTP + o; off_lo = -1; return; }
+        k -= S::NOUT * S::H2;
+        off_hi = ob2 + k; off_lo = -1;
+    }
+};
+
+__device__ __forceinline__ bool elect_one() {
+    uint32_t p = 0;
+    asm volatile("{\n\t.reg .pred P1;\n\telect.sync _|P1, 0xffffffff;\n\tselp.b32 %0, 1, 0, P1;\n\t}" : "=r"(p));
+    return p != 0;
+}
+
+__device__ __forceinline__ float leaky_f(float x, float leak) { return x > 0.0f ? x : x * leak; }
+__device__ __forceinline__ float out_act_fast(float s, int clamp_out) {
+    return clamp_out ? fminf(fmaxf(s, 0.0f), 1.0f) : __frcp_rn(1.0f + __expf(-s));
+}
+
+// Split N (multiple of 8) values into hi / lo and store them to TMEM columns [ch, ch + N) / [cl, cl + N).
+template <int N>
+__device__ __forceinline__ void store_split(uint32_t trow, int ch, int cl, const float* v) {
+#pragma unroll
+    for (int q = 0; q < N; q += 8) {
+        float hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) { hi[j] = tc::tf32_hi(v[q + j]); lo[j] = v[q + j] - hi[j]; }
+        tc::st_x8(trow + ch + q, hi);
+        tc::st_x8(trow + cl + q, lo);
+    }
+}
+
+// Warp 0 (converged): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K step), then commit.
+template <int K, int N>
+__device__ __forceinline__ void issue3(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo, uint64_t* bar) {
+    constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
+    constexpr uint32_t sbo = (uint32_t)K * 32u;
+    tc::fence_after_sync();
+#pragma unroll
+    for (int s = 0; s < K / 8; s++) {
+        if (elect_one()) tc::mma_tf32_ts(d, a_lo + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, s > 0 ? 1u : 0u);
+        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_lo + 256 * s, 128, sbo), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, 1u);
+    }
+    if (elect_one()) tc::commit(bar);
+    __syncwarp();
+}
+
+// Named barrier over the 128 threads of one stream (ids 1..kTcStreams; 0 is __syncthreads), AND-reducing v.
+__device__ __forceinline__ bool stream_sync_and(int id, bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"((uint32_t)v), "r"(id) : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void stream_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// Fixed-order sum over one stream's 128 threads (warp trees, then the 4 warp totals in order); valid in its thread 0.
+__device__ __forceinline__ double stream_sum(double v, double* red4, int id) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3;
+    stream_sync(id);
+    if (lane == 0) red4[w] = v;
+    stream_sync(id);
+    return red4[0] + red4[1] + red4[2] + red4[3];
+}
+
+// One CTA per SM (a kernel that allocates TMEM is held to one resident CTA per SM), four streams of 128
+// threads. Stream g owns TMEM columns [128 g, 128 g + 128), one mbarrier, one named barrier and one pair of
+// weight sets, and works through a contiguous range of the (pair, chunk) items, so consecutive items
+// mostly share a pair and its weights are staged once. The streams interleave on the SM: one stream's
+// element-wise work overlaps the others' MMAs.
+template <class S>
+__global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a, int chunks) {
+    using T = TcShape<S>;
+    extern __shared__ __align__(1024) float dyn[];   // [kTcStreams][2][T::SIGN]
+    __shared__ __align__(8) uint64_t bars[kTcStreams];
+    __shared__ uint32_t tbase;
+    __shared__ double red[kTcStreams][4];
+    const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
+    const int bar_id = 1 + g;
+    float* sw = dyn + g * 2 * T::SIGN;
+    uint64_t* bar = &bars[g];
+
+    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, 128 * kTcStreams);
+    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
+    for (int i = threadIdx.x; i < kTcStreams * 2 * T::SIGN; i += kTcTPB) dyn[i] = 0.0f;   // padding stays zero
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+
+    const uint32_t tb = tbase + 128u * (uint32_t)g;
+    const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+    const uint32_t sb0 = tc::smem_addr(sw), sb1 = sb0 + (uint32_t)(T::SIGN * 4);
+    const float leak = m.leak;
+    const bool leak_unit = leak >= 0.0f && leak <= 1.0f;
+    uint32_t waited = 0;   // commits whose completion this thread has observed (parity of the next wait)
+    bool ok = true;
+
+    auto wait_mma = [&]() {
+        const bool done = tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+        if (done) waited++;
+        ok = ok && done;
+        tc::fence_after_sync();
+    };
+    float xr[S::NIN];      // features of the next tile (prefetched one tile ahead)
+    auto load_x = [&](int base) {
+        const int s = min(base + tid, a.M - 1);
+#pragma unroll
+        for (int i = 0; i < S::NIN; i++) xr[i] = __ldg(a.feat_t + (long long)i * a.mstride + s);
+    };
+    auto store_x = [&]() {
+        float x[T::K1];
+#pragma unroll
+        for (int i = 0; i < T::K1; i++) x[i] = i < S::NIN ? xr[i] : (i == S::NIN ? 1.0f : 0.0f);
+        store_split<T::K1>(trow, T::cXh, T::cXl, x);
+    };
+    // Output layer + error of one row for one sign, from the layer-2 accumulator row h (b1 not yet added).
+    auto finish_row = [&](const float* ws, float (&h)[S::H2], const float (&t)[S::NOUT], bool valid) -> double {
+        float2 o[T::NOUTP / 2];
+#pragma unroll
+        for (int q = 0; q < T::NOUTP; q += 2) o[q / 2] = make_float2(ws[T::ob2 + q], ws[T::ob2 + q + 1]);
+#pragma unroll
+        for (int j = 0; j < S::H2; j++) {
+            const float s = h[j] + ws[T::ob1 + j];
+            const float hj = leak_unit ? fmaxf(s, s * leak) : leaky_f(s, leak);
+            const float2 hh = make_float2(hj, hj);
+#pragma unroll
+            for (int q = 0; q < T::NOUTP; q += 4) {
+                const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + j * T::NOUTP + q);
+                o[q / 2] = __ffma2_rn(make_float2(w.x, w.y), hh, o[q / 2]);
+                o[q / 2 + 1] = __ffma2_rn(make_float2(w.z, w.w), hh, o[q / 2 + 1]);
+            }
+        }
+        double e = 0.0;
+        if (valid) {
+#pragma unroll
+            for (int c = 0; c < S::NOUT; c++) {
+                const float ov = out_act_fast((c & 1) ? o[c / 2].y : o[c / 2].x, m.clamp_out);
+                const float d = ov - t[c];
+                e += (double)(m.cw[c] * (d * d));
+            }
+        }
+        return e;
+    };
+
+    const long long items = (long long)a.ncand * chunks;
+    const long long nstreams = (long long)gridDim.x * kTcStreams, gs = (long long)blockIdx.x * kTcStreams + g;
+    const long long i0 = gs * items / nstreams, i1 = (gs + 1) * items / nstreams;
+    int cur = -1;
+#pragma unroll 1
+    for (long long item = i0; item < i1 && ok; item++) {
+        const int pl = (int)(item / chunks), chunk = (int)(item - (long long)pl * chunks);
+        if (pl != cur) {
+            // stage both perturbed weight sets of this pair (the previous pair's MMAs have all completed)
+            const int cand = a.cand_begin + pl;
+            const float* e = (a.mode == 0 && a.sigma != 0.0f) ? a.eps + (long long)pl * m.P : nullptr;
+            for (int k = tid; k < m.P; k += kTcRows) {
+                float wp, wm;
+                perturbed_weight(a, e, k, cand, wp, wm);
+                int oh, ol;
+                T::place(k, oh, ol);
+                if (ol < 0) { sw[oh] = wp; sw[T::SIGN + oh] = wm; continue; }
+                const float hp = tc::tf32_hi(wp), hm = tc::tf32_hi(wm);
+                sw[oh] = hp; sw[ol] = wp - hp;
+                sw[T::SIGN + oh] = hm; sw[T::SIGN + ol] = wm - hm;
+            }
+            tc::fence_proxy_async_smem();
+            cur = pl;
+        }
+        const int row0 = chunk * a.chunk;
+        const int row1 = min(a.M, row0 + a.chunk);
+        double acc_p = 0.0, acc_m = 0.0;
+
+        // prologue: first tile's features to TMEM, the next tile's prefetched, L1 of (first tile, +) issued
+        load_x(row0);
+        store_x();
+        load_x(row0 + kTcRows);
+        tc::wait_st();
+        tc::fence_before_sync();
+        stream_sync(bar_id);
+        if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb0 + T::oB1h * 4, sb0 + T::oB1l * 4, bar);
+
+#pragma unroll 1
+        for (int base = row0; base < row1; base += kTcRows) {
+            const int row = base + tid;
+            const bool valid = row < row1;
+            const bool more = base + kTcRows < row1;
+            float t[S::NOUT];
+            {
+                const int s = min(row, a.M - 1);
+#pragma unroll
+                for (int c = 0; c < S::NOUT; c++) t[c] = __ldg(a.tgt_t + (long long)c * a.mstride + s);
+            }
+#pragma unroll
+            for (int sg = 0; sg < 2; sg++) {
+                const uint32_t sb = sg ? sb1 : sb0;
+                const float* ws = sw + sg * T::SIGN;
+                float h[S::H1 > S::H2 ? S::H1 : S::H2];
+                // layer 1 result -> H
+                wait_mma();
+#pragma unroll
+                for (int q = 0; q < S::H1; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+                tc::wait_ld();
+#pragma unroll
+                for (int j = 0; j < S::H1; j++) h[j] = leak_unit ? fmaxf(h[j], h[j] * leak) : leaky_f(h[j], leak);
+                store_split<T::K2>(trow, T::cHh, T::cHl, h);
+                tc::wait_st();
+                tc::fence_before_sync();
+                ok = stream_sync_and(bar_id, ok);
+                if (!ok) break;
+                if (warp == 0) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+                // layer 2 result -> registers
+                wait_mma();
+#pragma unroll
+                for (int q = 0; q < S::H2; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+                tc::wait_ld();
+                // next unit's layer 1: the other sign of this tile, or the next tile's + sign
+                const bool next = sg == 0 || more;
+                if (sg == 1 && more) {
+                    store_x();
+                    load_x(base + 2 * kTcRows);
+                    tc::wait_st();
+                }
+                tc::fence_before_sync();
+                ok = stream_sync_and(bar_id, ok);
+                if (!ok) break;
+                if (next && warp == 0) {
+                    const uint32_t nb = sg ? sb0 : sb1;
+                    issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
+                }
+                // output layer and error of this unit, overlapping the tensor core's next layer 1
+                float (&h2)[S::H2] = *reinterpret_cast<float (*)[S::H2]>(h);
+                const double e = finish_row(ws, h2, t, valid);
+                if (sg == 0) acc_p += e; else acc_m += e;
+            }
+            if (!ok) break;
+        }
+        if (!ok) break;
+        const double sp = stream_sum(acc_p, red[g], bar_id);
+        const double sm = stream_sum(acc_m, red[g], bar_id);
+        if (tid == 0) {
+            double* dst = a.part + (long long)pl * 2 * chunks;
+            dst[chunk] = sp;
+            dst[chunks + chunk] = sm;
+        }
+    }
+    if (!ok) {
+        // A wait timed out: flag it, give the outstanding MMAs one more bounded wait, then free TMEM.
+        if (tid == 0) atomicExch(a.tc_err, 1);
+        tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, 128 * kTcStreams); }
+}
+
+template <class S>
+void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
+    using T = TcShape<S>;
+    const int chunks = pop_chunks(a.M, a.chunk);
+    const size_t smem = (size_t)kTcStreams * 2 * T::SIGN * sizeof(float);
+    static int nsm = 0;
+    if (nsm == 0) {
+        int dev = 0;
+        NTCB_CHECK(cudaGetDevice(&dev));
+        NTCB_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+        NTCB_CHECK(cudaFuncSetAttribute(k_pop_eval_tc<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    const long long items = (long long)a.ncand * chunks;
+    const int grid = (int)std::min<long long>(nsm, (items + kTcStreams - 1) / kTcStreams);
+    k_pop_eval_tc<S><<<grid, kTcTPB, smem, s>>>(m, a, chunks);
+}
+
+}  // namespace
+
+int pop_tc_rows() { return kTcRows; }
+
+bool launch_pop_eval_tc(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a) {
+    if (a.ncand <= 0) return true;
+    if (a.chunk % kTcRows != 0 || a.tc_err == nullptr) return false;
+    switch (shape) {
+#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: launch_tc<FixedShape<NIN, H1, H2, NOUT>>(s, m, a); break;
+        NTCB_FIXED_SHAPES(NTCB_CASE)
+#undef NTCB_CASE
+        default: return false;
+    }
+    NTCB_CHECK(cudaGetLastError());
+    return true;
+}
+
+}  // namespace ntcb

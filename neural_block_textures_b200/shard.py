@@ -7,6 +7,10 @@
 * Latent ES step — the image: rank r evaluates the K pairs' per-pixel loss differences for image rows
   [r H / G, (r + 1) H / G); one in-place all-gather per pair plane gives every rank the full [K][W H] array,
   from which each rank runs the identical footprint gathers, Adam and snap.
+* FD step — the weights: rank r evaluates the central differences of weights [r B, min((r + 1) B, P)) with
+  B = ceil(P / G) (every rank also evaluates the unperturbed stats pair); one all-gather of the padded
+  [G][B] fitness pairs leaves all P weights' (L+, L-) in weight order at the front, and every rank runs the
+  identical FD gradient and Adam.
 * Selector search — level-0 texel rows: rank r searches rows [r LH / G, (r + 1) LH / G) (texels are
   independent); one all-gather of the level installs every rank's result everywhere.
 
@@ -19,6 +23,15 @@ import contextlib
 
 def pair_range(N: int, world: int, rank: int) -> tuple[int, int]:
     return even_range(N, world, rank, "pairs")
+
+
+def padded_range(n: int, world: int, rank: int) -> tuple[int, int, int]:
+    """[begin, end) of rank's block of ceil(n / world) items (the last blocks may be short or empty), and the
+    block size. Blocks are gathered at a stride of the block size, so the n items come out in order at the front."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad rank / world size")
+    per = -(-n // world)
+    return min(rank * per, n), min((rank + 1) * per, n), per
 
 
 def even_range(n: int, world: int, rank: int, what: str = "items") -> tuple[int, int]:
@@ -36,9 +49,10 @@ class ShardedES:
     `trainer` is a neural_block_textures_b200.Trainer (or any object with the same methods); `dist` is
     torch.distributed with an initialised process group; `device` is where the exchange buffers live (the
     trainer's GPU, or "cpu" for a gloo group); `stream` (optional) is the CUDA stream the trainer launches on.
-    `image` = (W, H) and `level0` = (LW, LH, LC) enable the sharded latent step and selector search."""
+    `image` = (W, H) and `level0` = (LW, LH, LC) enable the sharded latent step and selector search; `P` (the
+    weight count) enables the sharded FD step."""
 
-    def __init__(self, trainer, dist, N: int, device="cuda", stream=None, K: int = 0, image=None, level0=None):
+    def __init__(self, trainer, dist, N: int, device="cuda", stream=None, K: int = 0, image=None, level0=None, P: int = 0):
         import torch
         self.t, self.dist, self.N = trainer, dist, N
         self.world, self.rank = dist.get_world_size(), dist.get_rank()
@@ -60,6 +74,13 @@ class ShardedES:
             self.row_floats = LW * LC
             self.l0 = torch.zeros(LW * LH * LC, dtype=torch.float32, device=device)
 
+        self.fd_local = None
+        if P > 0:
+            self.P = P
+            self.j0, self.j1, per = padded_range(P, self.world, self.rank)
+            self.fd_local = torch.zeros(2 * per, dtype=torch.float64, device=device)
+            self.fd_all = torch.zeros(2 * per * self.world, dtype=torch.float64, device=device)
+
     def _ctx(self):
         import torch
         return torch.cuda.stream(self.stream) if self.stream is not None else contextlib.nullcontext()
@@ -70,6 +91,14 @@ class ShardedES:
         with self._ctx():
             self.dist.all_gather_into_tensor(self.fit_all, self.fit_local)
         self.t.shard_mlp_apply(it, sigma, lr, self.N, M, self.fit_all)
+
+    def fd_step(self, it: int, h: float, lr: float, M: int) -> None:
+        """One FD step (mlp_step_fd)."""
+        assert self.fd_local is not None
+        self.t.shard_fd_eval(it, h, M, self.j0, self.j1, self.fd_local)
+        with self._ctx():
+            self.dist.all_gather_into_tensor(self.fd_all, self.fd_local)
+        self.t.shard_fd_apply(h, lr, self.fd_all)
 
     def lat_step(self, it: int, sigma: float, lr: float, K: int) -> None:
         """One latent ES step (lat_step)."""

@@ -178,6 +178,13 @@ class Trainer:
     def launch_count(self) -> int:
         return int(self.lib.ntcb_launch_count(self.h))
 
+    def set_pop_kernel(self, tensor: bool) -> None:
+        """True: ES pairs on the tensor-core (3xTF32) kernel; False: the bit-exact packed-FP32 kernel."""
+        self.lib.ntcb_set_pop_kernel(self.h, 1 if tensor else 0)
+
+    def pop_kernel(self) -> str:
+        return "tensor" if self.lib.ntcb_pop_kernel(self.h) else "ffma"
+
     def shard_mlp_eval(self, it: int, sigma: float, N: int, M: int, p0: int, p1: int, fit_dev) -> None:
         """fit_dev: a CUDA tensor (or device pointer) of 2 * (p1 - p0) doubles on this trainer's GPU."""
         ptr = fit_dev if isinstance(fit_dev, int) else fit_dev.data_ptr()
@@ -187,6 +194,14 @@ class Trainer:
         """fit_all_dev: a CUDA tensor (or device pointer) with all N pairs' (L+, L-) in pair order."""
         ptr = fit_all_dev if isinstance(fit_all_dev, int) else fit_all_dev.data_ptr()
         self.lib.ntcb_shard_mlp_apply(self.h, it, sigma, lr, N, M, C.c_void_p(ptr))
+
+    def shard_fd_eval(self, it: int, h: float, M: int, j_begin: int, j_end: int, fit_dev) -> None:
+        """fit_dev: device buffer of >= 2 * (j_end - j_begin) doubles; receives (L+, L-) of weights [j_begin, j_end)."""
+        self.lib.ntcb_shard_fd_eval(self.h, it, h, M, j_begin, j_end, C.c_void_p(_dptr(fit_dev)))
+
+    def shard_fd_apply(self, h: float, lr: float, fit_all_dev) -> None:
+        """fit_all_dev: device buffer whose first 2 * P doubles are every weight's (L+, L-) in weight order."""
+        self.lib.ntcb_shard_fd_apply(self.h, h, lr, C.c_void_p(_dptr(fit_all_dev)))
 
     def shard_lat_eval(self, sigma: float, K: int, row_begin: int, row_end: int, dpix_dev) -> None:
         """dpix_dev: a CUDA tensor [K, W * H] of float32; rows [row_begin, row_end) of every plane are written."""

@@ -1,4 +1,4 @@
-"""Population / image / texel-row sharding on 2 GPUs over NCCL (neural_block_textures_b200.shard.ShardedES, the code
+"""Population / weight (FD) / image / texel-row sharding on 2 GPUs over NCCL (neural_block_textures_b200.shard.ShardedES, the code
 bench.py runs with torchrun): two ranks must end with the same weights and latent as one GPU running the plain
 Trainer steps, bit for bit (every per-pair, per-pixel and per-texel value is computed by the same kernels
 whichever rank computes it, and the gradient sums keep their order). Needs >= 2 GPUs; skipped otherwise."""
@@ -48,11 +48,13 @@ def _rank_main(rank, world, port, out_dir):
         stream = torch.cuda.Stream()
         tr.set_stream(stream.cuda_stream)
         L0 = spec.levels[0]
-        es = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K, image=(spec.W, spec.H), level0=(L0.W, L0.H, L0.C))
+        es = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K, image=(spec.W, spec.H), level0=(L0.W, L0.H, L0.C),
+                       P=spec.P)
         for it in range(1, ITERS + 1):
             es.step(it, 0.02, 0.005, M)
             es.lat_step(it, 0.05, 0.02, K)
             es.qat_search()
+        es.fd_step(ITERS + 1, 1e-3, 0.005, M)
         zz, pp = tr.download_model()
         np.save(os.path.join(out_dir, f"z{rank}.npy"), zz)
         np.save(os.path.join(out_dir, f"p{rank}.npy"), pp)
@@ -85,6 +87,7 @@ def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device):
             tr.mlp_step(it, 0.02, 0.005, N, M)
             tr.lat_step(it, 0.05, 0.02, K)
             tr.qat_search()
+        tr.mlp_step_fd(ITERS + 1, 1e-3, 0.005, M)
         z1, p1 = tr.download_model()
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"p{r}.npy"), p1), f"rank {r} weights"

@@ -1,0 +1,86 @@
+"""The tensor-core ES population kernel (tcgen05, 3xTF32) against the oracle's loss_subset and against the
+bit-exact packed-FP32 kernel, on every fixed shape (nin 5 / 6 / 8, 3 and 12 outputs), including minibatch
+sizes that leave a ragged last 128-row tile and the sigma = 0 case where both signs must agree exactly.
+
+Bars: per-candidate fitness within 1e-5 relative of the oracle (the build's fitness tolerance) and within
+2e-6 relative of the exact kernel; the ES loss differences dl = L+ - L- within 1e-3 rms(dl) of the
+exact kernel's (the reference's --cuda-check bar for dl, main.cpp:3008-3030)."""
+import dataclasses
+
+import numpy as np
+import pytest
+
+from neural_block_textures_b200 import Trainer
+from oracle.oracle import Oracle
+
+from .helpers import rel_err, spec_named, target_for
+
+pytestmark = pytest.mark.gpu
+
+FIT_RTOL = 1e-5
+TC_VS_EXACT = 2e-6
+SIGMA = 0.02
+
+
+def _trainer(spec, tgt):
+    z, p = spec.init_params()
+    tr = Trainer()
+    ok, why = tr.init(spec.model_desc(), z, p, tgt)
+    assert ok, why
+    return tr, z, p
+
+
+def _fitness(tr, tensor, it, N, M, sigma=SIGMA):
+    tr.set_pop_kernel(tensor)
+    assert tr.pop_kernel() == ("tensor" if tensor else "ffma")
+    tr.mlp_step(it, sigma, 0.0, N, M)
+    lp, lm = tr.debug_last_fitness()
+    return lp.copy(), lm.copy(), tr.debug_last_batch().copy()
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg5"])
+@pytest.mark.parametrize("M", [1024, 300])
+def test_tensor_fitness_matches_oracle_and_exact(name, M, cuda_device):
+    spec = dataclasses.replace(spec_named(name), max_pairs=64)
+    tgt = target_for(spec)
+    tr, z, p = _trainer(spec, tgt)
+    N, it = 48, 7
+    lp_t, lm_t, b_t = _fitness(tr, True, it, N, M)
+    lp_e, lm_e, b_e = _fitness(tr, False, it, N, M)
+    assert np.array_equal(b_t, b_e)
+    # against the exact kernel
+    assert rel_err(lp_t, lp_e) < TC_VS_EXACT and rel_err(lm_t, lm_e) < TC_VS_EXACT
+    dl_t, dl_e = lp_t - lm_t, lp_e - lm_e
+    assert np.abs(dl_t - dl_e).max() < 1e-3 * np.sqrt(np.mean(dl_e ** 2))
+    # against the oracle (the reference's CPU loss_subset on the same batch and noise)
+    orc = Oracle(spec, tgt)
+    olp, olm = orc.es_fitness(p, z, spec.seed, it, SIGMA, 0, N, b_t)
+    assert rel_err(lp_t, olp) < FIT_RTOL and rel_err(lm_t, olm) < FIT_RTOL
+    tr.close()
+
+
+def test_tensor_sigma_zero_signs_agree(cuda_device):
+    spec = spec_named("cfg2")
+    tr, z, p = _trainer(spec, target_for(spec))
+    lp, lm, _ = _fitness(tr, True, 3, 16, 512, sigma=0.0)
+    assert np.array_equal(lp, lm)
+    assert np.all(lp == lp[0])
+    tr.close()
+
+
+def test_tensor_training_steps_track_exact(cuda_device):
+    """Ten ES steps with lr > 0 on each kernel: the weights stay within a small fraction of the Adam step."""
+    spec = dataclasses.replace(spec_named("cfg2"), max_pairs=64)
+    tgt = target_for(spec)
+    res = {}
+    for tensor in (True, False):
+        tr, z, p = _trainer(spec, tgt)
+        tr.set_pop_kernel(tensor)
+        for it in range(1, 11):
+            tr.mlp_step(it, SIGMA, 0.005, 64, 1024)
+        res[tensor] = tr.download_model()[1]
+        tr.close()
+    # Adam moves each weight by ~lr per step; near-zero gradient components may take the other sign
+    d = np.abs(res[True] - res[False])
+    assert np.median(d) < 1e-4 * 0.005
+    assert np.mean(d > 0.5 * 0.005) < 0.02

@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from neural_block_textures_b200.shard import ShardedES, pair_range
+from neural_block_textures_b200.shard import ShardedES, padded_range, pair_range
 
 from .helpers import spec_named, target_for
 
@@ -61,7 +61,7 @@ def _rank_main(rank, world, port, out_dir):
 
 class PlumbingTrainer:
     """Writes known values into its own rows / texel rows and records what the exchange delivered."""
-    W, H, LW, LH, LC, K = 12, 8, 6, 4, 2, 3
+    W, H, LW, LH, LC, K, P = 12, 8, 6, 4, 2, 3, 11
 
     def shard_lat_eval(self, sigma, K, r0, r1, dpix):
         for k in range(K):
@@ -79,24 +79,34 @@ class PlumbingTrainer:
     def shard_qat_apply(self, l0_all):
         self.l0 = l0_all.clone()
 
+    def shard_fd_eval(self, it, h, M, j0, j1, fit):
+        for j in range(j0, j1):
+            fit[2 * (j - j0)] = 10.0 * j + 1.0
+            fit[2 * (j - j0) + 1] = 10.0 * j + 2.0
+
+    def shard_fd_apply(self, h, lr, fit_all):
+        self.fd = fit_all[: 2 * self.P].clone()
+
 
 def _plumbing_main(rank, world, port, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         t = PlumbingTrainer()
-        es = ShardedES(t, dist, 4, device="cpu", K=t.K, image=(t.W, t.H), level0=(t.LW, t.LH, t.LC))
+        es = ShardedES(t, dist, 4, device="cpu", K=t.K, image=(t.W, t.H), level0=(t.LW, t.LH, t.LC), P=t.P)
         es.lat_step(1, 0.05, 0.0, t.K)
         es.qat_search()
+        es.fd_step(1, 1e-3, 0.0, 64)
+        np.save(os.path.join(out_dir, f"f{rank}.npy"), t.fd.numpy())
         np.save(os.path.join(out_dir, f"d{rank}.npy"), t.dpix.numpy())
         np.save(os.path.join(out_dir, f"l{rank}.npy"), t.l0.numpy())
     finally:
         dist.destroy_process_group()
 
 
-def test_latent_and_qat_row_sharding_plumbing(tmp_path):
-    """Two gloo ranks: each fills only its own image rows / level-0 texel rows; after the all-gathers every rank
-    holds the whole arrays in row order."""
+def test_latent_qat_fd_sharding_plumbing(tmp_path):
+    """Two gloo ranks: each fills only its own image rows / level-0 texel rows / FD weights (P = 11, uneven);
+    after the all-gathers every rank holds the whole arrays in order."""
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_plumbing_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
@@ -108,9 +118,16 @@ def test_latent_and_qat_row_sharding_plumbing(tmp_path):
     T = PlumbingTrainer
     want_d = np.array([[1000.0 * k + p for p in range(T.W * T.H)] for k in range(T.K)], np.float32)
     want_l = np.array([-1.0 - i for i in range(T.LW * T.LH * T.LC)], np.float32)
+    want_f = np.array([10.0 * j + 1.0 + s for j in range(T.P) for s in range(2)])
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"d{r}.npy"), want_d)
         assert np.array_equal(np.load(tmp_path / f"l{r}.npy"), want_l)
+        assert np.array_equal(np.load(tmp_path / f"f{r}.npy"), want_f)
+
+
+def test_padded_range():
+    assert [padded_range(11, 2, r) for r in range(2)] == [(0, 6, 6), (6, 11, 6)]
+    assert [padded_range(10, 8, r)[:2] for r in range(8)] == [(0, 2), (2, 4), (4, 6), (6, 8), (8, 10), (10, 10), (10, 10), (10, 10)]
 
 
 def test_pair_range():
