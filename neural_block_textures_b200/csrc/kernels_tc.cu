@@ -63,8 +63,9 @@ struct TcShape {
     static constexpr int oB1h = 0, oB1l = oB1h + N1 * K1;
     static constexpr int oB2h = oB1l + N1 * K1, oB2l = oB2h + N2 * K2;
     static constexpr int ob1 = oB2l + N2 * K2;                 // b1 [H2]
-    static constexpr int oW2 = round_up(ob1 + S::H2, 4);      // W2 transposed [H2][NOUTP]
-    static constexpr int ob2 = oW2 + S::H2 * NOUTP;           // b2 [NOUTP]
+    static constexpr int oW2 = round_up(ob1 + S::H2, 4);      // W2 [NOUT][H2], the reference's row-major order
+    static constexpr int ob2 = oW2 + S::NOUT * S::H2;         // b2 [NOUTP]
+    static_assert(S::H2 % 4 == 0, "output-layer rows are read as float4");
     static constexpr int SIGN = round_up(ob2 + NOUTP, 32);
     // TMEM columns
     static constexpr int cD = 0, cXh = 32, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
@@ -81,7 +82,7 @@ struct TcShape {
         k -= S::H2 * S::H1;
         if (k < S::H2) { off_hi = ob1 + k; off_lo = -1; return; }
         k -= S::H2;
-        if (k < S::NOUT * S::H2) { const int o = k / S::H2, j = k - o * S::H2; off_hi = oW2 + j * NOUTP + o; off_lo = -1; return; }
+        if (k < S::NOUT * S::H2) { off_hi = oW2 + k; off_lo = -1; return; }
         k -= S::NOUT * S::H2;
         off_hi = ob2 + k; off_lo = -1;
     }
@@ -93,9 +94,19 @@ __device__ __forceinline__ bool elect_one() {
     return p != 0;
 }
 
-__device__ __forceinline__ float leaky_f(float x, float leak) { return x > 0.0f ? x : x * leak; }
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
 __device__ __forceinline__ float out_act_fast(float s, int clamp_out) {
-    return clamp_out ? fminf(fmaxf(s, 0.0f), 1.0f) : __frcp_rn(1.0f + __expf(-s));
+    return clamp_out ? fminf(fmaxf(s, 0.0f), 1.0f) : rcp_approx(1.0f + __expf(-s));
+}
+// Leaky ReLU of a pair; for 0 <= leak <= 1, max(x, leak x) equals the select for every float.
+__device__ __forceinline__ float2 leaky_pair(float2 x, float leak, bool leak_unit) {
+    const float2 t = __fmul2_rn(x, make_float2(leak, leak));
+    if (leak_unit) return make_float2(fmaxf(x.x, t.x), fmaxf(x.y, t.y));
+    return make_float2(x.x > 0.0f ? x.x : t.x, x.y > 0.0f ? x.y : t.y);
 }
 
 // Split N (multiple of 8) values into hi / lo and store them to TMEM columns [ch, ch + N) / [cl, cl + N).
@@ -105,7 +116,12 @@ __device__ __forceinline__ void store_split(uint32_t trow, int ch, int cl, const
     for (int q = 0; q < N; q += 8) {
         float hi[8], lo[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) { hi[j] = tc::tf32_hi(v[q + j]); lo[j] = v[q + j] - hi[j]; }
+        for (int j = 0; j < 8; j += 2) {
+            const float2 x = make_float2(v[q + j], v[q + j + 1]);
+            const float2 h = make_float2(tc::tf32_hi(x.x), tc::tf32_hi(x.y));
+            const float2 l = __ffma2_rn(h, make_float2(-1.0f, -1.0f), x);   // x - hi, exact
+            hi[j] = h.x; hi[j + 1] = h.y; lo[j] = l.x; lo[j + 1] = l.y;
+        }
         tc::st_x8(trow + ch + q, hi);
         tc::st_x8(trow + cl + q, lo);
     }
@@ -197,33 +213,32 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
         for (int i = 0; i < T::K1; i++) x[i] = i < S::NIN ? xr[i] : (i == S::NIN ? 1.0f : 0.0f);
         store_split<T::K1>(trow, T::cXh, T::cXl, x);
     };
-    // Output layer + error of one row for one sign, from the layer-2 accumulator row h (b1 not yet added).
+    // Output layer + error of one row for one sign, from the layer-2 accumulator row h (b1 not yet added):
+    // hidden units in pairs (packed bias, activation and products), two partial sums per output.
     auto finish_row = [&](const float* ws, float (&h)[S::H2], const float (&t)[S::NOUT], bool valid) -> double {
-        float2 o[T::NOUTP / 2];
+        float2 acc[S::NOUT];
 #pragma unroll
-        for (int q = 0; q < T::NOUTP; q += 2) o[q / 2] = make_float2(ws[T::ob2 + q], ws[T::ob2 + q + 1]);
+        for (int c = 0; c < S::NOUT; c++) acc[c] = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int j = 0; j < S::H2; j++) {
-            const float s = h[j] + ws[T::ob1 + j];
-            const float hj = leak_unit ? fmaxf(s, s * leak) : leaky_f(s, leak);
-            const float2 hh = make_float2(hj, hj);
-#pragma unroll
-            for (int q = 0; q < T::NOUTP; q += 4) {
-                const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + j * T::NOUTP + q);
-                o[q / 2] = __ffma2_rn(make_float2(w.x, w.y), hh, o[q / 2]);
-                o[q / 2 + 1] = __ffma2_rn(make_float2(w.z, w.w), hh, o[q / 2 + 1]);
-            }
-        }
-        double e = 0.0;
-        if (valid) {
+        for (int j = 0; j < S::H2; j += 4) {
+            const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
+            const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak, leak_unit);
+            const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak, leak_unit);
 #pragma unroll
             for (int c = 0; c < S::NOUT; c++) {
-                const float ov = out_act_fast((c & 1) ? o[c / 2].y : o[c / 2].x, m.clamp_out);
-                const float d = ov - t[c];
-                e += (double)(m.cw[c] * (d * d));
+                const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + c * S::H2 + j);
+                acc[c] = __ffma2_rn(make_float2(w.x, w.y), h0, acc[c]);
+                acc[c] = __ffma2_rn(make_float2(w.z, w.w), h1, acc[c]);
             }
         }
-        return e;
+        float e = 0.0f;
+#pragma unroll
+        for (int c = 0; c < S::NOUT; c++) {
+            const float ov = out_act_fast(ws[T::ob2 + c] + (acc[c].x + acc[c].y), m.clamp_out);
+            const float d = ov - t[c];
+            e = fmaf(m.cw[c], d * d, e);
+        }
+        return valid ? (double)e : 0.0;
     };
 
     const long long items = (long long)a.ncand * chunks;
@@ -285,7 +300,10 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
                 for (int q = 0; q < S::H1; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
                 tc::wait_ld();
 #pragma unroll
-                for (int j = 0; j < S::H1; j++) h[j] = leak_unit ? fmaxf(h[j], h[j] * leak) : leaky_f(h[j], leak);
+                for (int j = 0; j < S::H1; j += 2) {
+                    const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak, leak_unit);
+                    h[j] = v.x; h[j + 1] = v.y;
+                }
                 store_split<T::K2>(trow, T::cHh, T::cHl, h);
                 tc::wait_st();
                 tc::fence_before_sync();
