@@ -134,16 +134,21 @@ void flush_timing(Impl& I) {
     I.pending.clear();
 }
 
+// After a stream synchronisation: a tensor-core CTA whose MMA completion wait timed out has flagged it (and
+// left its partial sums unwritten); that is a runtime failure like any CUDA error.
+void check_tc_err(const Impl& I) {
+    if (!I.tc_err) return;
+    int e = 0;
+    NTCB_CHECK(cudaMemcpy(&e, I.tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        fprintf(stderr, "ntc_b200: a tensor-core population CTA timed out waiting for its MMAs\n");
+        exit(1);
+    }
+}
+
 void sync(Impl& I) {
     NTCB_CHECK(cudaStreamSynchronize(I.stream));
-    if (I.tc_err) {
-        int e = 0;
-        NTCB_CHECK(cudaMemcpy(&e, I.tc_err, sizeof(int), cudaMemcpyDeviceToHost));
-        if (e) {
-            fprintf(stderr, "ntc_b200: a tensor-core population CTA timed out waiting for its MMAs\n");
-            exit(1);
-        }
-    }
+    check_tc_err(I);
 }
 void set_device(Impl& I) { if (I.device >= 0) NTCB_CHECK(cudaSetDevice(I.device)); }
 
@@ -746,6 +751,7 @@ size_t copy_out(const Impl& I, const T* dev, size_t count, T* out, size_t cap) {
     if (n && out) {
         NTCB_CHECK(cudaMemcpyAsync(out, dev, n * sizeof(T), cudaMemcpyDeviceToHost, I.stream));
         NTCB_CHECK(cudaStreamSynchronize(I.stream));
+        check_tc_err(I);
     }
     return count;
 }

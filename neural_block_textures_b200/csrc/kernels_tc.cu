@@ -6,7 +6,8 @@
 //
 //   D1 = X  W0^T      X  = [features | 1 | 0 pad]  (K1 = NIN + 1 rounded up to 8; b0 folded in as a column)
 //   D2 = H1 W1^T      H1 = leaky(D1)               (K2 = H1 width)
-//   o  = b2 + W2 leaky(D2 + b1)                    (packed FP32 in registers: N = NOUT is too narrow for MMAs)
+//   o  = b2 + W2 H2   H2 = leaky(D2 + b1)          3 outputs: packed FP32 in registers (a 16-wide MMA would be
+//                                                  mostly padding); 12 outputs: one more MMA layer into D3
 //
 // Row r of a tile is TMEM lane r, so thread t (warp w = t / 32) owns row t: it loads its accumulator row
 // from TMEM, applies bias / activation, and stores the next layer's A operand back to TMEM (A-from-TMEM
@@ -14,10 +15,11 @@
 // Warp 0 issues the MMAs converged, one elected lane per instruction, with compile-time TMEM / shared
 // addresses (a divergent single-thread issue loop costs ~4x more per MMA), and commits them to an mbarrier.
 //
-// Schedule per CTA (u = tile x sign): L1(u) issued -> wait, load, activation, store H -> L2(u) issued ->
-// wait, load D2 -> L1(u + 1) issued (next tile's features were prefetched one tile ahead) -> the output
-// layer and error of u run on the CUDA cores while the tensor core works on L1(u + 1). Four CTAs per SM
-// (128 TMEM columns each) overlap one another's waits.
+// Schedule per stream (u = tile x sign): L1(u) issued -> wait, load, activation, store H -> L2(u) issued ->
+// wait, load D2 -> L1(u + 1) issued (the next tile's features were prefetched one tile ahead), together with
+// the output-layer MMAs of u when those run on the tensor core -> the output layer / error of u finish on the
+// CUDA cores while the tensor core works on L1(u + 1). A kernel that allocates TMEM is held to one resident
+// CTA per SM, so the overlap comes from four independent 128-thread streams inside each CTA (below).
 //
 // Precision: every tensor product is formed as 3xTF32, a b = a_hi b_hi + a_hi b_lo + a_lo b_hi with x_hi the
 // top 19 bits of x and x_lo = x - x_hi (exact), accumulated in FP32 by the tensor core. The dropped a_lo b_lo
@@ -56,9 +58,11 @@ struct TcShape {
     static constexpr int N1 = round_up(S::H1, 16);
     static constexpr int K2 = S::H1;
     static constexpr int N2 = round_up(S::H2, 16);
+    static constexpr int K3 = S::H2;
+    static constexpr int N3 = round_up(S::NOUT, 16);
     static constexpr int NOUTP = round_up(S::NOUT, 4);
     static_assert(S::H1 % 8 == 0 && S::H2 % 8 == 0, "hidden widths must be multiples of 8");
-    static_assert(N1 <= 32 && N2 <= 32, "accumulator wider than the 32 reserved TMEM columns");
+    static_assert(N1 <= 32 && N2 <= 32 && N3 <= 16, "accumulators wider than their reserved TMEM columns");
     // shared memory, floats, per sign
     static constexpr int oB1h = 0, oB1l = oB1h + N1 * K1;
     static constexpr int oB2h = oB1l + N1 * K1, oB2l = oB2h + N2 * K2;
@@ -66,25 +70,32 @@ struct TcShape {
     static constexpr int oW2 = round_up(ob1 + S::H2, 4);      // W2 [NOUT][H2], the reference's row-major order
     static constexpr int ob2 = oW2 + S::NOUT * S::H2;         // b2 [NOUTP]
     static_assert(S::H2 % 4 == 0, "output-layer rows are read as float4");
-    static constexpr int SIGN = round_up(ob2 + NOUTP, 32);
-    // TMEM columns
-    static constexpr int cD = 0, cXh = 32, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
+    static constexpr int oB3h = round_up(ob2 + NOUTP, 4), oB3l = oB3h + N3 * K3;   // W2 as an MMA B operand
+    static constexpr int SIGN = round_up(oB3l + N3 * K3, 32);
+    // TMEM columns: D (layers 1 and 2), D3 (output layer), X hi / lo, H hi / lo
+    static constexpr int cD = 0, cD3 = 32, cXh = 48, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
     static constexpr int NCOLS = 128;
     static_assert(cHl + K2 <= NCOLS, "TMEM columns");
 
-    // Where flat reference weight k goes: an MMA B-operand element (split into hi / lo) or a plain slot.
-    __device__ static void place(int k, int& off_hi, int& off_lo) {
-        if (k < S::H1 * S::NIN) { const int j = k / S::NIN, i = k - j * S::NIN; off_hi = oB1h + kmajor(j, i, K1); off_lo = oB1l + kmajor(j, i, K1); return; }
+    // Writes flat reference weight k (value w) to every place a kernel variant reads it from: MMA B operands
+    // as hi / lo, biases and the row-major output layer as plain floats.
+    __device__ static void store(float* sw, int k, float w) {
+        const float hi = tc::tf32_hi(w), lo = w - hi;
+        if (k < S::H1 * S::NIN) { const int j = k / S::NIN, i = k - j * S::NIN; sw[oB1h + kmajor(j, i, K1)] = hi; sw[oB1l + kmajor(j, i, K1)] = lo; return; }
         k -= S::H1 * S::NIN;
-        if (k < S::H1) { off_hi = oB1h + kmajor(k, S::NIN, K1); off_lo = oB1l + kmajor(k, S::NIN, K1); return; }
+        if (k < S::H1) { sw[oB1h + kmajor(k, S::NIN, K1)] = hi; sw[oB1l + kmajor(k, S::NIN, K1)] = lo; return; }
         k -= S::H1;
-        if (k < S::H2 * S::H1) { const int j = k / S::H1, i = k - j * S::H1; off_hi = oB2h + kmajor(j, i, K2); off_lo = oB2l + kmajor(j, i, K2); return; }
+        if (k < S::H2 * S::H1) { const int j = k / S::H1, i = k - j * S::H1; sw[oB2h + kmajor(j, i, K2)] = hi; sw[oB2l + kmajor(j, i, K2)] = lo; return; }
         k -= S::H2 * S::H1;
-        if (k < S::H2) { off_hi = ob1 + k; off_lo = -1; return; }
+        if (k < S::H2) { sw[ob1 + k] = w; return; }
         k -= S::H2;
-        if (k < S::NOUT * S::H2) { off_hi = oW2 + k; off_lo = -1; return; }
+        if (k < S::NOUT * S::H2) {
+            const int o = k / S::H2, j = k - o * S::H2;
+            sw[oW2 + k] = w; sw[oB3h + kmajor(o, j, K3)] = hi; sw[oB3l + kmajor(o, j, K3)] = lo;
+            return;
+        }
         k -= S::NOUT * S::H2;
-        off_hi = ob2 + k; off_lo = -1;
+        sw[ob2 + k] = w;
     }
 };
 
@@ -168,20 +179,25 @@ __device__ __forceinline__ double stream_sum(double v, double* red4, int id) {
 // weight sets, and works through a contiguous range of the (pair, chunk) items, so consecutive items
 // mostly share a pair and its weights are staged once. The streams interleave on the SM: one stream's
 // element-wise work overlaps the others' MMAs.
-template <class S>
+template <class S, bool L3TC>
 __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a, int chunks) {
     using T = TcShape<S>;
     extern __shared__ __align__(1024) float dyn[];   // [kTcStreams][2][T::SIGN]
     __shared__ __align__(8) uint64_t bars[kTcStreams];
+    __shared__ __align__(8) uint64_t bars3[kTcStreams];   // output-layer commits (separate: see below)
     __shared__ uint32_t tbase;
     __shared__ double red[kTcStreams][4];
     const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
     const int bar_id = 1 + g;
     float* sw = dyn + g * 2 * T::SIGN;
     uint64_t* bar = &bars[g];
+    // The output-layer MMAs and the next unit's layer 1 are committed back to back. On one mbarrier both
+    // phases could complete before a thread polls, leaving the barrier at the parity it waits for (it would
+    // then wait for a phase nobody completes); with their own barrier, commits and waits alternate on each.
+    uint64_t* bar3 = &bars3[g];
 
     if (threadIdx.x < 32) tc::tmem_alloc(&tbase, 128 * kTcStreams);
-    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
+    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init(bar3, 1); tc::mbar_init_fence(); }
     for (int i = threadIdx.x; i < kTcStreams * 2 * T::SIGN; i += kTcTPB) dyn[i] = 0.0f;   // padding stays zero
     tc::fence_before_sync();
     __syncthreads();
@@ -192,12 +208,18 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
     const uint32_t sb0 = tc::smem_addr(sw), sb1 = sb0 + (uint32_t)(T::SIGN * 4);
     const float leak = m.leak;
     const bool leak_unit = leak >= 0.0f && leak <= 1.0f;
-    uint32_t waited = 0;   // commits whose completion this thread has observed (parity of the next wait)
+    uint32_t waited = 0, waited3 = 0;   // completed phases this thread has observed on bar / bar3
     bool ok = true;
 
     auto wait_mma = [&]() {
         const bool done = tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
         if (done) waited++;
+        ok = ok && done;
+        tc::fence_after_sync();
+    };
+    auto wait_mma3 = [&]() {
+        const bool done = tc::mbar_wait_bounded(bar3, waited3 & 1u, kTcWaitPolls);
+        if (done) waited3++;
         ok = ok && done;
         tc::fence_after_sync();
     };
@@ -255,12 +277,8 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
             for (int k = tid; k < m.P; k += kTcRows) {
                 float wp, wm;
                 perturbed_weight(a, e, k, cand, wp, wm);
-                int oh, ol;
-                T::place(k, oh, ol);
-                if (ol < 0) { sw[oh] = wp; sw[T::SIGN + oh] = wm; continue; }
-                const float hp = tc::tf32_hi(wp), hm = tc::tf32_hi(wm);
-                sw[oh] = hp; sw[ol] = wp - hp;
-                sw[T::SIGN + oh] = hm; sw[T::SIGN + ol] = wm - hm;
+                T::store(sw, k, wp);
+                T::store(sw + T::SIGN, k, wm);
             }
             tc::fence_proxy_async_smem();
             cur = pl;
@@ -317,22 +335,59 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
                 tc::wait_ld();
                 // next unit's layer 1: the other sign of this tile, or the next tile's + sign
                 const bool next = sg == 0 || more;
-                if (sg == 1 && more) {
-                    store_x();
-                    load_x(base + 2 * kTcRows);
+                if constexpr (L3TC) {
+                    // H2 = leaky(D2 + b1) -> TMEM; output-layer MMAs (into D3) and the next unit's layer 1
+                    // (into D) go out together as two commits
+#pragma unroll
+                    for (int j = 0; j < S::H2; j += 4) {
+                        const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
+                        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak, leak_unit);
+                        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak, leak_unit);
+                        h[j] = h0.x; h[j + 1] = h0.y; h[j + 2] = h1.x; h[j + 3] = h1.y;
+                    }
+                    store_split<T::K3>(trow, T::cHh, T::cHl, h);
+                    if (sg == 1 && more) { store_x(); load_x(base + 2 * kTcRows); }
                     tc::wait_st();
+                    tc::fence_before_sync();
+                    ok = stream_sync_and(bar_id, ok);
+                    if (!ok) break;
+                    if (warp == 0) {
+                        issue3<T::K3, T::N3>(tb + T::cD3, tb + T::cHh, tb + T::cHl, sb + T::oB3h * 4, sb + T::oB3l * 4, bar3);
+                        if (next) {
+                            const uint32_t nb = sg ? sb0 : sb1;
+                            issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
+                        }
+                    }
+                    wait_mma3();
+                    float o[T::NOUTP];
+#pragma unroll
+                    for (int q = 0; q < T::NOUTP; q += 4) tc::ld_x4p(trow + T::cD3 + q, o + q);
+                    tc::wait_ld();
+                    float e = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < S::NOUT; c++) {
+                        const float d = out_act_fast(o[c] + ws[T::ob2 + c], m.clamp_out) - t[c];
+                        e = fmaf(m.cw[c], d * d, e);
+                    }
+                    if (valid) { if (sg == 0) acc_p += (double)e; else acc_m += (double)e; }
+                } else {
+                    if (sg == 1 && more) {
+                        store_x();
+                        load_x(base + 2 * kTcRows);
+                        tc::wait_st();
+                    }
+                    tc::fence_before_sync();
+                    ok = stream_sync_and(bar_id, ok);
+                    if (!ok) break;
+                    if (next && warp == 0) {
+                        const uint32_t nb = sg ? sb0 : sb1;
+                        issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
+                    }
+                    // output layer and error of this unit, overlapping the tensor core's next layer 1
+                    float (&h2)[S::H2] = *reinterpret_cast<float (*)[S::H2]>(h);
+                    const double e = finish_row(ws, h2, t, valid);
+                    if (sg == 0) acc_p += e; else acc_m += e;
                 }
-                tc::fence_before_sync();
-                ok = stream_sync_and(bar_id, ok);
-                if (!ok) break;
-                if (next && warp == 0) {
-                    const uint32_t nb = sg ? sb0 : sb1;
-                    issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
-                }
-                // output layer and error of this unit, overlapping the tensor core's next layer 1
-                float (&h2)[S::H2] = *reinterpret_cast<float (*)[S::H2]>(h);
-                const double e = finish_row(ws, h2, t, valid);
-                if (sg == 0) acc_p += e; else acc_m += e;
             }
             if (!ok) break;
         }
@@ -349,6 +404,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
         // A wait timed out: flag it, give the outstanding MMAs one more bounded wait, then free TMEM.
         if (tid == 0) atomicExch(a.tc_err, 1);
         tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+        if (L3TC) tc::mbar_wait_bounded(bar3, waited3 & 1u, kTcWaitPolls);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -361,15 +417,18 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
     const int chunks = pop_chunks(a.M, a.chunk);
     const size_t smem = (size_t)kTcStreams * 2 * T::SIGN * sizeof(float);
     static int nsm = 0;
+    // The output layer runs on the tensor core for wide outputs (12: measured 1.33 vs 1.52 ms at config 3)
+    // and on the FP32 pipe for 3 outputs (0.86 vs 1.03 ms at config 2), where 16-wide MMAs are mostly padding.
+    constexpr bool kL3TC = S::NOUT > 4;
     if (nsm == 0) {
         int dev = 0;
         NTCB_CHECK(cudaGetDevice(&dev));
         NTCB_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-        NTCB_CHECK(cudaFuncSetAttribute(k_pop_eval_tc<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        NTCB_CHECK(cudaFuncSetAttribute(k_pop_eval_tc<S, kL3TC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     }
     const long long items = (long long)a.ncand * chunks;
     const int grid = (int)std::min<long long>(nsm, (items + kTcStreams - 1) / kTcStreams);
-    k_pop_eval_tc<S><<<grid, kTcTPB, smem, s>>>(m, a, chunks);
+    k_pop_eval_tc<S, kL3TC><<<grid, kTcTPB, smem, s>>>(m, a, chunks);
 }
 
 }  // namespace
