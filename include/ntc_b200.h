@@ -163,12 +163,12 @@ int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi);
 double ntcb_fp32_peak_tflops(void);
 /* Number of kernels this trainer has launched since creation. */
 long long ntcb_launch_count(const ntcb_trainer* t);
-/* Which kernel evaluates ES pairs (mlp_step, ntcb_shard_mlp_eval). tensor = 1 (the default): tcgen05 MMAs with
- * 3xTF32 products, FP32-level accuracy (fitness within ~1e-6 relative of the exact kernel); tensor = 0: the
- * packed-FP32 kernel, bit-identical per unit to the reference CUDA backend (cuda/ntc_cuda.cu:164-194). The FD
- * step always uses the exact kernel, and runtime-shaped models (no fixed-shape kernel) always do too. The
- * environment variable NTCB_POP_KERNEL=ffma selects 0 at init for callers of the C++ Trainer.
- * No counterpart in the reference. */
+/* Which kernels evaluate the ES decodes (mlp_step / ntcb_shard_mlp_eval pairs and the lat_step pass). tensor = 1
+ * (the default): tcgen05 MMAs with 3xTF32 products, FP32-level accuracy (fitness within ~1e-6 relative of the
+ * exact kernels); tensor = 0: the packed-FP32 kernels, bit-identical per unit to the reference CUDA backend
+ * (cuda/ntc_cuda.cu:164-194). The FD step and the selector search always use the exact kernels, and
+ * runtime-shaped models (no fixed-shape kernel) always do too. The environment variable NTCB_POP_KERNEL=ffma
+ * selects 0 at init for callers of the C++ Trainer. No counterpart in the reference. */
 void ntcb_set_pop_kernel(ntcb_trainer* t, int tensor);
 /* 1 when ES pairs currently run on the tensor-core kernel, else 0. */
 int ntcb_pop_kernel(const ntcb_trainer* t);

@@ -73,8 +73,9 @@ struct Trainer::Impl {
     double* part = nullptr; long long part_cap = 0;
     double *fit = nullptr, *dl = nullptr, *lsum = nullptr, *hh = nullptr;
     double* fit_stats = nullptr;
-    // ES pair evaluation: true (default) = the tensor-core kernel (3xTF32) where the shape has one; false = the
-    // packed-FP32 kernel, bit-identical per unit to the reference backend. FD always uses the latter.
+    // ES evaluations (MLP pairs and the latent pass): true (default) = the tensor-core kernels (3xTF32) where the
+    // shape has them; false = the packed-FP32 kernels, bit-identical per unit to the reference backend. FD always
+    // uses the latter.
     bool tensor_pop = true;
     int* tc_err = nullptr;   // device flag the tensor-core kernel sets when an MMA completion wait times out
     float* gpart = nullptr; long long gpart_cap = 0;
@@ -585,7 +586,9 @@ void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_e
     timed(I, "lat_noise", nact, [&] { ntcb::launch_lat_noise(I.stream, I.d.seed, step, K, I.dm, mask, I.nz, I.lat_eps); });
     const float inv_px = 1.0f / (3.0f * I.d.wsum * (float)I.d.W * (float)I.d.H);
     timed(I, "lat_eval", 1, [&] {
-        ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, dpix, p_begin, p_end);
+        if (!(I.tensor_pop && ntcb::launch_lat_eval_tc(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma,
+                                                       inv_px, dpix, p_begin, p_end, I.tc_err)))
+            ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, dpix, p_begin, p_end);
     });
 }
 

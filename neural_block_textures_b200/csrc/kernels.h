@@ -45,6 +45,11 @@ void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs
 // chunk size (a multiple of pop_tc_rows()) does not fit it, in which case nothing was launched.
 bool launch_pop_eval_tc(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a);
 int pop_tc_rows();
+// Tensor-core latent ES pass (same contract as launch_lat_eval) for the fixed shapes; false when the shape has
+// no tensor kernel (nothing launched). err: device flag set when an MMA completion wait timed out.
+bool launch_lat_eval_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
+                        long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
+                        long long p_begin, long long p_end, int* err);
 // Sum the chunk partials of every candidate in order, normalise, and write (lp, lm) pairs to fit[2*i], fit[2*i+1].
 void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit);
 // ES: dl, lsum from the fitness of all N pairs; FD: dl, hh.

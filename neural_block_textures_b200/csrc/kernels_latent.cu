@@ -2,6 +2,7 @@
 // gradient, and the exhaustive per-texel selector search of --qat.
 #include "kernels.h"
 #include "mlp_tile.cuh"
+#include "latent_features.cuh"
 #include "noise.cuh"
 
 namespace ntcb {
@@ -31,82 +32,6 @@ void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevM
         k_lat_noise<<<grid, 256, 0, s>>>(seed, step, K, lo, lo + n, nz, eps);
         NTCB_CHECK(cudaGetLastError());
     }
-}
-
-// Features of one pixel with the active levels perturbed by sign * sg * eps (pair k). The reference
-// perturbs the latent texel by texel, zp = zb + sg eps (fma), and samples the perturbed latent
-// (LatentTrainer::step, main.cpp:1997-2007); the same is done here per tap.
-__device__ __forceinline__ void perturbed_features(const DevModel& m, const float* __restrict__ z, const float* __restrict__ ek,
-                                                   unsigned active, float sgn_sg, int px, int py, float* f) {
-    const float u = pix_u(m, px), v = pix_v(m, py);
-    Tap t1 = {0, 0, 0, 0, 0.0f, 0.0f};
-    int slot = 0;
-    for (int l = 0; l < m.nlev; l++) {
-        const DevLevel& L = m.lv[l];
-        const Tap t = level_tap(L, u, v);
-        if (l == 1) t1 = t;
-        const float* zl = z + L.off;
-        if (!(active & (1u << l))) {
-            sample_level(L, zl, t, f + slot);
-        } else {
-            const float* el = ek + L.off;
-            const long long ia = ((long long)t.y0 * L.W + t.x0) * L.C;
-            if (L.nearest) {
-                for (int c = 0; c < L.C; c++) f[slot + c] = fmaf(sgn_sg, el[ia + c], zl[ia + c]);
-            } else {
-                const long long ib = ((long long)t.y0 * L.W + t.x1) * L.C;
-                const long long ic = ((long long)t.y1 * L.W + t.x0) * L.C;
-                const long long id = ((long long)t.y1 * L.W + t.x1) * L.C;
-                const TapW w = tap_weights(t);
-                for (int c = 0; c < L.C; c++)
-                    f[slot + c] = blend4(w, fmaf(sgn_sg, el[ia + c], zl[ia + c]), fmaf(sgn_sg, el[ib + c], zl[ib + c]),
-                                         fmaf(sgn_sg, el[ic + c], zl[ic + c]), fmaf(sgn_sg, el[id + c], zl[id + c]));
-            }
-        }
-        slot += L.C;
-    }
-    pos_encode(m, u, v, t1, f + slot);
-}
-
-// The + and - features of one pixel for pair k in one pass (taps, latent and noise loads shared).
-__device__ __forceinline__ void perturbed_features_pm(const DevModel& m, const float* __restrict__ z, const float* __restrict__ ek,
-                                                      unsigned active, float sg, int px, int py, float* fp, float* fm) {
-    const float u = pix_u(m, px), v = pix_v(m, py);
-    Tap t1 = {0, 0, 0, 0, 0.0f, 0.0f};
-    int slot = 0;
-    for (int l = 0; l < m.nlev; l++) {
-        const DevLevel& L = m.lv[l];
-        const Tap t = level_tap(L, u, v);
-        if (l == 1) t1 = t;
-        const float* zl = z + L.off;
-        if (!(active & (1u << l))) {
-            sample_level(L, zl, t, fp + slot);
-            for (int c = 0; c < L.C; c++) fm[slot + c] = fp[slot + c];
-        } else {
-            const float* el = ek + L.off;
-            const long long ia = ((long long)t.y0 * L.W + t.x0) * L.C;
-            if (L.nearest) {
-                for (int c = 0; c < L.C; c++) {
-                    const float e = el[ia + c], zz = zl[ia + c];
-                    fp[slot + c] = fmaf(sg, e, zz); fm[slot + c] = fmaf(-sg, e, zz);
-                }
-            } else {
-                const long long ib = ((long long)t.y0 * L.W + t.x1) * L.C;
-                const long long ic = ((long long)t.y1 * L.W + t.x0) * L.C;
-                const long long id = ((long long)t.y1 * L.W + t.x1) * L.C;
-                const TapW w = tap_weights(t);
-                for (int c = 0; c < L.C; c++) {
-                    const float ea = el[ia + c], eb = el[ib + c], ec = el[ic + c], ed = el[id + c];
-                    const float za = zl[ia + c], zb = zl[ib + c], zc = zl[ic + c], zd = zl[id + c];
-                    fp[slot + c] = blend4(w, fmaf(sg, ea, za), fmaf(sg, eb, zb), fmaf(sg, ec, zc), fmaf(sg, ed, zd));
-                    fm[slot + c] = blend4(w, fmaf(-sg, ea, za), fmaf(-sg, eb, zb), fmaf(-sg, ec, zc), fmaf(-sg, ed, zd));
-                }
-            }
-        }
-        slot += L.C;
-    }
-    pos_encode(m, u, v, t1, fp + slot);
-    for (int q = slot; q < m.nin; q++) fm[q] = fp[q];
 }
 
 // One thread per (pixel, group of kLatPairs pairs): the 2 x kLatPairs perturbed decodes of the pixel run
@@ -250,6 +175,9 @@ __device__ __forceinline__ int qat_index(float v, int bits) {
 // value's cell loss (double, pixels in raster order) is computed — kQatRows candidates per forward tile —
 // then the reference's rule picks the winner: the current value first, any other value only if strictly
 // lower. The winner is written in place before the next channel is searched.
+// The rule is applied as the losses stream in: the first strict minimum over the other grid values (index
+// order), which wins only if it is below the current value's loss — the same choice as the reference's scan
+// (best = loss[current]; for k != current in order: if loss[k] < best take it), with no per-value array.
 template <class S, int TPB>
 __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __restrict__ wg, float* __restrict__ z,
                                                    const float* __restrict__ tgt, const int* __restrict__ xr,
@@ -265,10 +193,12 @@ __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __re
     const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
     if (x0 >= x1 || y0 >= y1) return;
     float* zt = z + L.off + t * L.C;
-    double loss[256];
     for (int c = 0; c < L.C; c++) {
         const int bits = bits_c[c], n = 1 << bits;
         const float* gv = grid + bits * 257;
+        const int cur = qat_index(zt[c], bits);
+        double cur_loss = 0.0, other = 0.0;
+        int other_k = -1;
         for (int kg = 0; kg < n; kg += R) {
             double acc[R];
 #pragma unroll
@@ -297,15 +227,14 @@ __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __re
                         }
                 }
 #pragma unroll
-            for (int r = 0; r < R; r++) if (kg + r < n) loss[kg + r] = acc[r];
+            for (int r = 0; r < R; r++) {
+                const int k = kg + r;
+                if (k >= n) continue;
+                if (k == cur) cur_loss = acc[r];
+                else if (other_k < 0 || acc[r] < other) { other = acc[r]; other_k = k; }
+            }
         }
-        int best_k = qat_index(zt[c], bits);
-        double best = loss[best_k];
-        for (int k = 0; k < n; k++) {
-            if (k == best_k) continue;
-            if (loss[k] < best) { best = loss[k]; best_k = k; }
-        }
-        zt[c] = gv[best_k];
+        zt[c] = gv[(other_k >= 0 && other < cur_loss) ? other_k : cur];
     }
 }
 

@@ -34,6 +34,7 @@
 #include "mlp_tile.cuh"
 #include "pop_common.cuh"
 #include "tc.cuh"
+#include "latent_features.cuh"
 
 #include <algorithm>
 
@@ -138,6 +139,37 @@ __device__ __forceinline__ void store_split(uint32_t trow, int ch, int cl, const
     }
 }
 
+// Output layer + weighted squared error of one row on the FP32 pipe, from the layer-2 accumulator row h
+// (b1 not yet added): hidden units in pairs (packed bias, activation and products), two partial sums per
+// output, float error sum over the channels.
+template <class S>
+__device__ __forceinline__ float out_layer_error(const DevModel& m, const float* ws, const float* h, const float* t,
+                                                 float leak, bool leak_unit) {
+    using T = TcShape<S>;
+    float2 acc[S::NOUT];
+#pragma unroll
+    for (int c = 0; c < S::NOUT; c++) acc[c] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int j = 0; j < S::H2; j += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
+        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak, leak_unit);
+        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak, leak_unit);
+#pragma unroll
+        for (int c = 0; c < S::NOUT; c++) {
+            const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + c * S::H2 + j);
+            acc[c] = __ffma2_rn(make_float2(w.x, w.y), h0, acc[c]);
+            acc[c] = __ffma2_rn(make_float2(w.z, w.w), h1, acc[c]);
+        }
+    }
+    float e = 0.0f;
+#pragma unroll
+    for (int c = 0; c < S::NOUT; c++) {
+        const float d = out_act_fast(ws[T::ob2 + c] + (acc[c].x + acc[c].y), m.clamp_out) - t[c];
+        e = fmaf(m.cw[c], d * d, e);
+    }
+    return e;
+}
+
 // Warp 0 (converged): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K step), then commit.
 template <int K, int N>
 __device__ __forceinline__ void issue3(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo, uint64_t* bar) {
@@ -235,34 +267,6 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
         for (int i = 0; i < T::K1; i++) x[i] = i < S::NIN ? xr[i] : (i == S::NIN ? 1.0f : 0.0f);
         store_split<T::K1>(trow, T::cXh, T::cXl, x);
     };
-    // Output layer + error of one row for one sign, from the layer-2 accumulator row h (b1 not yet added):
-    // hidden units in pairs (packed bias, activation and products), two partial sums per output.
-    auto finish_row = [&](const float* ws, float (&h)[S::H2], const float (&t)[S::NOUT], bool valid) -> double {
-        float2 acc[S::NOUT];
-#pragma unroll
-        for (int c = 0; c < S::NOUT; c++) acc[c] = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int j = 0; j < S::H2; j += 4) {
-            const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
-            const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak, leak_unit);
-            const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak, leak_unit);
-#pragma unroll
-            for (int c = 0; c < S::NOUT; c++) {
-                const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + c * S::H2 + j);
-                acc[c] = __ffma2_rn(make_float2(w.x, w.y), h0, acc[c]);
-                acc[c] = __ffma2_rn(make_float2(w.z, w.w), h1, acc[c]);
-            }
-        }
-        float e = 0.0f;
-#pragma unroll
-        for (int c = 0; c < S::NOUT; c++) {
-            const float ov = out_act_fast(ws[T::ob2 + c] + (acc[c].x + acc[c].y), m.clamp_out);
-            const float d = ov - t[c];
-            e = fmaf(m.cw[c], d * d, e);
-        }
-        return valid ? (double)e : 0.0;
-    };
-
     const long long items = (long long)a.ncand * chunks;
     const long long nstreams = (long long)gridDim.x * kTcStreams, gs = (long long)blockIdx.x * kTcStreams + g;
     const long long i0 = gs * items / nstreams, i1 = (gs + 1) * items / nstreams;
@@ -384,8 +388,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
                         issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
                     }
                     // output layer and error of this unit, overlapping the tensor core's next layer 1
-                    float (&h2)[S::H2] = *reinterpret_cast<float (*)[S::H2]>(h);
-                    const double e = finish_row(ws, h2, t, valid);
+                    const double e = valid ? (double)out_layer_error<S>(m, ws, h, t, leak, leak_unit) : 0.0;
                     if (sg == 0) acc_p += e; else acc_m += e;
                 }
             }
@@ -431,6 +434,175 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
     k_pop_eval_tc<S, kL3TC><<<grid, kTcTPB, smem, s>>>(m, a, chunks);
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// Latent ES pass on the tensor core: every pixel of [p_begin, p_end) decoded with the active latent levels
+// perturbed by +sigma eps_k and by -sigma eps_k for each of the K pairs, dpix[k][p] = (e+ - e-) inv_px with
+// e the weighted squared error summed in float (decode_err, main.cpp:1722-1735; LatentTrainer::step,
+// main.cpp:1990-2015). The reference launches one kernel per pair (k_lat_pair, cuda/ntc_cuda.cu:358-409).
+//
+// Same machinery as the population kernel with one weight set shared by all rows: an item is (pair k,
+// 128-pixel tile), its two units are the + and - decodes of the tile (X = the +/- perturbed features, which
+// share their taps and are gathered together, one item ahead, while the layer-2 MMAs of the current item
+// run). The output layer runs on the FP32 pipe.
+template <class S>
+__global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
+                                                         const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
+                                                         int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
+                                                         long long p_begin, long long p_end, int* __restrict__ err) {
+    using T = TcShape<S>;
+    extern __shared__ __align__(1024) float sw[];   // one weight set [T::SIGN]
+    __shared__ __align__(8) uint64_t bars[kTcStreams];
+    __shared__ uint32_t tbase;
+    const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
+    const int bar_id = 1 + g;
+    uint64_t* bar = &bars[g];
+
+    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, 128 * kTcStreams);
+    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
+    for (int i = threadIdx.x; i < T::SIGN; i += kTcTPB) sw[i] = 0.0f;
+    __syncthreads();
+    for (int k = threadIdx.x; k < m.P; k += kTcTPB) T::store(sw, k, wg[k]);
+    tc::fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+
+    const uint32_t tb = tbase + 128u * (uint32_t)g;
+    const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+    const uint32_t sb = tc::smem_addr(sw);
+    const float leak = m.leak;
+    const bool leak_unit = leak >= 0.0f && leak <= 1.0f;
+    uint32_t waited = 0;
+    bool ok = true;
+    auto wait_mma = [&]() {
+        const bool done = tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+        if (done) waited++;
+        ok = ok && done;
+        tc::fence_after_sync();
+    };
+
+    const long long npix = (long long)m.W * m.H;
+    const long long ntiles = (p_end - p_begin + kTcRows - 1) / kTcRows;
+    const long long items = (long long)K * ntiles;
+    const long long nstreams = (long long)gridDim.x * kTcStreams, gs = (long long)blockIdx.x * kTcStreams + g;
+    const long long i0 = gs * items / nstreams, i1 = (gs + 1) * items / nstreams;
+
+    // +/- features and targets of this thread's pixel in an item
+    float fp[S::NIN], fm[S::NIN], t[S::NOUT];
+    auto gather = [&](long long item, float (&xp)[S::NIN], float (&xm)[S::NIN], float (&tt)[S::NOUT]) {
+        const int k = (int)(item / ntiles);
+        const long long p = p_begin + (item - (long long)k * ntiles) * kTcRows + tid;
+        const long long pc = p < p_end ? p : p_end - 1;
+        float a[kMaxIn], b[kMaxIn];
+        perturbed_features_pm(m, z, eps + (long long)k * nz, active, sg, (int)(pc % m.W), (int)(pc / m.W), a, b);
+#pragma unroll
+        for (int i = 0; i < S::NIN; i++) { xp[i] = a[i]; xm[i] = b[i]; }
+#pragma unroll
+        for (int c = 0; c < S::NOUT; c++) tt[c] = __ldg(tgt + pc * S::NOUT + c);
+    };
+    auto store_x = [&](const float (&x)[S::NIN]) {
+        float v[T::K1];
+#pragma unroll
+        for (int i = 0; i < T::K1; i++) v[i] = i < S::NIN ? x[i] : (i == S::NIN ? 1.0f : 0.0f);
+        store_split<T::K1>(trow, T::cXh, T::cXl, v);
+    };
+    // layer-1 result -> H in TMEM, then layer 2 issued
+    auto layer1_to_layer2 = [&]() {
+        float h[S::H1];
+        wait_mma();
+#pragma unroll
+        for (int q = 0; q < S::H1; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+        tc::wait_ld();
+#pragma unroll
+        for (int j = 0; j < S::H1; j += 2) {
+            const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak, leak_unit);
+            h[j] = v.x; h[j + 1] = v.y;
+        }
+        store_split<T::K2>(trow, T::cHh, T::cHl, h);
+        tc::wait_st();
+        tc::fence_before_sync();
+        ok = stream_sync_and(bar_id, ok);
+        if (ok && warp == 0) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+    };
+
+    if (i0 < i1) {
+        gather(i0, fp, fm, t);
+        store_x(fp);
+        tc::wait_st();
+        tc::fence_before_sync();
+        stream_sync(bar_id);
+        if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+    }
+#pragma unroll 1
+    for (long long item = i0; item < i1 && ok; item++) {
+        const bool more = item + 1 < i1;
+        float h[S::H2];
+        float np[S::NIN], nm[S::NIN], nt[S::NOUT];
+        // + unit
+        layer1_to_layer2();
+        if (!ok) break;
+        if (more) gather(item + 1, np, nm, nt);    // overlaps the layer-2 MMAs
+        wait_mma();
+#pragma unroll
+        for (int q = 0; q < S::H2; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+        tc::wait_ld();
+        store_x(fm);
+        tc::wait_st();
+        tc::fence_before_sync();
+        ok = stream_sync_and(bar_id, ok);
+        if (!ok) break;
+        if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        const float ep = out_layer_error<S>(m, sw, h, t, leak, leak_unit);
+        // - unit
+        layer1_to_layer2();
+        if (!ok) break;
+        wait_mma();
+#pragma unroll
+        for (int q = 0; q < S::H2; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+        tc::wait_ld();
+        if (more) { store_x(np); tc::wait_st(); }
+        tc::fence_before_sync();
+        ok = stream_sync_and(bar_id, ok);
+        if (!ok) break;
+        if (more && warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        const float em = out_layer_error<S>(m, sw, h, t, leak, leak_unit);
+        {
+            const int k = (int)(item / ntiles);
+            const long long p = p_begin + (item - (long long)k * ntiles) * kTcRows + tid;
+            if (p < p_end) dpix[(long long)k * npix + p] = (ep - em) * inv_px;
+        }
+#pragma unroll
+        for (int i = 0; i < S::NIN; i++) { fp[i] = np[i]; fm[i] = nm[i]; }
+#pragma unroll
+        for (int c = 0; c < S::NOUT; c++) t[c] = nt[c];
+    }
+    if (!ok) {
+        if (tid == 0) atomicExch(err, 1);
+        tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, 128 * kTcStreams); }
+}
+
+template <class S>
+void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const float* zdec, const float* eps, long long nz,
+                   const float* tgt, int K, unsigned active, float sg, float inv_px, float* dpix, long long p_begin,
+                   long long p_end, int* err) {
+    using T = TcShape<S>;
+    const size_t smem = (size_t)T::SIGN * sizeof(float);
+    static int nsm = 0;
+    if (nsm == 0) {
+        int dev = 0;
+        NTCB_CHECK(cudaGetDevice(&dev));
+        NTCB_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+        NTCB_CHECK(cudaFuncSetAttribute(k_lat_eval_tc<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    const long long items = (long long)K * ((p_end - p_begin + kTcRows - 1) / kTcRows);
+    const int grid = (int)std::min<long long>(nsm, (items + kTcStreams - 1) / kTcStreams);
+    k_lat_eval_tc<S><<<grid, kTcTPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, err);
+}
+
 }  // namespace
 
 int pop_tc_rows() { return kTcRows; }
@@ -440,6 +612,21 @@ bool launch_pop_eval_tc(cudaStream_t s, int shape, const DevModel& m, const PopA
     if (a.chunk % kTcRows != 0 || a.tc_err == nullptr) return false;
     switch (shape) {
 #define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: launch_tc<FixedShape<NIN, H1, H2, NOUT>>(s, m, a); break;
+        NTCB_FIXED_SHAPES(NTCB_CASE)
+#undef NTCB_CASE
+        default: return false;
+    }
+    NTCB_CHECK(cudaGetLastError());
+    return true;
+}
+
+bool launch_lat_eval_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
+                        long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
+                        long long p_begin, long long p_end, int* err) {
+    if (p_end <= p_begin || K <= 0) return true;
+    if (err == nullptr) return false;
+    switch (shape) {
+#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: launch_lat_tc<FixedShape<NIN, H1, H2, NOUT>>(s, m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, p_begin, p_end, err); break;
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: return false;

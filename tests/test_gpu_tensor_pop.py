@@ -1,4 +1,4 @@
-"""The tensor-core ES population kernel (tcgen05, 3xTF32) against the oracle's loss_subset and against the
+"""The tensor-core ES kernels (tcgen05, 3xTF32: population and latent pass) against the oracle's loss_subset and against the
 bit-exact packed-FP32 kernel, on every fixed shape (nin 5 / 6 / 8, 3 and 12 outputs), including minibatch
 sizes that leave a ragged last 128-row tile and the sigma = 0 case where both signs must agree exactly.
 
@@ -84,3 +84,21 @@ def test_tensor_training_steps_track_exact(cuda_device):
     d = np.abs(res[True] - res[False])
     assert np.median(d) < 1e-4 * 0.005
     assert np.mean(d > 0.5 * 0.005) < 0.02
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg5"])
+def test_tensor_latent_gradient_tracks_exact(name, cuda_device):
+    """One latent ES pass (lr 0) per kernel on fresh trainers (same noise step): the tensor-core gradient within
+    1e-4 rms of the exact kernel's (the reference's --cuda-check bar against the CPU is 1e-3 rms)."""
+    spec = spec_named(name)
+    tgt = target_for(spec)
+    g = {}
+    for tensor in (True, False):
+        tr, z, p = _trainer(spec, tgt)
+        tr.set_pop_kernel(tensor)
+        tr.lat_step(1, 0.05, 0.0, 4)
+        g[tensor] = tr.debug_last_zgrad().astype(np.float64)
+        tr.close()
+    rms = np.sqrt(np.mean(g[False] ** 2))
+    assert rms > 0
+    assert np.abs(g[True] - g[False]).max() < 1e-4 * rms
