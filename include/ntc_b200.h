@@ -181,6 +181,15 @@ int ntcb_pop_kernel(const ntcb_trainer* t);
  * step; every rank computes the identical update, so the replicas stay bit-identical. */
 void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, double* fit_dev);
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev);
+/* The same step with the ES gradient sharded too (no rank regenerates other ranks' noise). A rank's pair range
+ * must start and end on a gradient segment (64 pairs; N > 256); ntcb_shard_es_block_bytes returns the size of
+ * its exchange block in bytes, or -1 when the range does not qualify (then use the pair above). The block is
+ * [2 * n doubles: (L+, L-) per pair][n / 64 * P floats: the rank's gradient segment sums]. After the caller
+ * all-gathers every rank's block (rank order = pair order, equal n), ntcb_shard_mlp_apply_grad sums all
+ * segments in order and runs Adam: the same update, bit for bit, as the single-GPU step. */
+long long ntcb_shard_es_block_bytes(const ntcb_trainer* t, int N, int pair_begin, int pair_end);
+void ntcb_shard_mlp_eval_grad(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, void* block_dev);
+void ntcb_shard_mlp_apply_grad(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const void* blocks_dev, int world);
 /* The FD step (mlp_step_fd) sharded by weight: a rank draws the step's minibatch, evaluates the unperturbed
  * stats pair and the central differences of weights [j_begin, j_end), and writes their (lp, lm) as 2 doubles per
  * weight into fit_dev (DEVICE, 2 * (j_end - j_begin) doubles). After the caller gathers all P weights' pairs in
@@ -189,11 +198,12 @@ void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N,
 void ntcb_shard_fd_eval(ntcb_trainer* t, int it, float h, int M, int j_begin, int j_end, double* fit_dev);
 void ntcb_shard_fd_apply(ntcb_trainer* t, float h, float lr, const double* fit_all_dev);
 /* The latent ES step sharded by pixel rows: a rank writes the per-pixel loss differences of image rows
- * [row_begin, row_end) for all K pairs into dpix_dev, a DEVICE buffer laid out [K][W * H] (each pair's plane is
- * row-major, so a rank's rows are one contiguous range per plane); after the caller all-gathers every plane,
- * ntcb_shard_lat_apply runs the footprint gathers, Adam and the snap identically on every rank. */
-void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* dpix_dev);
-void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* dpix_all_dev);
+ * [row_begin, row_end) for all K pairs into block_dev, a DEVICE buffer laid out [K][(row_end - row_begin) * W].
+ * After the caller all-gathers the ranks' blocks (rank order = row order, equal blocks of rows_per_block rows,
+ * so one collective carries all K planes), ntcb_shard_lat_apply runs the footprint gathers, Adam and the snap
+ * identically on every rank. */
+void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* block_dev);
+void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* blocks_dev, int rows_per_block);
 /* The selector search sharded by level-0 texel rows: a rank searches rows [trow_begin, trow_end) and copies
  * their level-0 values into level0_dev (a DEVICE buffer of the level's W * H * C floats, rows contiguous);
  * after the caller's all-gather, ntcb_shard_qat_apply installs the full level 0 on every rank. */

@@ -118,12 +118,15 @@ SIGNATURES = {
     "ntcb_es_fitness_noalloc": (C.c_int, [C.POINTER(ModelDesc), C.c_int, C.c_float, C.c_int, C.c_int, _fp, _fp, _fp, C.c_int, _dp,
                                           C.c_char_p, C.c_size_t]),
     "ntcb_noise_fill": (None, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_size_t, _fp, C.POINTER(C.c_uint32)]),
+    "ntcb_shard_es_block_bytes": (C.c_longlong, [_vp, C.c_int, C.c_int, C.c_int]),
+    "ntcb_shard_mlp_eval_grad": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_mlp_apply_grad": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _vp, C.c_int]),
     "ntcb_shard_fd_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),
     "ntcb_shard_fd_apply": (None, [_vp, C.c_float, C.c_float, _vp]),
     "ntcb_shard_mlp_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "ntcb_shard_mlp_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _vp]),
     "ntcb_shard_lat_eval": (None, [_vp, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),
-    "ntcb_shard_lat_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, _vp]),
+    "ntcb_shard_lat_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, _vp, C.c_int]),
     "ntcb_shard_qat": (None, [_vp, C.c_int, C.c_int, _vp]),
     "ntcb_shard_qat_apply": (None, [_vp, _vp]),
 }

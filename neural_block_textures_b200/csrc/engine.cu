@@ -475,11 +475,15 @@ void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* 
 }
 
 // ES gradient from the fitness of all N pairs (pair order) and the Adam step on the weights.
+// Pairs per ES gradient segment: partial sums over consecutive pairs, summed in segment order (one segment,
+// the reference's serial order, for small populations).
+int es_seglen(int N) { return N <= 256 ? N : 64; }
+
 void es_apply(Impl& I, int it, float sigma, float lr, int N, const double* fit_all, bool regenerate_noise) {
     if (regenerate_noise) timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, 0, N, I.P, I.mlp_eps); });
     timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit_all, N, I.dl, I.lsum); });
     const float scale = 1.0f / (2.0f * (float)N * sigma);
-    const int seglen = N <= 256 ? N : 64;
+    const int seglen = es_seglen(N);
     const int nseg = (N + seglen - 1) / seglen;
     ensure_gpart(I, (long long)nseg * I.P);
     timed(I, "mlp_grad", 2, [&] {
@@ -576,7 +580,8 @@ unsigned lat_mask(const Impl& I) {
 
 // The first half of a latent ES step: the noise of every ES-trained texel for the K pairs of this step, and
 // the per-pixel loss differences of pixels [p_begin, p_end) written into dpix ([K][W H]).
-void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_end, float* dpix) {
+// Pixels [p_begin, p_end) of all K pairs; pair k's value of pixel p goes to dpix[k * pstride + p - p_begin].
+void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_end, float* dpix, long long pstride) {
     const unsigned mask = lat_mask(I);
     if (!mask) return;
     ensure_lat(I, K);
@@ -587,13 +592,15 @@ void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_e
     const float inv_px = 1.0f / (3.0f * I.d.wsum * (float)I.d.W * (float)I.d.H);
     timed(I, "lat_eval", 1, [&] {
         if (!(I.tensor_pop && ntcb::launch_lat_eval_tc(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma,
-                                                       inv_px, dpix, p_begin, p_end, I.tc_err)))
-            ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, dpix, p_begin, p_end);
+                                                       inv_px, dpix, p_begin, p_end, pstride, I.tc_err)))
+            ntcb::launch_lat_eval(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma, inv_px, dpix, p_begin, p_end,
+                                  pstride);
     });
 }
 
 // The second half: the DCT rate pass, the footprint gathers of every pixel's dpix, Adam, the snap.
-void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix) {
+// dpix in blocks of rows_per_block image rows, each [K][rows_per_block * W] (one block of H rows: [K][W * H]).
+void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix, int rows_per_block) {
     const unsigned mask = lat_mask(I);
     NTCB_CHECK(cudaMemsetAsync(I.zgrad, 0, I.nz * sizeof(float), I.stream));
     const bool rate = I.dct_live && I.rate_es;
@@ -613,7 +620,7 @@ void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix) {
             if (!(mask & (1u << l))) continue;
             const ntcb::RateTerm r = (l == 0) ? rt : ntcb::RateTerm{nullptr, 0.0f, 0, 0};
             timed(I, "lat_gather", 1, [&] {
-                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad);
+                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad, rows_per_block);
             });
         }
     }
@@ -632,16 +639,19 @@ void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
     if (K < 1) die("lat_step needs K >= 1 pairs");
     if (lat_mask(I)) {
         ensure_lat(I, K);
-        lat_eval_part(I, sigma, K, 0, I.npix, I.dpix);
+        lat_eval_part(I, sigma, K, 0, I.npix, I.dpix, I.npix);
     }
-    lat_apply_part(I, sigma, lr, K, I.dpix);
+    lat_apply_part(I, sigma, lr, K, I.dpix, I.d.H);
 }
 
 // Level-0 texels [t_begin, t_end) (row-major over the level) searched in place on the decode buffer.
 void qat_rows_part(Impl& I, long long t_begin, long long t_end) {
     if (I.d.qat <= 0) die("qat_search without --qat in the model description");
     timed(I, "qat", 1, [&] {
-        ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits, t_begin, t_end);
+        int max_bits = 0;
+        for (int c = 0; c < I.d.lv[0].C; c++) max_bits = std::max(max_bits, I.d.qat_bits[c]);
+        ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits, t_begin, t_end,
+                         max_bits);
     });
 }
 void qat_copy_back(Impl& I) {
@@ -891,19 +901,20 @@ void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int
     draw_batch(I, it, M);
     es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit_dev);
 }
-void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* dpix_dev) {
+void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* block_dev) {
     Impl& I = t->impl;
     require_ready(I); set_device(I);
     if (K < 1 || row_begin < 0 || row_end > I.d.H || row_begin > row_end) die("shard_lat_eval: bad pair count or row range");
-    lat_eval_part(I, sigma, K, (long long)row_begin * I.d.W, (long long)row_end * I.d.W, dpix_dev);
+    lat_eval_part(I, sigma, K, (long long)row_begin * I.d.W, (long long)row_end * I.d.W, block_dev, (long long)(row_end - row_begin) * I.d.W);
 }
-void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* dpix_all_dev) {
+void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* blocks_dev, int rows_per_block) {
     (void)it;
     Impl& I = t->impl;
     require_ready(I); set_device(I);
     if (K < 1) die("shard_lat_apply needs K >= 1 pairs");
+    if (rows_per_block < 1 || I.d.H % rows_per_block) die("shard_lat_apply: rows_per_block must divide the image height");
     if (lat_mask(I)) ensure_lat(I, K);
-    lat_apply_part(I, sigma, lr, K, dpix_all_dev);
+    lat_apply_part(I, sigma, lr, K, blocks_dev, rows_per_block);
 }
 void ntcb_shard_qat(ntcb_trainer* t, int trow_begin, int trow_end, float* level0_dev) {
     Impl& I = t->impl;
@@ -933,6 +944,50 @@ void ntcb_shard_fd_apply(ntcb_trainer* t, float h, float lr, const double* fit_a
     require_ready(I); set_device(I);
     NTCB_CHECK(cudaMemcpyAsync(I.fit, fit_all_dev, 2 * (size_t)I.P * sizeof(double), cudaMemcpyDeviceToDevice, I.stream));
     fd_apply(I, h, lr);
+}
+long long ntcb_shard_es_block_bytes(const ntcb_trainer* t, int N, int pair_begin, int pair_end) {
+    const Impl& I = t->impl;
+    const int seglen = es_seglen(N), n = pair_end - pair_begin;
+    if (!I.ready || N <= 256 || n <= 0 || pair_begin % seglen || n % seglen) return -1;
+    return 16LL * n + 4LL * (n / seglen) * I.P;
+}
+void ntcb_shard_mlp_eval_grad(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, void* block_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (ntcb_shard_es_block_bytes(t, N, pair_begin, pair_end) < 0 || N > I.pairs_cap || M > I.Mcap || M < 1)
+        die("shard_mlp_eval_grad: pair range not aligned to gradient segments, or sizes outside the buffers sized at init");
+    const int n = pair_end - pair_begin, seglen = es_seglen(N);
+    double* fit = static_cast<double*>(block_dev);
+    float* part = reinterpret_cast<float*>(static_cast<char*>(block_dev) + 16LL * n);
+    draw_batch(I, it, M);
+    es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit);
+    // this rank's pairs' loss differences and their gradient segments (the noise of these pairs is in mlp_eps)
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit, n, I.dl, I.lsum); });
+    const float scale = 1.0f / (2.0f * (float)N * sigma);
+    timed(I, "mlp_grad", 1, [&] { ntcb::launch_es_grad_partial(I.stream, I.dl, I.mlp_eps, n, I.P, scale, seglen, part); });
+}
+void ntcb_shard_mlp_apply_grad(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const void* blocks_dev, int world) {
+    (void)it; (void)sigma; (void)M;
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (world < 1 || N % world || N > I.pairs_cap) die("shard_mlp_apply_grad: N must split evenly over the ranks and fit the buffers");
+    const int n = N / world, seglen = es_seglen(N);
+    const long long bytes = ntcb_shard_es_block_bytes(t, N, 0, n);
+    if (bytes < 0) die("shard_mlp_apply_grad: the ranks' pair ranges are not aligned to gradient segments");
+    const size_t fit_bytes = 16 * (size_t)n, part_bytes = (size_t)bytes - fit_bytes;
+    const int nseg = N / seglen;
+    ensure_gpart(I, (long long)nseg * I.P);
+    const char* src = static_cast<const char*>(blocks_dev);
+    // [rank][fitness | partials] -> fitness of all N pairs in pair order, partials of all segments in order
+    NTCB_CHECK(cudaMemcpy2DAsync(I.fit, fit_bytes, src, (size_t)bytes, fit_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
+    NTCB_CHECK(cudaMemcpy2DAsync(I.gpart, part_bytes, src + fit_bytes, (size_t)bytes, part_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, I.fit, N, I.dl, I.lsum); });
+    timed(I, "mlp_grad", 1, [&] {
+        I.mlp_t++;
+        float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
+        ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
+    });
+    I.last_N = N; I.last_fd = false; I.last_pairs = N;
 }
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev) {
     Impl& I = t->impl;

@@ -49,7 +49,7 @@ int pop_tc_rows();
 // no tensor kernel (nothing launched). err: device flag set when an MMA completion wait timed out.
 bool launch_lat_eval_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                         long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
-                        long long p_begin, long long p_end, int* err);
+                        long long p_begin, long long p_end, long long pstride, int* err);
 // Sum the chunk partials of every candidate in order, normalise, and write (lp, lm) pairs to fit[2*i], fit[2*i+1].
 void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit);
 // ES: dl, lsum from the fitness of all N pairs; FD: dl, hh.
@@ -69,15 +69,19 @@ void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w,
 void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevModel& m, unsigned active_mask, long long nz, float* eps);
 void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                      long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
-                     long long p_begin, long long p_end);   // pixels [p_begin, p_end) of every pair
+                     long long p_begin, long long p_end, long long pstride);
+// (pixels [p_begin, p_end) of every pair; pair k's value of pixel p goes to dpix[k * pstride + p - p_begin])
 struct RateTerm {              // DCT rate term of the latent gradient (level 0), null dbits = off
     const int* dbits;          // [K][nblk * C]
     float rate_scale;
     int BW, C;
 };
+// dpix: blocks of rows_per_block image rows, each block [K][rows_per_block * W] (one block = the plain [K][W * H]).
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
-                       const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad);
+                       const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
+                       int rows_per_block);
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
-                const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end);
+                const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end,
+                int max_bits);
 
 }  // namespace ntcb

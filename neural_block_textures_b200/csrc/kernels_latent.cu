@@ -11,7 +11,6 @@ namespace {
 constexpr int kLatTPB = 128;
 constexpr int kLatPairs = 2;            // pairs per thread: rows = 2 pairs x 2 signs
 constexpr int kQatTPB = 128;
-constexpr int kQatRows = 4;             // candidate values per forward tile
 inline unsigned blocks_for(long long n, int tpb) { return (unsigned)((n + tpb - 1) / tpb); }
 }  // namespace
 
@@ -43,11 +42,10 @@ template <class S, int TPB>
 __global__ void __launch_bounds__(TPB) k_lat_eval_fixed(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                         const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
                                                         int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
-                                                        long long p_begin, long long p_end) {
+                                                        long long p_begin, long long p_end, long long pstride) {
     constexpr int R2 = kLatPairs;
     extern __shared__ __align__(16) float ws[];
     load_weights_x2<S>(wg, m.P, ws);
-    const long long npix = (long long)m.W * m.H;
     const long long p = p_begin + (long long)blockIdx.x * TPB + threadIdx.x;
     const long long pc = p < p_end ? p : p_end - 1;
     const int px = (int)(pc % m.W), py = (int)(pc / m.W);
@@ -78,17 +76,16 @@ __global__ void __launch_bounds__(TPB) k_lat_eval_fixed(DevModel m, const float*
             ep += m.cw[c] * (dp * dp);
             em += m.cw[c] * (dm * dm);
         }
-        if (k < K) dpix[(long long)k * npix + p] = (ep - em) * inv_px;
+        if (k < K) dpix[(long long)k * pstride + (p - p_begin)] = (ep - em) * inv_px;
     }
 }
 
 __global__ void k_lat_eval_generic(DevModel m, const float* __restrict__ wg, const float* __restrict__ z, const float* __restrict__ eps,
                                    long long nz, const float* __restrict__ tgt, int K, unsigned active, float sg, float inv_px,
-                                   float* __restrict__ dpix, long long p_begin, long long p_end) {
+                                   float* __restrict__ dpix, long long p_begin, long long p_end, long long pstride) {
     extern __shared__ __align__(16) float ws[];
     for (int k = threadIdx.x; k < m.P; k += blockDim.x) ws[k] = wg[k];
     __syncthreads();
-    const long long npix = (long long)m.W * m.H;
     const long long p = p_begin + (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int k = blockIdx.y;
     if (p >= p_end) return;
@@ -101,24 +98,24 @@ __global__ void k_lat_eval_generic(DevModel m, const float* __restrict__ wg, con
     perturbed_features(m, z, eps + (long long)k * nz, active, -sg, px, py, f);
     generic_forward(m, ws, f, o);
     const float em = pixel_err_f(m, o, t);
-    dpix[(long long)k * npix + p] = (ep - em) * inv_px;
+    dpix[(long long)k * pstride + (p - p_begin)] = (ep - em) * inv_px;
 }
 
 void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                      long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
-                     long long p_begin, long long p_end) {
+                     long long p_begin, long long p_end, long long pstride) {
     const long long n = p_end - p_begin;
     if (n <= 0) return;
     switch (shape) {
 #define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: { using S = FixedShape<NIN, H1, H2, NOUT>; \
         dim3 grid(blocks_for(n, kLatTPB), (unsigned)((K + kLatPairs - 1) / kLatPairs)); \
         k_lat_eval_fixed<S, kLatTPB><<<grid, kLatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, \
-                                                                                     p_begin, p_end); break; }
+                                                                                     p_begin, p_end, pstride); break; }
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: {
             dim3 grid(blocks_for(n, 128), (unsigned)K);
-            k_lat_eval_generic<<<grid, 128, m.P * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, p_begin, p_end);
+            k_lat_eval_generic<<<grid, 128, m.P * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, p_begin, p_end, pstride);
         }
     }
     NTCB_CHECK(cudaGetLastError());
@@ -131,19 +128,21 @@ void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* 
 // the DCT rate term is on (level 0), pair k's rate contribution follows its mse contribution
 // (dct_rate_pass, main.cpp:1935-1958).
 __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, const int* __restrict__ yr, const float* __restrict__ dpix,
-                             const float* __restrict__ eps, long long nz, int K, float scale, RateTerm rate, float* __restrict__ grad) {
+                             const float* __restrict__ eps, long long nz, int K, float scale, RateTerm rate, float* __restrict__ grad,
+                             int rpb) {
     const DevLevel& L = m.lv[level];
     const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (long long)L.W * L.H) return;
     const int tx = (int)(t % L.W), ty = (int)(t / L.W);
     const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
-    const long long npix = (long long)m.W * m.H;
     const long long base = L.off + t * L.C;
+    const long long plane = (long long)rpb * m.W, block = (long long)K * plane;
     for (int k = 0; k < K; k++) {
         float d = 0.0f;
-        const float* dp = dpix + (long long)k * npix;
-        for (int py = y0; py < y1; py++)
-            for (int px = x0; px < x1; px++) d += dp[(long long)py * m.W + px];
+        for (int py = y0; py < y1; py++) {
+            const float* row = dpix + (py / rpb) * block + k * plane + (long long)(py % rpb) * m.W;
+            for (int px = x0; px < x1; px++) d += row[px];
+        }
         const float w = d * scale;
         const float* ek = eps + (long long)k * nz;
         for (int c = 0; c < L.C; c++) grad[base + c] = fmaf(w, ek[base + c], grad[base + c]);
@@ -157,9 +156,10 @@ __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, 
 }
 
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
-                       const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad) {
+                       const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
+                       int rows_per_block) {
     const long long ntx = (long long)m.lv[level].W * m.lv[level].H;
-    k_lat_gather<<<blocks_for(ntx, 128), 128, 0, s>>>(m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad);
+    k_lat_gather<<<blocks_for(ntx, 128), 128, 0, s>>>(m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block);
     NTCB_CHECK(cudaGetLastError());
 }
 
@@ -171,46 +171,53 @@ __device__ __forceinline__ int qat_index(float v, int bits) {
     return max(0, min(levels, k));
 }
 
-// qat_search (main.cpp:2088-2139), one thread per level-0 texel: channels in order; for channel c every grid
-// value's cell loss (double, pixels in raster order) is computed — kQatRows candidates per forward tile —
-// then the reference's rule picks the winner: the current value first, any other value only if strictly
-// lower. The winner is written in place before the next channel is searched.
-// The rule is applied as the losses stream in: the first strict minimum over the other grid values (index
-// order), which wins only if it is below the current value's loss — the same choice as the reference's scan
-// (best = loss[current]; for k != current in order: if loss[k] < best take it), with no per-value array.
-template <class S, int TPB>
-__global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __restrict__ wg, float* __restrict__ z,
+// qat_search (main.cpp:2088-2139) for the fixed shapes: G consecutive lanes of a warp share one level-0
+// texel; lane gi evaluates the candidate pairs gi, gi + G, ... (grid values 2q and 2q + 1 as one packed-FP32
+// row pair). A candidate's cell loss is accumulated in double over the texel's pixels in raster order by
+// one lane, as the reference does. Channels run in order and the winner is installed before the next
+// channel. The reference's choice (best = loss[current]; for every other value k in order: if loss[k] <
+// best take it) equals: the smallest k != current attaining the minimum of the other losses, if that
+// minimum is below loss[current]; the lanes combine their (loss, k) with that rule by shuffles.
+template <class S, int TPB, int G, int R2>
+__global__ void __launch_bounds__(TPB, 4) k_qat_fixed(DevModel m, const float* __restrict__ wg, float* __restrict__ z,
                                                    const float* __restrict__ tgt, const int* __restrict__ xr,
                                                    const int* __restrict__ yr, const float* __restrict__ grid,
                                                    const int* __restrict__ bits_c, long long t_begin, long long t_end) {
-    constexpr int R = kQatRows, R2 = kQatRows / 2;
+    static_assert(G == 1 || G == 2 || G == 4 || G == 8, "lanes per texel");
     extern __shared__ __align__(16) float ws[];
     load_weights_x2<S>(wg, m.P, ws);
     const DevLevel& L = m.lv[0];
-    const long long t = t_begin + (long long)blockIdx.x * TPB + threadIdx.x;
-    if (t >= t_end) return;   // no barrier below
-    const int tx = (int)(t % L.W), ty = (int)(t / L.W);
+    const long long gt = (long long)blockIdx.x * TPB + threadIdx.x;
+    const int gi = (int)(gt % G);
+    const long long t = t_begin + gt / G;
+    const bool live = t < t_end;
+    const long long tc = live ? t : t_end - 1;            // dead lanes shadow a live texel and write nothing
+    const int tx = (int)(tc % L.W), ty = (int)(tc / L.W);
     const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
-    if (x0 >= x1 || y0 >= y1) return;
-    float* zt = z + L.off + t * L.C;
+    float* zt = z + L.off + tc * L.C;
+    const unsigned gmask = (G == 1) ? 0xffffffffu : (((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1)));
     for (int c = 0; c < L.C; c++) {
         const int bits = bits_c[c], n = 1 << bits;
         const float* gv = grid + bits * 257;
         const int cur = qat_index(zt[c], bits);
-        double cur_loss = 0.0, other = 0.0;
-        int other_k = -1;
-        for (int kg = 0; kg < n; kg += R) {
-            double acc[R];
+        double cur_loss = 0.0, best = 0.0;
+        int best_k = -1;
+        for (int q = gi; 2 * R2 * q < n; q += G) {
+            double acc[2 * R2];
 #pragma unroll
-            for (int r = 0; r < R; r++) acc[r] = 0.0;
+            for (int r = 0; r < 2 * R2; r++) acc[r] = 0.0;
+#pragma unroll 1
             for (int py = y0; py < y1; py++)
+#pragma unroll 1
                 for (int px = x0; px < x1; px++) {
+                    // keeps the weight loads of the forward inside the loop (hoisted, they exhaust the registers)
+                    asm volatile("" ::: "memory");
                     float f[kMaxIn];
                     pixel_features(m, z, px, py, f);
                     float2 x[R2][S::NIN];
 #pragma unroll
                     for (int h = 0; h < R2; h++) {
-                        const float va = gv[min(kg + 2 * h, n - 1)], vb = gv[min(kg + 2 * h + 1, n - 1)];
+                        const float va = gv[min(2 * R2 * q + 2 * h, n - 1)], vb = gv[min(2 * R2 * q + 2 * h + 1, n - 1)];
 #pragma unroll
                         for (int i = 0; i < S::NIN; i++) x[h][i] = (i == c) ? make_float2(va, vb) : make_float2(f[i], f[i]);
                     }
@@ -220,21 +227,35 @@ __global__ void __launch_bounds__(TPB) k_qat_fixed(DevModel m, const float* __re
 #pragma unroll
                     for (int h = 0; h < R2; h++)
 #pragma unroll
-                        for (int q = 0; q < S::NOUT; q++) {
-                            const float da = o[h][q].x - tp[q], db = o[h][q].y - tp[q];
-                            acc[2 * h] += (double)(m.cw[q] * (da * da));
-                            acc[2 * h + 1] += (double)(m.cw[q] * (db * db));
+                        for (int k = 0; k < S::NOUT; k++) {
+                            const float da = o[h][k].x - tp[k], db = o[h][k].y - tp[k];
+                            acc[2 * h] += (double)(m.cw[k] * (da * da));
+                            acc[2 * h + 1] += (double)(m.cw[k] * (db * db));
                         }
                 }
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int k = kg + r;
+            for (int r = 0; r < 2 * R2; r++) {
+                const int k = 2 * R2 * q + r;
                 if (k >= n) continue;
-                if (k == cur) cur_loss = acc[r];
-                else if (other_k < 0 || acc[r] < other) { other = acc[r]; other_k = k; }
+                const double lk = acc[r];
+                if (k == cur) cur_loss = lk;
+                else if (best_k < 0 || lk < best) { best = lk; best_k = k; }
             }
         }
-        zt[c] = gv[(other_k >= 0 && other < cur_loss) ? other_k : cur];
+        if (G > 1) {
+            // combine: smaller loss wins, equal losses go to the smaller index (the first in scan order)
+#pragma unroll
+            for (int o = 1; o < G; o <<= 1) {
+                const double ob = __shfl_xor_sync(gmask, best, o);
+                const int ok = __shfl_xor_sync(gmask, best_k, o);
+                if (ok >= 0 && (best_k < 0 || ob < best || (ob == best && ok < best_k))) { best = ob; best_k = ok; }
+            }
+            const int owner = (cur / (2 * R2)) % G;
+            cur_loss = __shfl_sync(gmask, cur_loss, ((threadIdx.x & 31) & ~(G - 1)) + owner);
+        }
+        const float win = gv[(best_k >= 0 && best < cur_loss) ? best_k : cur];
+        if (live && gi == 0) zt[c] = win;
+        __syncwarp(gmask);
     }
 }
 
@@ -277,14 +298,30 @@ __global__ void k_qat_generic(DevModel m, const float* __restrict__ wg, float* _
     }
 }
 
+template <class S, int G, int R2>
+void launch_qat_fixed(cudaStream_t s, const DevModel& m, const float* w, float* zdec, const float* tgt, const int* xr0,
+                      const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end) {
+    const long long lanes = (t_end - t_begin) * G;
+    k_qat_fixed<S, kQatTPB, G, R2><<<blocks_for(lanes, kQatTPB), kQatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0,
+                                                                                                           grid, bits, t_begin, t_end);
+}
+
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
-                const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end) {
+                const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end,
+                int max_bits) {
     const long long ntx = t_end - t_begin;
     if (ntx <= 0) return;
+    // 3 outputs: one lane per texel with 4 candidates per tile (measured 1.72 ms at config 5 against 1.92 ms
+    // for 2 lanes x 2); 12 outputs: the wider output layer leaves room for one candidate pair per lane and up
+    // to 4 lanes per texel (0.19 ms against 0.27 ms at config 3).
+    const int G = max_bits <= 1 ? 1 : (max_bits == 2 ? 2 : 4);
     switch (shape) {
 #define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: { using S = FixedShape<NIN, H1, H2, NOUT>; \
-        k_qat_fixed<S, kQatTPB><<<blocks_for(ntx, kQatTPB), kQatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits, \
-                                                                                                      t_begin, t_end); break; }
+        if constexpr (NOUT <= 4) launch_qat_fixed<S, 1, 2>(s, m, w, zdec, tgt, xr0, yr0, grid, bits, t_begin, t_end); \
+        else if (G == 1) launch_qat_fixed<S, 1, 1>(s, m, w, zdec, tgt, xr0, yr0, grid, bits, t_begin, t_end); \
+        else if (G == 2) launch_qat_fixed<S, 2, 1>(s, m, w, zdec, tgt, xr0, yr0, grid, bits, t_begin, t_end); \
+        else launch_qat_fixed<S, 4, 1>(s, m, w, zdec, tgt, xr0, yr0, grid, bits, t_begin, t_end); \
+        break; }
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: k_qat_generic<<<blocks_for(ntx, 128), 128, m.P * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits, t_begin, t_end);

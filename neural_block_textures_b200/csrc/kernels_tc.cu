@@ -448,7 +448,8 @@ template <class S>
 __global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                          const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
                                                          int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
-                                                         long long p_begin, long long p_end, int* __restrict__ err) {
+                                                         long long p_begin, long long p_end, long long pstride,
+                                                         int* __restrict__ err) {
     using T = TcShape<S>;
     extern __shared__ __align__(1024) float sw[];   // one weight set [T::SIGN]
     __shared__ __align__(8) uint64_t bars[kTcStreams];
@@ -569,7 +570,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const flo
         {
             const int k = (int)(item / ntiles);
             const long long p = p_begin + (item - (long long)k * ntiles) * kTcRows + tid;
-            if (p < p_end) dpix[(long long)k * npix + p] = (ep - em) * inv_px;
+            if (p < p_end) dpix[(long long)k * pstride + (p - p_begin)] = (ep - em) * inv_px;
         }
 #pragma unroll
         for (int i = 0; i < S::NIN; i++) { fp[i] = np[i]; fm[i] = nm[i]; }
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const flo
 template <class S>
 void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const float* zdec, const float* eps, long long nz,
                    const float* tgt, int K, unsigned active, float sg, float inv_px, float* dpix, long long p_begin,
-                   long long p_end, int* err) {
+                   long long p_end, long long pstride, int* err) {
     using T = TcShape<S>;
     const size_t smem = (size_t)T::SIGN * sizeof(float);
     static int nsm = 0;
@@ -600,7 +601,7 @@ void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const floa
     }
     const long long items = (long long)K * ((p_end - p_begin + kTcRows - 1) / kTcRows);
     const int grid = (int)std::min<long long>(nsm, (items + kTcStreams - 1) / kTcStreams);
-    k_lat_eval_tc<S><<<grid, kTcTPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, err);
+    k_lat_eval_tc<S><<<grid, kTcTPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
 }
 
 }  // namespace
@@ -622,11 +623,11 @@ bool launch_pop_eval_tc(cudaStream_t s, int shape, const DevModel& m, const PopA
 
 bool launch_lat_eval_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                         long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
-                        long long p_begin, long long p_end, int* err) {
+                        long long p_begin, long long p_end, long long pstride, int* err) {
     if (p_end <= p_begin || K <= 0) return true;
     if (err == nullptr) return false;
     switch (shape) {
-#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: launch_lat_tc<FixedShape<NIN, H1, H2, NOUT>>(s, m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, p_begin, p_end, err); break;
+#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: launch_lat_tc<FixedShape<NIN, H1, H2, NOUT>>(s, m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, p_begin, p_end, pstride, err); break;
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: return false;

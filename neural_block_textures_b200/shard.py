@@ -1,12 +1,14 @@
 """Sharding one ES training iteration over G ranks (one process and one GPU per rank).
 
 * MLP ES step — the population: rank r evaluates the antithetic pairs [r N / G, (r + 1) N / G), regenerating
-  their noise from the counter (no noise crosses the wire), and contributes 2 doubles per pair (L+, L-). One
-  all-gather gives every rank the fitness of all N pairs in pair order; each rank computes the identical ES
-  gradient and Adam step, so the weight replicas stay bit-identical without exchanging weights.
+  their noise from the counter (no noise crosses the wire). When its range is aligned to the 64-pair gradient
+  segments it also sums its own segments of the ES gradient and contributes one block: 2 doubles per pair
+  (L+, L-) and P floats per segment; otherwise just the fitness. One all-gather gives every rank all blocks in
+  pair order; each rank runs the identical segment sum (or full gradient) and Adam, so the weight replicas
+  stay bit-identical without exchanging weights.
 * Latent ES step — the image: rank r evaluates the K pairs' per-pixel loss differences for image rows
-  [r H / G, (r + 1) H / G); one in-place all-gather per pair plane gives every rank the full [K][W H] array,
-  from which each rank runs the identical footprint gathers, Adam and snap.
+  [r H / G, (r + 1) H / G) into its block [K][rows W]; one all-gather of the blocks (rank order = row order)
+  gives every rank all K planes, from which each rank runs the identical footprint gathers, Adam and snap.
 * FD step — the weights: rank r evaluates the central differences of weights [r B, min((r + 1) B, P)) with
   B = ceil(P / G) (every rank also evaluates the unperturbed stats pair); one all-gather of the padded
   [G][B] fitness pairs leaves all P weights' (L+, L-) in weight order at the front, and every rank runs the
@@ -60,13 +62,22 @@ class ShardedES:
         per = self.p1 - self.p0
         self.fit_local = torch.zeros(2 * per, dtype=torch.float64, device=device)
         self.fit_all = torch.zeros(2 * N, dtype=torch.float64, device=device)
+        self.block = -1
+        if hasattr(trainer, "shard_es_block_bytes"):
+            self.block = trainer.shard_es_block_bytes(N, self.p0, self.p1)
+        if self.block > 0:
+            self.blk_local = torch.zeros(self.block, dtype=torch.uint8, device=device)
+            self.blk_all = torch.zeros(self.block * self.world, dtype=torch.uint8, device=device)
         self.stream = stream
         self.dpix = None
         if image is not None and K > 0:
             W, H = image
             self.W = W
             self.r0, self.r1 = even_range(H, self.world, self.rank, "image rows")
-            self.dpix = torch.zeros(K, W * H, dtype=torch.float32, device=device)
+            self.rows = self.r1 - self.r0
+            self.dblock = torch.zeros(K * self.rows * W, dtype=torch.float32, device=device)
+            self.dpix = torch.zeros(self.world * K * self.rows * W, dtype=torch.float32, device=device)
+            self.K = K
         self.l0 = None
         if level0 is not None:
             LW, LH, LC = level0
@@ -87,6 +98,12 @@ class ShardedES:
 
     def step(self, it: int, sigma: float, lr: float, M: int) -> None:
         """One MLP ES step (mlp_step)."""
+        if self.block > 0:
+            self.t.shard_mlp_eval_grad(it, sigma, self.N, M, self.p0, self.p1, self.blk_local)
+            with self._ctx():
+                self.dist.all_gather_into_tensor(self.blk_all, self.blk_local)
+            self.t.shard_mlp_apply_grad(it, sigma, lr, self.N, M, self.blk_all, self.world)
+            return
         self.t.shard_mlp_eval(it, sigma, self.N, M, self.p0, self.p1, self.fit_local)
         with self._ctx():
             self.dist.all_gather_into_tensor(self.fit_all, self.fit_local)
@@ -102,13 +119,11 @@ class ShardedES:
 
     def lat_step(self, it: int, sigma: float, lr: float, K: int) -> None:
         """One latent ES step (lat_step)."""
-        assert self.dpix is not None and K == self.dpix.shape[0]
-        self.t.shard_lat_eval(sigma, K, self.r0, self.r1, self.dpix)
-        a, b = self.r0 * self.W, self.r1 * self.W
+        assert self.dpix is not None and K == self.K
+        self.t.shard_lat_eval(sigma, K, self.r0, self.r1, self.dblock)
         with self._ctx():
-            for k in range(K):
-                self.dist.all_gather_into_tensor(self.dpix[k], self.dpix[k, a:b])
-        self.t.shard_lat_apply(it, sigma, lr, K, self.dpix)
+            self.dist.all_gather_into_tensor(self.dpix, self.dblock)
+        self.t.shard_lat_apply(it, sigma, lr, K, self.dpix, self.rows)
 
     def qat_search(self) -> None:
         """One selector search (qat_search)."""

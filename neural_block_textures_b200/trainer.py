@@ -195,6 +195,16 @@ class Trainer:
         ptr = fit_all_dev if isinstance(fit_all_dev, int) else fit_all_dev.data_ptr()
         self.lib.ntcb_shard_mlp_apply(self.h, it, sigma, lr, N, M, C.c_void_p(ptr))
 
+    def shard_es_block_bytes(self, N: int, p0: int, p1: int) -> int:
+        return int(self.lib.ntcb_shard_es_block_bytes(self.h, N, p0, p1))
+
+    def shard_mlp_eval_grad(self, it: int, sigma: float, N: int, M: int, p0: int, p1: int, block_dev) -> None:
+        """block_dev: device buffer of shard_es_block_bytes(N, p0, p1) bytes (fitness, then gradient segments)."""
+        self.lib.ntcb_shard_mlp_eval_grad(self.h, it, sigma, N, M, p0, p1, C.c_void_p(_dptr(block_dev)))
+
+    def shard_mlp_apply_grad(self, it: int, sigma: float, lr: float, N: int, M: int, blocks_dev, world: int) -> None:
+        self.lib.ntcb_shard_mlp_apply_grad(self.h, it, sigma, lr, N, M, C.c_void_p(_dptr(blocks_dev)), world)
+
     def shard_fd_eval(self, it: int, h: float, M: int, j_begin: int, j_end: int, fit_dev) -> None:
         """fit_dev: device buffer of >= 2 * (j_end - j_begin) doubles; receives (L+, L-) of weights [j_begin, j_end)."""
         self.lib.ntcb_shard_fd_eval(self.h, it, h, M, j_begin, j_end, C.c_void_p(_dptr(fit_dev)))
@@ -203,12 +213,13 @@ class Trainer:
         """fit_all_dev: device buffer whose first 2 * P doubles are every weight's (L+, L-) in weight order."""
         self.lib.ntcb_shard_fd_apply(self.h, h, lr, C.c_void_p(_dptr(fit_all_dev)))
 
-    def shard_lat_eval(self, sigma: float, K: int, row_begin: int, row_end: int, dpix_dev) -> None:
-        """dpix_dev: a CUDA tensor [K, W * H] of float32; rows [row_begin, row_end) of every plane are written."""
-        self.lib.ntcb_shard_lat_eval(self.h, sigma, K, row_begin, row_end, C.c_void_p(_dptr(dpix_dev)))
+    def shard_lat_eval(self, sigma: float, K: int, row_begin: int, row_end: int, block_dev) -> None:
+        """block_dev: a CUDA tensor of K * (row_end - row_begin) * W float32, laid out [K][rows * W]."""
+        self.lib.ntcb_shard_lat_eval(self.h, sigma, K, row_begin, row_end, C.c_void_p(_dptr(block_dev)))
 
-    def shard_lat_apply(self, it: int, sigma: float, lr: float, K: int, dpix_all_dev) -> None:
-        self.lib.ntcb_shard_lat_apply(self.h, it, sigma, lr, K, C.c_void_p(_dptr(dpix_all_dev)))
+    def shard_lat_apply(self, it: int, sigma: float, lr: float, K: int, blocks_dev, rows_per_block: int) -> None:
+        """blocks_dev: every rank's block in row order, each [K][rows_per_block * W]."""
+        self.lib.ntcb_shard_lat_apply(self.h, it, sigma, lr, K, C.c_void_p(_dptr(blocks_dev)), rows_per_block)
 
     def shard_qat(self, trow_begin: int, trow_end: int, level0_dev) -> None:
         """level0_dev: a CUDA tensor of the level-0 W * H * C floats; the searched rows are written into it."""

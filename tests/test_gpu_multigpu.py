@@ -10,7 +10,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-N, M, K, ITERS = 32, 256, 4, 3
+N, M, K, ITERS = 512, 256, 4, 3   # 256 pairs per rank: the segment-aligned ES block exchange
 
 
 def _spec():
@@ -50,6 +50,7 @@ def _rank_main(rank, world, port, out_dir):
         L0 = spec.levels[0]
         es = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K, image=(spec.W, spec.H), level0=(L0.W, L0.H, L0.C),
                        P=spec.P)
+        assert es.block > 0
         for it in range(1, ITERS + 1):
             es.step(it, 0.02, 0.005, M)
             es.lat_step(it, 0.05, 0.02, K)

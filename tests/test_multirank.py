@@ -63,13 +63,17 @@ class PlumbingTrainer:
     """Writes known values into its own rows / texel rows and records what the exchange delivered."""
     W, H, LW, LH, LC, K, P = 12, 8, 6, 4, 2, 3, 11
 
-    def shard_lat_eval(self, sigma, K, r0, r1, dpix):
+    def shard_lat_eval(self, sigma, K, r0, r1, block):
+        n = (r1 - r0) * self.W
         for k in range(K):
             for p in range(r0 * self.W, r1 * self.W):
-                dpix[k, p] = 1000.0 * k + p
+                block[k * n + p - r0 * self.W] = 1000.0 * k + p
 
-    def shard_lat_apply(self, it, sigma, lr, K, dpix_all):
-        self.dpix = dpix_all.clone()
+    def shard_lat_apply(self, it, sigma, lr, K, blocks, rows_per_block):
+        # back to [K][W * H] planes: block b holds rows [b R, (b + 1) R) of every plane
+        n = rows_per_block * self.W
+        b = blocks.reshape(-1, K, n)
+        self.dpix = b.permute(1, 0, 2).reshape(K, -1).clone()
 
     def shard_qat(self, t0, t1, l0):
         n = self.LW * self.LC
@@ -78,6 +82,25 @@ class PlumbingTrainer:
 
     def shard_qat_apply(self, l0_all):
         self.l0 = l0_all.clone()
+
+    def shard_es_block_bytes(self, N, p0, p1):
+        n = p1 - p0
+        return 16 * n + 4 * (n // 64) * self.P
+
+    def shard_mlp_eval_grad(self, it, sigma, N, M, p0, p1, block):
+        # fitness doubles: (10 i + 1, 10 i + 2) per pair i; segment floats: 100 seg + k
+        n = p1 - p0
+        f = block[: 16 * n].view(torch.float64)
+        for i in range(p0, p1):
+            f[2 * (i - p0)] = 10.0 * i + 1.0
+            f[2 * (i - p0) + 1] = 10.0 * i + 2.0
+        g = block[16 * n:].view(torch.float32)
+        for sg in range(n // 64):
+            for k in range(self.P):
+                g[sg * self.P + k] = 100.0 * (p0 // 64 + sg) + k
+
+    def shard_mlp_apply_grad(self, it, sigma, lr, N, M, blocks, world):
+        self.es_blocks = blocks.clone()
 
     def shard_fd_eval(self, it, h, M, j0, j1, fit):
         for j in range(j0, j1):
@@ -98,6 +121,10 @@ def _plumbing_main(rank, world, port, out_dir):
         es.qat_search()
         es.fd_step(1, 1e-3, 0.0, 64)
         np.save(os.path.join(out_dir, f"f{rank}.npy"), t.fd.numpy())
+        es2 = ShardedES(t, dist, 256, device="cpu")       # 128 pairs per rank: the segment-aligned block exchange
+        assert es2.block > 0
+        es2.step(1, 0.02, 0.0, 64)
+        np.save(os.path.join(out_dir, f"b{rank}.npy"), t.es_blocks.numpy())
         np.save(os.path.join(out_dir, f"d{rank}.npy"), t.dpix.numpy())
         np.save(os.path.join(out_dir, f"l{rank}.npy"), t.l0.numpy())
     finally:
@@ -105,8 +132,8 @@ def _plumbing_main(rank, world, port, out_dir):
 
 
 def test_latent_qat_fd_sharding_plumbing(tmp_path):
-    """Two gloo ranks: each fills only its own image rows / level-0 texel rows / FD weights (P = 11, uneven);
-    after the all-gathers every rank holds the whole arrays in order."""
+    """Two gloo ranks: each fills only its own image rows / level-0 texel rows / FD weights (P = 11, uneven) /
+    ES block (fitness + gradient segments); after the all-gathers every rank holds the whole arrays in order."""
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_plumbing_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
@@ -119,10 +146,17 @@ def test_latent_qat_fd_sharding_plumbing(tmp_path):
     want_d = np.array([[1000.0 * k + p for p in range(T.W * T.H)] for k in range(T.K)], np.float32)
     want_l = np.array([-1.0 - i for i in range(T.LW * T.LH * T.LC)], np.float32)
     want_f = np.array([10.0 * j + 1.0 + s for j in range(T.P) for s in range(2)])
+    n = 128
+    want_b = []
+    for r in range(2):
+        want_b.append(np.array([10.0 * i + 1.0 + s for i in range(r * n, (r + 1) * n) for s in range(2)]).view(np.uint8))
+        want_b.append(np.array([100.0 * (r * n // 64 + sg) + k for sg in range(n // 64) for k in range(T.P)], np.float32).view(np.uint8))
+    want_b = np.concatenate(want_b)
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"d{r}.npy"), want_d)
         assert np.array_equal(np.load(tmp_path / f"l{r}.npy"), want_l)
         assert np.array_equal(np.load(tmp_path / f"f{r}.npy"), want_f)
+        assert np.array_equal(np.load(tmp_path / f"b{r}.npy"), want_b)
 
 
 def test_padded_range():
