@@ -161,6 +161,13 @@ int ntcb_es_fitness_noalloc(const ntcb_model_desc* d, int it, float sigma, int p
 int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi);
 /* Measured FP32 FMA throughput of the current device in TFLOP/s (the roofline of the population kernels). */
 double ntcb_fp32_peak_tflops(void);
+/* The DCT scale-code sensitivity probe (dct_probe_codes, main.cpp:1002-1030) on the device, for the current MLP
+ * and decode buffer: one code per (8x8 block of the image, level-0 channel), [block raster][channel], and the
+ * block gains. Fills min(n, cap) entries of codes / gains (host buffers, either may be null) and returns n =
+ * (W / 8) * (H / 8) * C. Replaces the host probe of the --dct-q switch and refits (main.cpp:4110-4120), which
+ * would otherwise download the model and decode on the host. Not strict FP, like the host probe: codes can
+ * differ from a host run where a gain lies on a code boundary. No counterpart in the reference. */
+size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap);
 /* Number of kernels this trainer has launched since creation. */
 long long ntcb_launch_count(const ntcb_trainer* t);
 /* Which kernels evaluate the ES decodes (mlp_step / ntcb_shard_mlp_eval pairs and the lat_step pass). tensor = 1

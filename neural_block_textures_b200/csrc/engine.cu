@@ -867,6 +867,22 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
     I.totals.erase(it);
 }
 long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
+size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    const int BW = I.d.W / 8, BH = I.d.H / 8, C = I.d.lv[0].C;
+    const size_t n = (size_t)BW * BH * C;
+    if ((!codes && !gains) || n == 0) return n;
+    uint8_t* dc = dalloc<uint8_t>(n);
+    float* dg = dalloc<float>(n);
+    timed(I, "dct_probe", 1, [&] { ntcb::launch_dct_probe(I.stream, I.dm, I.w, I.zdec, BW, BH, C, dc, dg); });
+    const size_t k = std::min(n, cap);
+    if (codes) NTCB_CHECK(cudaMemcpyAsync(codes, dc, k, cudaMemcpyDeviceToHost, I.stream));
+    if (gains) NTCB_CHECK(cudaMemcpyAsync(gains, dg, k * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+    dfree(dc); dfree(dg);
+    return n;
+}
 void ntcb_set_pop_kernel(ntcb_trainer* t, int tensor) { t->impl.tensor_pop = tensor != 0; }
 int ntcb_pop_kernel(const ntcb_trainer* t) { return (t->impl.tensor_pop && t->impl.shape != 0) ? 1 : 0; }
 int ntcb_footprint_ranges(int npx, int ntex, int nearest, int* lo, int* hi) {

@@ -64,6 +64,8 @@ void launch_fd_grad_adam(cudaStream_t s, const double* dl, const double* hh, int
                          float lr, float c1, float c2);
 void launch_adam(cudaStream_t s, float* theta, const float* g, float* m, float* v, long long n, float lr, float c1, float c2);
 void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* z, float* img);
+// DCT sensitivity probe (codes [BW * BH][C], gains optional) of the MLP w on the decode buffer z.
+void launch_dct_probe(cudaStream_t s, const DevModel& m, const float* w, const float* z, int BW, int BH, int C, uint8_t* code, float* gain);
 
 // ---- latent ES and selector search (kernels_latent.cu) ----
 void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevModel& m, unsigned active_mask, long long nz, float* eps);

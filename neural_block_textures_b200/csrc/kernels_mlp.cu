@@ -412,6 +412,52 @@ void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w,
     NTCB_CHECK(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ DCT sensitivity probe
+// dct_probe_codes (main.cpp:1002-1030), one thread per (8x8 block, level-0 channel): at the 4 pixels
+// (8 bx + {2, 5}, 8 by + {2, 5}) the features of the decode buffer with channel c set to -1, -0.5, 0, 0.5, 1
+// go through the MLP; each of the 4 segments contributes g^2 with g = (255 / 16) sqrt(sum_o cw[o] d_o^2 / wsum)
+// in double; the block gain is sqrt(sum / 16) and the code lround(log2(gain / floor) / 0.6) clamped to
+// [0, 15] (dct_code_of_gain, main.cpp:981-985). The reference runs it on the host between steps; it is an
+// estimate there too (its comment: a CPU and a --cuda run may differ on a code boundary).
+__global__ void k_dct_probe(DevModel m, const float* __restrict__ wg, const float* __restrict__ z, int BW, int BH, int C,
+                            uint8_t* __restrict__ code, float* __restrict__ gain) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)BW * BH * C) return;
+    const int c = (int)(i % C);
+    const long long b = i / C;
+    const int bx = (int)(b % BW), by = (int)(b / BW);
+    const int P[2] = {2, 5};
+    const float SJ[5] = {-1.0f, -0.5f, 0.0f, 0.5f, 1.0f};
+    double acc = 0.0;
+    for (int qy = 0; qy < 2; qy++)
+        for (int qx = 0; qx < 2; qx++) {
+            float f[kMaxIn], out[5][kMaxOut];
+            pixel_features(m, z, bx * 8 + P[qx], by * 8 + P[qy], f);
+            for (int j = 0; j < 5; j++) { f[c] = SJ[j]; generic_forward(m, wg, f, out[j]); }
+            for (int j = 0; j < 4; j++) {
+                double ss = 0.0;
+                for (int o = 0; o < m.nout; o++) {
+                    const double d = (double)out[j + 1][o] - (double)out[j][o];
+                    ss += (double)m.cw[o] * d * d;
+                }
+                const double g = (255.0 / 16.0) * sqrt(ss / (double)m.wsum);
+                acc += g * g;
+            }
+        }
+    const double gb = sqrt(acc / 16.0);
+    const double floor_g = 14.0 / 64.0;
+    const double gg = gb > floor_g ? gb : floor_g;
+    const long long k = llround(log2(gg / floor_g) / 0.6);
+    code[i] = (uint8_t)(k < 0 ? 0 : (k > 15 ? 15 : k));
+    if (gain) gain[i] = (float)gb;
+}
+void launch_dct_probe(cudaStream_t s, const DevModel& m, const float* w, const float* z, int BW, int BH, int C, uint8_t* code, float* gain) {
+    const long long n = (long long)BW * BH * C;
+    if (n <= 0) return;
+    k_dct_probe<<<blocks_for(n, 128), 128, 0, s>>>(m, w, z, BW, BH, C, code, gain);
+    NTCB_CHECK(cudaGetLastError());
+}
+
 }  // namespace ntcb
 
 namespace ntcb {

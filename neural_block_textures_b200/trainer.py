@@ -178,6 +178,14 @@ class Trainer:
     def launch_count(self) -> int:
         return int(self.lib.ntcb_launch_count(self.h))
 
+    def dct_probe(self) -> tuple[np.ndarray, np.ndarray]:
+        """Device DCT sensitivity probe: (codes uint8, gains float32), [block raster][level-0 channel]."""
+        n = self.lib.ntcb_dct_probe(self.h, None, None, 0)
+        codes = np.zeros(n, np.uint8)
+        gains = np.zeros(n, np.float32)
+        self.lib.ntcb_dct_probe(self.h, codes.ctypes.data_as(C.POINTER(C.c_uint8)), _ptr(gains, C.c_float), n)
+        return codes, gains
+
     def set_pop_kernel(self, tensor: bool) -> None:
         """True: ES pairs on the tensor-core (3xTF32) kernel; False: the bit-exact packed-FP32 kernel."""
         self.lib.ntcb_set_pop_kernel(self.h, 1 if tensor else 0)

@@ -337,6 +337,17 @@ class RefSession:
     def psnr_of_decode(self, img):
         return self.lib.ref_psnr_of_decode(C.c_void_p(self.h), f32p(img))
 
+    def dct_probe_codes(self, q, dc_step: int = 4):
+        """The reference's own host probe: turn on the DCT-coded level 0 (ref_dct_enable), fit the scale codes
+        on the current model and decode buffer (Decoder::dct_fit_all), return the codes [block][channel]."""
+        qa = np.ascontiguousarray(q, np.int32)
+        self.lib.ref_dct_enable(C.c_void_p(self.h), qa.ctypes.data_as(_ip), dc_step, 0, C.c_float(0.0), 0, 0, C.c_float(0.0))
+        self.lib.ref_dct_fit(C.c_void_p(self.h), 1)
+        n = (self.spec.W // 8) * (self.spec.H // 8) * self.spec.levels[0].C
+        code = np.zeros(n, np.uint8)
+        self.lib.ref_dct_state(C.c_void_p(self.h), None, code.ctypes.data_as(C.POINTER(C.c_uint8)), None, None, None, None, None, None, None)
+        return code
+
     def zdec(self):
         z = np.zeros(self.spec.nz, np.float32)
         self.lib.ref_get_zdec(C.c_void_p(self.h), z.ctypes.data_as(_fp))

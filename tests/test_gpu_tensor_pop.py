@@ -102,3 +102,20 @@ def test_tensor_latent_gradient_tracks_exact(name, cuda_device):
     rms = np.sqrt(np.mean(g[False] ** 2))
     assert rms > 0
     assert np.abs(g[True] - g[False]).max() < 1e-4 * rms
+
+
+@pytest.mark.parametrize("tensor", [True, False])
+def test_population_beyond_65535_candidates(tensor, cuda_device):
+    """40000 pairs = 80000 candidates (the reference's (16, 2N) grid would overflow gridDim.y at 65536): the
+    last pairs' fitness against the oracle on the same batch and noise."""
+    N, M, it = 40000, 128, 3
+    spec = dataclasses.replace(spec_named("cfg2"), max_pairs=N, max_batch=M)
+    tgt = target_for(spec)
+    tr, z, p = _trainer(spec, tgt)
+    lp, lm, bidx = _fitness(tr, tensor, it, N, M)
+    tr.close()
+    assert lp.shape == (N,) and np.all(lp > 0) and np.all(lm > 0)
+    orc = Oracle(spec, tgt)
+    tail = 8
+    olp, olm = orc.es_fitness(p, z, spec.seed, it, SIGMA, N - tail, tail, bidx)
+    assert rel_err(lp[-tail:], olp) < FIT_RTOL and rel_err(lm[-tail:], olm) < FIT_RTOL
