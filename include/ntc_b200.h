@@ -168,6 +168,8 @@ double ntcb_fp32_peak_tflops(void);
  * would otherwise download the model and decode on the host. Not strict FP, like the host probe: codes can
  * differ from a host run where a gain lies on a code boundary. No counterpart in the reference. */
 size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap);
+/* The same for a drop-in C++ trainer: cpp_trainer points at an initialised ntc_cuda::Trainer. */
+size_t ntcb_cpp_dct_probe(void* cpp_trainer, uint8_t* codes, float* gains, size_t cap);
 /* Number of kernels this trainer has launched since creation. */
 long long ntcb_launch_count(const ntcb_trainer* t);
 /* Which kernels evaluate the ES decodes (mlp_step / ntcb_shard_mlp_eval pairs and the lat_step pass). tensor = 1

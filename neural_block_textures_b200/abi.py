@@ -113,6 +113,7 @@ SIGNATURES = {
     "ntcb_launch_count": (C.c_longlong, [_vp]),
     "ntcb_set_pop_kernel": (None, [_vp, C.c_int]),
     "ntcb_dct_probe": (C.c_size_t, [_vp, C.POINTER(C.c_uint8), _fp, C.c_size_t]),
+    "ntcb_cpp_dct_probe": (C.c_size_t, [_vp, C.POINTER(C.c_uint8), _fp, C.c_size_t]),
     "ntcb_pop_kernel": (C.c_int, [_vp]),
     "ntcb_fp32_peak_tflops": (C.c_double, []),
     "ntcb_footprint_ranges": (C.c_int, [C.c_int, C.c_int, C.c_int, _ip, _ip]),

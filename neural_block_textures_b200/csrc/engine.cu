@@ -867,8 +867,7 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
     I.totals.erase(it);
 }
 long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
-size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap) {
-    Impl& I = t->impl;
+static size_t dct_probe_impl(Impl& I, uint8_t* codes, float* gains, size_t cap) {
     require_ready(I); set_device(I);
     const int BW = I.d.W / 8, BH = I.d.H / 8, C = I.d.lv[0].C;
     const size_t n = (size_t)BW * BH * C;
@@ -882,6 +881,10 @@ size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap)
     sync(I);
     dfree(dc); dfree(dg);
     return n;
+}
+size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap) { return dct_probe_impl(t->impl, codes, gains, cap); }
+size_t ntcb_cpp_dct_probe(void* cpp_trainer, uint8_t* codes, float* gains, size_t cap) {
+    return dct_probe_impl(*static_cast<ntc_cuda::Trainer*>(cpp_trainer)->im, codes, gains, cap);
 }
 void ntcb_set_pop_kernel(ntcb_trainer* t, int tensor) { t->impl.tensor_pop = tensor != 0; }
 int ntcb_pop_kernel(const ntcb_trainer* t) { return (t->impl.tensor_pop && t->impl.shape != 0) ? 1 : 0; }
