@@ -43,8 +43,7 @@ namespace ntcb {
 namespace {
 
 constexpr int kTcRows = 128;                  // rows per tile (= TMEM lanes = threads of one stream)
-constexpr int kTcStreams = 4;                 // independent tile streams per CTA (one CTA per SM)
-constexpr int kTcTPB = kTcRows * kTcStreams;  // 512 threads, 16 warps
+constexpr int kTmemCols = 512;                // TMEM columns of an SM, all allocated by the one resident CTA
 constexpr uint32_t kTcWaitPolls = 4000;       // mbarrier polls (<= 1 ms each) before a wait is declared failed
 
 __host__ __device__ constexpr int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -74,9 +73,17 @@ struct TcShape {
     static constexpr int oB3h = round_up(ob2 + NOUTP, 4), oB3l = oB3h + N3 * K3;   // W2 as an MMA B operand
     static constexpr int SIGN = round_up(oB3l + N3 * K3, 32);
     // TMEM columns: D (layers 1 and 2), D3 (output layer), X hi / lo, H hi / lo
-    static constexpr int cD = 0, cD3 = 32, cXh = 48, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
-    static constexpr int NCOLS = 128;
-    static_assert(cHl + K2 <= NCOLS, "TMEM columns");
+    // The output layer runs on the tensor core for wide outputs (12: measured 1.33 vs 1.52 ms at config 3)
+    // and on the FP32 pipe for 3 outputs (0.86 vs 1.03 ms at config 2), where 16-wide MMAs are mostly padding.
+    static constexpr bool L3TC = S::NOUT > 4;
+    // TMEM columns of one stream: D (layers 1 and 2), D3 (tensor output layer only), X hi / lo, H hi / lo
+    static constexpr int cD = 0, cD3 = 32, cXh = L3TC ? 48 : 32, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
+    static constexpr int COLS = cHl + K2;
+    // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread;
+    // 4 streams is the floor the kernels were tuned at). Measured: 2 streams cost +33 % over 4.
+    static constexpr int STREAMS = kTmemCols / COLS >= 5 ? 5 : 4;
+    static constexpr int TPB = kTcRows * STREAMS;
+    static_assert(STREAMS * COLS <= kTmemCols, "TMEM columns");
 
     // Writes flat reference weight k (value w) to every place a kernel variant reads it from: MMA B operands
     // as hi / lo, biases and the row-major output layer as plain floats.
@@ -186,7 +193,7 @@ __device__ __forceinline__ void issue3(uint32_t d, uint32_t a_hi, uint32_t a_lo,
     __syncwarp();
 }
 
-// Named barrier over the 128 threads of one stream (ids 1..kTcStreams; 0 is __syncthreads), AND-reducing v.
+// Named barrier over the 128 threads of one stream (ids 1..STREAMS; 0 is __syncthreads), AND-reducing v.
 __device__ __forceinline__ bool stream_sync_and(int id, bool v) {
     uint32_t r;
     asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
@@ -212,13 +219,14 @@ __device__ __forceinline__ double stream_sum(double v, double* red4, int id) {
 // mostly share a pair and its weights are staged once. The streams interleave on the SM: one stream's
 // element-wise work overlaps the others' MMAs.
 template <class S, bool L3TC>
-__global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a, int chunks) {
+__global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, PopArgs a, int chunks) {
     using T = TcShape<S>;
-    extern __shared__ __align__(1024) float dyn[];   // [kTcStreams][2][T::SIGN]
-    __shared__ __align__(8) uint64_t bars[kTcStreams];
-    __shared__ __align__(8) uint64_t bars3[kTcStreams];   // output-layer commits (separate: see below)
+    constexpr int NS = T::STREAMS;
+    extern __shared__ __align__(1024) float dyn[];   // [NS][2][T::SIGN]
+    __shared__ __align__(8) uint64_t bars[NS];
+    __shared__ __align__(8) uint64_t bars3[NS];   // output-layer commits (separate: see below)
     __shared__ uint32_t tbase;
-    __shared__ double red[kTcStreams][4];
+    __shared__ double red[NS][4];
     const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
     const int bar_id = 1 + g;
     float* sw = dyn + g * 2 * T::SIGN;
@@ -228,14 +236,14 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
     // then wait for a phase nobody completes); with their own barrier, commits and waits alternate on each.
     uint64_t* bar3 = &bars3[g];
 
-    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, 128 * kTcStreams);
+    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, kTmemCols);
     if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init(bar3, 1); tc::mbar_init_fence(); }
-    for (int i = threadIdx.x; i < kTcStreams * 2 * T::SIGN; i += kTcTPB) dyn[i] = 0.0f;   // padding stays zero
+    for (int i = threadIdx.x; i < NS * 2 * T::SIGN; i += T::TPB) dyn[i] = 0.0f;   // padding stays zero
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
 
-    const uint32_t tb = tbase + 128u * (uint32_t)g;
+    const uint32_t tb = tbase + (uint32_t)(T::COLS * g);
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
     const uint32_t sb0 = tc::smem_addr(sw), sb1 = sb0 + (uint32_t)(T::SIGN * 4);
     const float leak = m.leak;
@@ -268,7 +276,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
         store_split<T::K1>(trow, T::cXh, T::cXl, x);
     };
     const long long items = (long long)a.ncand * chunks;
-    const long long nstreams = (long long)gridDim.x * kTcStreams, gs = (long long)blockIdx.x * kTcStreams + g;
+    const long long nstreams = (long long)gridDim.x * T::STREAMS, gs = (long long)blockIdx.x * T::STREAMS + g;
     const long long i0 = gs * items / nstreams, i1 = (gs + 1) * items / nstreams;
     int cur = -1;
 #pragma unroll 1
@@ -411,18 +419,16 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_pop_eval_tc(DevModel m, PopArgs a
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, 128 * kTcStreams); }
+    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, kTmemCols); }
 }
 
 template <class S>
 void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
     using T = TcShape<S>;
     const int chunks = pop_chunks(a.M, a.chunk);
-    const size_t smem = (size_t)kTcStreams * 2 * T::SIGN * sizeof(float);
+    const size_t smem = (size_t)T::STREAMS * 2 * T::SIGN * sizeof(float);
     static int nsm = 0;
-    // The output layer runs on the tensor core for wide outputs (12: measured 1.33 vs 1.52 ms at config 3)
-    // and on the FP32 pipe for 3 outputs (0.86 vs 1.03 ms at config 2), where 16-wide MMAs are mostly padding.
-    constexpr bool kL3TC = S::NOUT > 4;
+    constexpr bool kL3TC = T::L3TC;
     if (nsm == 0) {
         int dev = 0;
         NTCB_CHECK(cudaGetDevice(&dev));
@@ -430,8 +436,8 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
         NTCB_CHECK(cudaFuncSetAttribute(k_pop_eval_tc<S, kL3TC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     }
     const long long items = (long long)a.ncand * chunks;
-    const int grid = (int)std::min<long long>(nsm, (items + kTcStreams - 1) / kTcStreams);
-    k_pop_eval_tc<S, kL3TC><<<grid, kTcTPB, smem, s>>>(m, a, chunks);
+    const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
+    k_pop_eval_tc<S, kL3TC><<<grid, T::TPB, smem, s>>>(m, a, chunks);
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -445,30 +451,30 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
 // share their taps and are gathered together, one item ahead, while the layer-2 MMAs of the current item
 // run). The output layer runs on the FP32 pipe.
 template <class S>
-__global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
+__global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                          const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
                                                          int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
                                                          long long p_begin, long long p_end, long long pstride,
                                                          int* __restrict__ err) {
     using T = TcShape<S>;
     extern __shared__ __align__(1024) float sw[];   // one weight set [T::SIGN]
-    __shared__ __align__(8) uint64_t bars[kTcStreams];
+    __shared__ __align__(8) uint64_t bars[T::STREAMS];
     __shared__ uint32_t tbase;
     const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
     const int bar_id = 1 + g;
     uint64_t* bar = &bars[g];
 
-    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, 128 * kTcStreams);
+    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, kTmemCols);
     if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
-    for (int i = threadIdx.x; i < T::SIGN; i += kTcTPB) sw[i] = 0.0f;
+    for (int i = threadIdx.x; i < T::SIGN; i += T::TPB) sw[i] = 0.0f;
     __syncthreads();
-    for (int k = threadIdx.x; k < m.P; k += kTcTPB) T::store(sw, k, wg[k]);
+    for (int k = threadIdx.x; k < m.P; k += T::TPB) T::store(sw, k, wg[k]);
     tc::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
 
-    const uint32_t tb = tbase + 128u * (uint32_t)g;
+    const uint32_t tb = tbase + (uint32_t)(T::COLS * g);
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
     const uint32_t sb = tc::smem_addr(sw);
     const float leak = m.leak;
@@ -485,7 +491,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const flo
     const long long npix = (long long)m.W * m.H;
     const long long ntiles = (p_end - p_begin + kTcRows - 1) / kTcRows;
     const long long items = (long long)K * ntiles;
-    const long long nstreams = (long long)gridDim.x * kTcStreams, gs = (long long)blockIdx.x * kTcStreams + g;
+    const long long nstreams = (long long)gridDim.x * T::STREAMS, gs = (long long)blockIdx.x * T::STREAMS + g;
     const long long i0 = gs * items / nstreams, i1 = (gs + 1) * items / nstreams;
 
     // +/- features and targets of this thread's pixel in an item
@@ -583,7 +589,7 @@ __global__ void __launch_bounds__(kTcTPB, 1) k_lat_eval_tc(DevModel m, const flo
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, 128 * kTcStreams); }
+    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, kTmemCols); }
 }
 
 template <class S>
@@ -600,8 +606,8 @@ void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const floa
         NTCB_CHECK(cudaFuncSetAttribute(k_lat_eval_tc<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     }
     const long long items = (long long)K * ((p_end - p_begin + kTcRows - 1) / kTcRows);
-    const int grid = (int)std::min<long long>(nsm, (items + kTcStreams - 1) / kTcStreams);
-    k_lat_eval_tc<S><<<grid, kTcTPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
+    const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
+    k_lat_eval_tc<S><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
 }
 
 }  // namespace
