@@ -364,6 +364,13 @@ def main():
     eval_ms, eval_n = tr.kernel_time("mlp_eval")
     lat_ms, lat_n = tr.kernel_time("lat_eval")
     qat_ms, qat_n = tr.kernel_time("qat")
+    # every other kernel class the library times (device time of this library's kernels; the rest of a step
+    # is collectives and idle gaps)
+    other = {}
+    for cls in ("batch", "noise", "mlp_finish", "mlp_grad", "lat_noise", "lat_gather", "dct_rate", "adam", "snap"):
+        ms_c, n_c = tr.kernel_time(cls)
+        if n_c:
+            other[cls] = ms_c / args.steps
     tr.kernel_timing(False)
     if dist:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -450,7 +457,8 @@ def main():
                        "pop_kernel": kernel,
                        "l2": "flushed between steps (256 MiB memset outside the timed events)"},
             "roofline": pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks),
-            "phase_ms_per_step": {"mlp_eval": eval_ms / args.steps, "lat_eval": lat_ms / args.steps, "qat": qat_ms / args.steps},
+            "phase_ms_per_step": {"mlp_eval": eval_ms / args.steps, "lat_eval": lat_ms / args.steps, "qat": qat_ms / args.steps,
+                                  **other, "kernels_total": (eval_ms + lat_ms + qat_ms) / args.steps + sum(other.values())},
             "e2e": {"value": e2e_value, "unit": "decodes/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
             "gpu_launches": launches,
