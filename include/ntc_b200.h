@@ -213,6 +213,16 @@ void ntcb_shard_fd_apply(ntcb_trainer* t, float h, float lr, const double* fit_a
  * identically on every rank. */
 void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* block_dev);
 void ntcb_shard_lat_apply(ntcb_trainer* t, int it, float sigma, float lr, int K, const float* blocks_dev, int rows_per_block);
+/* The latent ES step sharded by texel rows (one ES-trained level, no qes / DCT snap; ntcb_shard_lat_plan
+ * returns 0 otherwise, and the pixel-row pair above applies). plan receives {level, ta, tb, pa, pb, n}: rank
+ * `rank` of `world` owns texel rows [ta, tb) of the level, evaluates pixel rows [pa, pb) (its footprints: own
+ * rows plus a halo), gathers and Adam-updates only its texels, and ntcb_shard_lat_step_rows copies its n updated
+ * latent floats (rows [ta, tb), contiguous) into zblock_dev. After the caller all-gathers the blocks (rank order
+ * = row order) into the whole level, ntcb_shard_lat_install writes it on every rank. The latent is then
+ * bit-identical to the single-GPU step; each rank keeps the Adam moments of its own rows only. */
+int ntcb_shard_lat_plan(const ntcb_trainer* t, int world, int rank, long long* plan);
+void ntcb_shard_lat_step_rows(ntcb_trainer* t, int it, float sigma, float lr, int K, int world, int rank, float* zblock_dev);
+void ntcb_shard_lat_install(ntcb_trainer* t, int level, const float* level_dev);
 /* The selector search sharded by level-0 texel rows: a rank searches rows [trow_begin, trow_end) and copies
  * their level-0 values into level0_dev (a DEVICE buffer of the level's W * H * C floats, rows contiguous);
  * after the caller's all-gather, ntcb_shard_qat_apply installs the full level 0 on every rank. */

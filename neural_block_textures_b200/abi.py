@@ -123,6 +123,9 @@ SIGNATURES = {
     "ntcb_shard_es_block_bytes": (C.c_longlong, [_vp, C.c_int, C.c_int, C.c_int]),
     "ntcb_shard_mlp_eval_grad": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "ntcb_shard_mlp_apply_grad": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _vp, C.c_int]),
+    "ntcb_shard_lat_plan": (C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(C.c_longlong)]),
+    "ntcb_shard_lat_step_rows": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),
+    "ntcb_shard_lat_install": (None, [_vp, C.c_int, _vp]),
     "ntcb_shard_fd_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, _vp]),
     "ntcb_shard_fd_apply": (None, [_vp, C.c_float, C.c_float, _vp]),
     "ntcb_shard_mlp_eval": (None, [_vp, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),

@@ -620,7 +620,8 @@ void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix, in
             if (!(mask & (1u << l))) continue;
             const ntcb::RateTerm r = (l == 0) ? rt : ntcb::RateTerm{nullptr, 0.0f, 0, 0};
             timed(I, "lat_gather", 1, [&] {
-                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad, rows_per_block);
+                ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad, rows_per_block,
+                                        0, I.d.lv[l].H, 0);
             });
         }
     }
@@ -631,6 +632,25 @@ void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix, in
     });
     snap_latent_impl(I);
     I.lat_step_no++;
+}
+
+// Texel-row sharding of the latent step: with one ES-trained level and no qes / DCT snap (so the decode
+// buffer is the latent itself), rank r of G owns texel rows [ta, tb) = [r LH / G, (r + 1) LH / G) of that level
+// and evaluates the pixel rows [pa, pb) their footprints cover (its own rows plus a halo); it gathers and
+// Adam-updates only its texels, and the ranks exchange the updated level instead of the per-pixel planes.
+bool lat_rows_plan(const Impl& I, int world, int rank, int& lvl, int& ta, int& tb, int& pa, int& pb) {
+    const unsigned mask = lat_mask(I);
+    if (!mask || (mask & (mask - 1)) || I.qes || I.dct || world < 1 || rank < 0 || rank >= world) return false;
+    lvl = 0;
+    while (!(mask & (1u << lvl))) lvl++;
+    const auto& L = I.d.lv[lvl];
+    if (L.H % world) return false;
+    ta = rank * (L.H / world); tb = ta + L.H / world;
+    std::vector<int> yb, ye;
+    if (!axis_ranges(I.d.H, L.H, L.nearest, yb, ye)) return false;
+    pa = I.d.H; pb = 0;
+    for (int t = ta; t < tb; t++) { pa = std::min(pa, yb[t]); pb = std::max(pb, ye[t]); }
+    return pb > pa;
 }
 
 void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
@@ -883,6 +903,48 @@ static size_t dct_probe_impl(Impl& I, uint8_t* codes, float* gains, size_t cap) 
     return n;
 }
 size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap) { return dct_probe_impl(t->impl, codes, gains, cap); }
+int ntcb_shard_lat_plan(const ntcb_trainer* t, int world, int rank, long long* plan) {
+    const Impl& I = t->impl;
+    int lvl, ta, tb, pa, pb;
+    if (!I.ready || !lat_rows_plan(I, world, rank, lvl, ta, tb, pa, pb)) return 0;
+    if (plan) {
+        plan[0] = lvl; plan[1] = ta; plan[2] = tb; plan[3] = pa; plan[4] = pb;
+        plan[5] = (long long)(tb - ta) * I.d.lv[lvl].W * I.d.lv[lvl].C;
+    }
+    return 1;
+}
+void ntcb_shard_lat_step_rows(ntcb_trainer* t, int it, float sigma, float lr, int K, int world, int rank, float* zblock_dev) {
+    (void)it;
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    int lvl, ta, tb, pa, pb;
+    if (K < 1 || !lat_rows_plan(I, world, rank, lvl, ta, tb, pa, pb)) die("shard_lat_step_rows: the texel-row plan does not apply");
+    const auto& L = I.d.lv[lvl];
+    ensure_lat(I, K);
+    const long long W = I.d.W;
+    lat_eval_part(I, sigma, K, (long long)pa * W, (long long)pb * W, I.dpix, (long long)(pb - pa) * W);
+    const long long off = (long long)L.off + (long long)ta * L.W * L.C, n = (long long)(tb - ta) * L.W * L.C;
+    NTCB_CHECK(cudaMemsetAsync(I.zgrad + off, 0, n * sizeof(float), I.stream));
+    const float scale = 1.0f / (2.0f * (float)K * sigma);
+    timed(I, "lat_gather", 1, [&] {
+        ntcb::launch_lat_gather(I.stream, I.dm, lvl, I.lvl_xr[lvl], I.lvl_yr[lvl], I.dpix, I.lat_eps, I.nz, K, scale,
+                                ntcb::RateTerm{nullptr, 0.0f, 0, 0}, I.zgrad, pb - pa, ta, tb, pa);
+    });
+    timed(I, "adam", 1, [&] {
+        I.lat_t++;
+        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
+        ntcb::launch_adam(I.stream, I.z + off, I.zgrad + off, I.zm + off, I.zv + off, n, lr, c1, c2);
+    });
+    I.lat_step_no++;
+    NTCB_CHECK(cudaMemcpyAsync(zblock_dev, I.z + off, n * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+}
+void ntcb_shard_lat_install(ntcb_trainer* t, int level, const float* level_dev) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (level < 0 || level >= I.d.nlev) die("shard_lat_install: bad level");
+    const auto& L = I.d.lv[level];
+    NTCB_CHECK(cudaMemcpyAsync(I.z + L.off, level_dev, (size_t)L.W * L.H * L.C * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+}
 size_t ntcb_cpp_dct_probe(void* cpp_trainer, uint8_t* codes, float* gains, size_t cap) {
     return dct_probe_impl(*static_cast<ntc_cuda::Trainer*>(cpp_trainer)->im, codes, gains, cap);
 }

@@ -78,10 +78,11 @@ struct RateTerm {              // DCT rate term of the latent gradient (level 0)
     float rate_scale;
     int BW, C;
 };
-// dpix: blocks of rows_per_block image rows, each block [K][rows_per_block * W] (one block = the plain [K][W * H]).
+// Texel rows [ty0, ty1) of the level. dpix: blocks of rows_per_block image rows starting at image row row_base,
+// each block [K][rows_per_block * W] (one block from row 0 = the plain [K][W * H]).
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
-                       int rows_per_block);
+                       int rows_per_block, int ty0, int ty1, int row_base);
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
                 const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end,
                 int max_bits);

@@ -129,10 +129,10 @@ void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* 
 // (dct_rate_pass, main.cpp:1935-1958).
 __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, const int* __restrict__ yr, const float* __restrict__ dpix,
                              const float* __restrict__ eps, long long nz, int K, float scale, RateTerm rate, float* __restrict__ grad,
-                             int rpb) {
+                             int rpb, int ty0, int ty1, int row_base) {
     const DevLevel& L = m.lv[level];
-    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= (long long)L.W * L.H) return;
+    const long long t = (long long)ty0 * L.W + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (long long)ty1 * L.W) return;
     const int tx = (int)(t % L.W), ty = (int)(t / L.W);
     const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
     const long long base = L.off + t * L.C;
@@ -140,7 +140,8 @@ __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, 
     for (int k = 0; k < K; k++) {
         float d = 0.0f;
         for (int py = y0; py < y1; py++) {
-            const float* row = dpix + (py / rpb) * block + k * plane + (long long)(py % rpb) * m.W;
+            const int pr = py - row_base;
+            const float* row = dpix + (pr / rpb) * block + k * plane + (long long)(pr % rpb) * m.W;
             for (int px = x0; px < x1; px++) d += row[px];
         }
         const float w = d * scale;
@@ -157,9 +158,11 @@ __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, 
 
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
-                       int rows_per_block) {
-    const long long ntx = (long long)m.lv[level].W * m.lv[level].H;
-    k_lat_gather<<<blocks_for(ntx, 128), 128, 0, s>>>(m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block);
+                       int rows_per_block, int ty0, int ty1, int row_base) {
+    const long long ntx = (long long)m.lv[level].W * (ty1 - ty0);
+    if (ntx <= 0) return;
+    k_lat_gather<<<blocks_for(ntx, 128), 128, 0, s>>>(m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block, ty0, ty1,
+                                                      row_base);
     NTCB_CHECK(cudaGetLastError());
 }
 

@@ -13,6 +13,10 @@
   B = ceil(P / G) (every rank also evaluates the unperturbed stats pair); one all-gather of the padded
   [G][B] fitness pairs leaves all P weights' (L+, L-) in weight order at the front, and every rank runs the
   identical FD gradient and Adam.
+* Latent ES step, texel rows (one ES-trained level, no qes / DCT): rank r owns texel rows [r LH / G, (r + 1)
+  LH / G) of the level, evaluates the pixel rows their footprints cover, gathers and Adam-updates only its own
+  texels; one all-gather of the updated rows installs the whole level everywhere. This replaces the per-pixel
+  planes (K W H floats) on the wire by the level (LW LH C floats) and shards the gather and Adam too.
 * Selector search — level-0 texel rows: rank r searches rows [r LH / G, (r + 1) LH / G) (texels are
   independent); one all-gather of the level installs every rank's result everywhere.
 
@@ -78,6 +82,14 @@ class ShardedES:
             self.dblock = torch.zeros(K * self.rows * W, dtype=torch.float32, device=device)
             self.dpix = torch.zeros(self.world * K * self.rows * W, dtype=torch.float32, device=device)
             self.K = K
+        self.lat_rows = None
+        if image is not None and K > 0 and hasattr(trainer, "shard_lat_plan"):
+            plan = trainer.shard_lat_plan(self.world, self.rank)
+            if plan is not None:
+                self.lat_rows = plan
+                n = plan[5]
+                self.zblock = torch.zeros(n, dtype=torch.float32, device=device)
+                self.zlevel = torch.zeros(n * self.world, dtype=torch.float32, device=device)
         self.l0 = None
         if level0 is not None:
             LW, LH, LC = level0
@@ -120,6 +132,12 @@ class ShardedES:
     def lat_step(self, it: int, sigma: float, lr: float, K: int) -> None:
         """One latent ES step (lat_step)."""
         assert self.dpix is not None and K == self.K
+        if self.lat_rows is not None:
+            self.t.shard_lat_step_rows(it, sigma, lr, K, self.world, self.rank, self.zblock)
+            with self._ctx():
+                self.dist.all_gather_into_tensor(self.zlevel, self.zblock)
+            self.t.shard_lat_install(self.lat_rows[0], self.zlevel)
+            return
         self.t.shard_lat_eval(sigma, K, self.r0, self.r1, self.dblock)
         with self._ctx():
             self.dist.all_gather_into_tensor(self.dpix, self.dblock)

@@ -213,6 +213,19 @@ class Trainer:
     def shard_mlp_apply_grad(self, it: int, sigma: float, lr: float, N: int, M: int, blocks_dev, world: int) -> None:
         self.lib.ntcb_shard_mlp_apply_grad(self.h, it, sigma, lr, N, M, C.c_void_p(_dptr(blocks_dev)), world)
 
+    def shard_lat_plan(self, world: int, rank: int):
+        """(level, ta, tb, pa, pb, n) of the texel-row latent sharding, or None when it does not apply."""
+        plan = (C.c_longlong * 6)()
+        if not self.lib.ntcb_shard_lat_plan(self.h, world, rank, plan):
+            return None
+        return tuple(int(v) for v in plan)
+
+    def shard_lat_step_rows(self, it: int, sigma: float, lr: float, K: int, world: int, rank: int, zblock_dev) -> None:
+        self.lib.ntcb_shard_lat_step_rows(self.h, it, sigma, lr, K, world, rank, C.c_void_p(_dptr(zblock_dev)))
+
+    def shard_lat_install(self, level: int, level_dev) -> None:
+        self.lib.ntcb_shard_lat_install(self.h, level, C.c_void_p(_dptr(level_dev)))
+
     def shard_fd_eval(self, it: int, h: float, M: int, j_begin: int, j_end: int, fit_dev) -> None:
         """fit_dev: device buffer of >= 2 * (j_end - j_begin) doubles; receives (L+, L-) of weights [j_begin, j_end)."""
         self.lib.ntcb_shard_fd_eval(self.h, it, h, M, j_begin, j_end, C.c_void_p(_dptr(fit_dev)))

@@ -119,3 +119,33 @@ def test_population_beyond_65535_candidates(tensor, cuda_device):
     tail = 8
     olp, olm = orc.es_fitness(p, z, spec.seed, it, SIGMA, N - tail, tail, bidx)
     assert rel_err(lp[-tail:], olp) < FIT_RTOL and rel_err(lm[-tail:], olm) < FIT_RTOL
+
+
+@pytest.mark.parametrize("tensor", [True, False])
+@pytest.mark.parametrize("N,M", [(1, 1), (1, 129), (3, 7)])
+def test_tiny_populations_and_batches(tensor, N, M, cuda_device):
+    """One pair / one row and other sizes below a tile: both kernels against the oracle."""
+    spec = dataclasses.replace(spec_named("cfg2"), max_pairs=8)
+    tgt = target_for(spec)
+    tr, z, p = _trainer(spec, tgt)
+    lp, lm, bidx = _fitness(tr, tensor, 5, N, M)
+    tr.close()
+    assert lp.shape == (N,)
+    olp, olm = Oracle(spec, tgt).es_fitness(p, z, spec.seed, 5, SIGMA, 0, N, bidx)
+    assert rel_err(lp, olp) < FIT_RTOL and rel_err(lm, olm) < FIT_RTOL
+
+
+@pytest.mark.parametrize("tensor", [True, False])
+def test_single_latent_pair(tensor, cuda_device):
+    """K = 1: the latent gradient of one antithetic pair, tensor-core and exact passes against each other."""
+    spec = spec_named("cfg5")
+    tgt = target_for(spec)
+    g = {}
+    for t in (tensor, False):
+        tr, z, p = _trainer(spec, tgt)
+        tr.set_pop_kernel(t)
+        tr.lat_step(1, 0.05, 0.0, 1)
+        g[t] = tr.debug_last_zgrad().astype(np.float64)
+        tr.close()
+    rms = np.sqrt(np.mean(g[False] ** 2))
+    assert rms > 0 and np.abs(g[tensor] - g[False]).max() < 1e-4 * rms

@@ -188,3 +188,50 @@ def test_two_gloo_ranks_match_single_process(tmp_path):
         ev.shard_mlp_apply(it, SIGMA, LR, N, M, fit)
     assert np.array_equal(p0, ev.p), "sharded == single process"
     assert not np.array_equal(p0, spec_named("cfg2").init_params()[1])
+
+
+class RowsTrainer:
+    """The texel-row latent exchange: each rank fills its own rows of a 12 x 8 x 2 level; install records the level."""
+    LW, LH, LC, K = 12, 8, 2, 3
+
+    def shard_lat_plan(self, world, rank):
+        ta, tb = rank * self.LH // world, (rank + 1) * self.LH // world
+        return (1, ta, tb, 0, 0, (tb - ta) * self.LW * self.LC)
+
+    def shard_lat_step_rows(self, it, sigma, lr, K, world, rank, zblock):
+        _, ta, tb, _, _, n = self.shard_lat_plan(world, rank)
+        base = ta * self.LW * self.LC
+        for i in range(n):
+            zblock[i] = 0.5 * (base + i)
+
+    def shard_lat_install(self, level, level_all):
+        self.level = (level, level_all.clone())
+
+
+def _rows_main(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        t = RowsTrainer()
+        es = ShardedES(t, dist, 4, device="cpu", K=t.K, image=(16, 16))
+        assert es.lat_rows is not None
+        es.lat_step(1, 0.05, 0.0, t.K)
+        assert t.level[0] == 1
+        np.save(os.path.join(out_dir, f"z{rank}.npy"), t.level[1].numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_latent_texel_row_sharding_plumbing(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rows_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    T = RowsTrainer
+    want = np.array([0.5 * i for i in range(T.LW * T.LH * T.LC)], np.float32)
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"z{r}.npy"), want)
