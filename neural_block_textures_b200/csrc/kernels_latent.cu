@@ -127,24 +127,40 @@ void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* 
 // reference's scatter adds them in; then grad[t, c] += (d * scale) * eps[k][t, c], pairs in order. When
 // the DCT rate term is on (level 0), pair k's rate contribution follows its mse contribution
 // (dct_rate_pass, main.cpp:1935-1958).
+// Up to 32 texels per CTA (fewer for many pairs, to fit the sums in 48 KB of shared memory): first one thread
+// per (texel, pair) sums that pair's dpix over the texel's footprint in
+// raster order (each sum stays one sequential float chain, so the values are unchanged), then one thread per
+// texel applies the pairs' updates in pair order. The footprint sums are latency-bound loads, so spreading
+// them over the pairs' threads is what sets the speed.
 __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, const int* __restrict__ yr, const float* __restrict__ dpix,
                              const float* __restrict__ eps, long long nz, int K, float scale, RateTerm rate, float* __restrict__ grad,
-                             int rpb, int ty0, int ty1, int row_base) {
+                             int rpb, int ty0, int ty1, int row_base, int tpc) {
+    extern __shared__ float dsum[];   // [tpc][K]
     const DevLevel& L = m.lv[level];
-    const long long t = (long long)ty0 * L.W + (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= (long long)ty1 * L.W) return;
-    const int tx = (int)(t % L.W), ty = (int)(t / L.W);
-    const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
-    const long long base = L.off + t * L.C;
+    const long long t0 = (long long)ty0 * L.W + (long long)blockIdx.x * tpc;
+    const long long t_end = (long long)ty1 * L.W;
     const long long plane = (long long)rpb * m.W, block = (long long)K * plane;
-    for (int k = 0; k < K; k++) {
+    for (int j = threadIdx.x; j < tpc * K; j += blockDim.x) {
+        const int tl = j % tpc, k = j / tpc;
+        const long long t = t0 + tl;
+        if (t >= t_end) continue;
+        const int tx = (int)(t % L.W), ty = (int)(t / L.W);
+        const int x0 = xr[tx], x1 = xr[L.W + tx], y0 = yr[ty], y1 = yr[L.H + ty];
         float d = 0.0f;
         for (int py = y0; py < y1; py++) {
             const int pr = py - row_base;
             const float* row = dpix + (pr / rpb) * block + k * plane + (long long)(pr % rpb) * m.W;
             for (int px = x0; px < x1; px++) d += row[px];
         }
-        const float w = d * scale;
+        dsum[tl * K + k] = d;
+    }
+    __syncthreads();
+    const long long t = t0 + threadIdx.x;
+    if ((int)threadIdx.x >= tpc || t >= t_end) return;
+    const int tx = (int)(t % L.W), ty = (int)(t / L.W);
+    const long long base = L.off + t * L.C;
+    for (int k = 0; k < K; k++) {
+        const float w = dsum[threadIdx.x * K + k] * scale;
         const float* ek = eps + (long long)k * nz;
         for (int c = 0; c < L.C; c++) grad[base + c] = fmaf(w, ek[base + c], grad[base + c]);
         if (rate.dbits) {
@@ -161,8 +177,9 @@ void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* 
                        int rows_per_block, int ty0, int ty1, int row_base) {
     const long long ntx = (long long)m.lv[level].W * (ty1 - ty0);
     if (ntx <= 0) return;
-    k_lat_gather<<<blocks_for(ntx, 128), 128, 0, s>>>(m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block, ty0, ty1,
-                                                      row_base);
+    const int tpc = std::max(1, std::min(32, 12288 / std::max(1, K)));
+    k_lat_gather<<<blocks_for(ntx, tpc), 128, (size_t)tpc * K * sizeof(float), s>>>(
+        m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block, ty0, ty1, row_base, tpc);
     NTCB_CHECK(cudaGetLastError());
 }
 
