@@ -170,6 +170,36 @@ double ntcb_fp32_peak_tflops(void);
 size_t ntcb_dct_probe(ntcb_trainer* t, uint8_t* codes, float* gains, size_t cap);
 /* The same for a drop-in C++ trainer: cpp_trainer points at an initialised ntc_cuda::Trainer. */
 size_t ntcb_cpp_dct_probe(void* cpp_trainer, uint8_t* codes, float* gains, size_t cap);
+
+#define NTCB_MAX_T (NTCB_MAX_OUT / 3)
+/* The figures of the reference trainer's progress print (main.cpp:4155-4205), computed on the device. */
+typedef struct ntcb_progress_stats {
+    /* mse_of (main.cpp:1764-1788) of the decode of the current latent, and of the decode of the quantized copy
+       (the print's recon and recon_q): weighted, and per texture */
+    double mse, mse_tex[NTCB_MAX_T];
+    double mse_q, mse_q_tex[NTCB_MAX_T];
+    /* bitrate_stats (main.cpp:2272-2352) as the progress print calls it: the order-0 entropy of level 0 stands
+       in for its context-model figure (g_ctx_stats off), so bpp_q8_ctx and bpp_ctx_level0 carry that */
+    double bpp_fp32, bpp_q8, bpp_q8_ent, bpp_q8_ctx, bpp_ctx_level0, bpp_est, bits_mlp, bits_raw_latent, bits_header;
+    /* latent_stats (main.cpp:2212-2217) of each level's training values */
+    float lat_mean[NTCB_MAX_LEVELS], lat_sd[NTCB_MAX_LEVELS], lat_max[NTCB_MAX_LEVELS];
+    /* --qat: level-0 training values off their channel's grid (main.cpp:4196-4200); 0 without --qat */
+    long long qat_off_grid;
+    /* 1 when level 0 is DCT-coded (set_dct): its bits are left out of every figure above and its quantized copy is
+       the snapped plane; the caller adds its bit simulator's totals (dct_analyze, main.cpp:1080) as bitrate_stats
+       does at main.cpp:2294-2301 */
+    int level0_dct;
+} ntcb_progress_stats;
+/* The progress print's statistics for the current model (main.cpp:4155-4205) without downloading it:
+ * level_bits[l] = the post-hoc depth of each continuous level (bitrate_stats' lbits, main.cpp:2288; ignored for
+ * the --qat level 0 and for live --qes levels, whose depths the trainer holds), eval_w x eval_h = the evaluation
+ * extent of mse_of (0 = the whole image). zq (host, nz floats, may be null) receives the quantized copy
+ * bitrate_stats returns (zpost). Returns 0, or -1 when a depth is outside 1..16. Leaves the model unchanged; uses
+ * the decode buffer of decode_full. No counterpart in the reference, whose print downloads the model and runs
+ * these on the host. */
+int ntcb_print_stats(ntcb_trainer* t, const int* level_bits, int eval_w, int eval_h, float* zq, ntcb_progress_stats* out);
+/* The same for a drop-in C++ trainer: cpp_trainer points at an initialised ntc_cuda::Trainer. */
+int ntcb_cpp_print_stats(void* cpp_trainer, const int* level_bits, int eval_w, int eval_h, float* zq, ntcb_progress_stats* out);
 /* Number of kernels this trainer has launched since creation. */
 long long ntcb_launch_count(const ntcb_trainer* t);
 /* Which kernels evaluate the ES decodes (mlp_step / ntcb_shard_mlp_eval pairs and the lat_step pass). tensor = 1

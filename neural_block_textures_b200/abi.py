@@ -73,6 +73,20 @@ class DctDesc(C.Structure):
     ]
 
 
+class ProgressStats(C.Structure):
+    """ntcb_progress_stats: the progress print's figures (main.cpp:4155-4205)."""
+    _fields_ = [
+        ("mse", C.c_double), ("mse_tex", C.c_double * (MAX_OUT // 3)),
+        ("mse_q", C.c_double), ("mse_q_tex", C.c_double * (MAX_OUT // 3)),
+        ("bpp_fp32", C.c_double), ("bpp_q8", C.c_double), ("bpp_q8_ent", C.c_double), ("bpp_q8_ctx", C.c_double),
+        ("bpp_ctx_level0", C.c_double), ("bpp_est", C.c_double), ("bits_mlp", C.c_double),
+        ("bits_raw_latent", C.c_double), ("bits_header", C.c_double),
+        ("lat_mean", C.c_float * MAX_LEVELS), ("lat_sd", C.c_float * MAX_LEVELS), ("lat_max", C.c_float * MAX_LEVELS),
+        ("qat_off_grid", C.c_longlong),
+        ("level0_dct", C.c_int),
+    ]
+
+
 _fp = C.POINTER(C.c_float)
 _dp = C.POINTER(C.c_double)
 _ip = C.POINTER(C.c_int)
@@ -114,6 +128,8 @@ SIGNATURES = {
     "ntcb_set_pop_kernel": (None, [_vp, C.c_int]),
     "ntcb_dct_probe": (C.c_size_t, [_vp, C.POINTER(C.c_uint8), _fp, C.c_size_t]),
     "ntcb_cpp_dct_probe": (C.c_size_t, [_vp, C.POINTER(C.c_uint8), _fp, C.c_size_t]),
+    "ntcb_print_stats": (C.c_int, [_vp, C.POINTER(C.c_int), C.c_int, C.c_int, _fp, C.POINTER(ProgressStats)]),
+    "ntcb_cpp_print_stats": (C.c_int, [_vp, C.POINTER(C.c_int), C.c_int, C.c_int, _fp, C.POINTER(ProgressStats)]),
     "ntcb_pop_kernel": (C.c_int, [_vp]),
     "ntcb_fp32_peak_tflops": (C.c_double, []),
     "ntcb_footprint_ranges": (C.c_int, [C.c_int, C.c_int, C.c_int, _ip, _ip]),

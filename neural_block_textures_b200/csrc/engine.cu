@@ -80,6 +80,9 @@ struct Trainer::Impl {
     int* tc_err = nullptr;   // device flag the tensor-core kernel sets when an MMA completion wait times out
     float* gpart = nullptr; long long gpart_cap = 0;
     float* qat_grid = nullptr; int* qat_bits = nullptr;
+    // progress-print statistics: the last set_qes description (host copy) and a device scratch buffer
+    ntc_cuda::QesDesc qes_host{};
+    char* stats_buf = nullptr; size_t stats_cap = 0;
     // counters
     int mlp_t = 0, lat_t = 0, lat_step_no = 0;
     int last_N = 0, last_M = 0, last_pairs = 0; bool last_fd = false;
@@ -250,7 +253,7 @@ void free_all(Impl& I) {
     dfree(I.w); dfree(I.wgrad); dfree(I.wm); dfree(I.wv); dfree(I.tgt); dfree(I.img);
     dfree(I.bidx); dfree(I.feat_t); dfree(I.tgt_t); dfree(I.mlp_eps); dfree(I.part);
     dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart); dfree(I.tc_err);
-    dfree(I.qat_grid); dfree(I.qat_bits);
+    dfree(I.qat_grid); dfree(I.qat_bits); dfree(I.stats_buf); I.stats_cap = 0;
     for (auto& p : I.pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     I.pending.clear();
     if (I.own_stream) { cudaStreamDestroy(I.own_stream); I.own_stream = nullptr; }
@@ -456,8 +459,9 @@ void draw_batch(Impl& I, int it, int M) {
     I.last_M = M;
 }
 
-// Evaluates the ES pairs [p0, p1) of step `it` on the current minibatch; writes (lp, lm) per pair to fit.
-void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* fit) {
+// Evaluates the ES pairs [p0, p1) of step `it` on the current minibatch; writes (lp, lm) per pair to fit, and
+// with `reduce` (the whole population on this trainer) dl and lsum as well.
+void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* fit, bool reduce = false) {
     const int n = p1 - p0;
     if (n <= 0) return;
     timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, p0, n, I.P, I.mlp_eps); });
@@ -471,7 +475,10 @@ void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* 
     timed(I, "mlp_eval", 1, [&] {
         if (!(I.tensor_pop && ntcb::launch_pop_eval_tc(I.stream, I.shape, I.dm, a))) ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a);
     });
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, n, chunks, 3.0 * (double)I.d.wsum * M, fit); });
+    timed(I, "mlp_finish", 1, [&] {
+        ntcb::launch_pop_finish(I.stream, I.part, n, chunks, 3.0 * (double)I.d.wsum * M, fit, reduce ? I.dl : nullptr,
+                                reduce ? I.lsum : nullptr);
+    });
 }
 
 // ES gradient from the fitness of all N pairs (pair order) and the Adam step on the weights.
@@ -479,9 +486,9 @@ void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* 
 // the reference's serial order, for small populations).
 int es_seglen(int N) { return N <= 256 ? N : 64; }
 
-void es_apply(Impl& I, int it, float sigma, float lr, int N, const double* fit_all, bool regenerate_noise) {
+void es_apply(Impl& I, int it, float sigma, float lr, int N, const double* fit_all, bool regenerate_noise, bool reduced = false) {
     if (regenerate_noise) timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, 0, N, I.P, I.mlp_eps); });
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit_all, N, I.dl, I.lsum); });
+    if (!reduced) timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit_all, N, I.dl, I.lsum); });
     const float scale = 1.0f / (2.0f * (float)N * sigma);
     const int seglen = es_seglen(N);
     const int nseg = (N + seglen - 1) / seglen;
@@ -502,8 +509,8 @@ void mlp_step_impl(Impl& I, int it, float sigma, float lr, int N, int M) {
         exit(1);
     }
     draw_batch(I, it, M);
-    es_eval_pairs(I, it, sigma, M, 0, N, I.fit);
-    es_apply(I, it, sigma, lr, N, I.fit, false);
+    es_eval_pairs(I, it, sigma, M, 0, N, I.fit, true);
+    es_apply(I, it, sigma, lr, N, I.fit, false, true);
 }
 
 // FD candidates [j0, j1) of step `it` on a fresh minibatch: the unperturbed stats pair into fit_stats
@@ -702,6 +709,7 @@ void set_qes_impl(Impl& I, const ntc_cuda::QesDesc& q, const float* grid, size_t
     if (!I.qes) die("set_qes without a --qes level in the model description");
     if (grid_n > (size_t)ntcb::kMaxLevels * 64 * 4096) die("--qes grid table too large");
     NTCB_CHECK(cudaMemcpyAsync(I.qes_dev, &q, sizeof(q), cudaMemcpyHostToDevice, I.stream));
+    I.qes_host = q;
     if (grid_n) NTCB_CHECK(cudaMemcpyAsync(I.qgrid, grid, grid_n * sizeof(float), cudaMemcpyHostToDevice, I.stream));
     snap_latent_impl(I);
     sync(I);
@@ -887,6 +895,155 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
     I.totals.erase(it);
 }
 long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
+// The progress print's statistics (main.cpp:4155-4205) on the device; see ntcb_print_stats. The host part
+// below is bitrate_stats' arithmetic (main.cpp:2272-2352) on the device's exact histograms, term for term.
+static int print_stats_impl(Impl& I, const int* level_bits, int ew, int eh, float* zq_out, ntcb_progress_stats* out) {
+    using namespace ntcb;
+    require_ready(I); set_device(I);
+    const ntc_cuda::ModelDesc& d = I.d;
+    const int nl = d.nlev, nb = lat_moment_blocks();
+    struct Plan { int mode, hstride; bool dct; int bits[kMaxCh]; long long hist_at, mm_at; };
+    std::vector<Plan> plan(nl);
+    long long ints = 0;
+    for (int l = 0; l < nl; l++) {
+        Plan& q = plan[l];
+        const int C = d.lv[l].C;
+        const bool fixed = l == 0 && d.qat > 0;
+        const bool qes = I.qes && I.qes_host.live && I.qes_host.bits[l] > 0;
+        q.dct = l == 0 && I.dct_live;
+        q.mode = fixed ? 1 : (qes ? 2 : 0);
+        q.hstride = 1;
+        for (int c = 0; c < C; c++) {
+            q.bits[c] = fixed ? d.qat_bits[c] : (qes ? I.qes_host.bits[l] : (level_bits ? level_bits[l] : 8));
+            if (!q.dct && (q.bits[c] < 1 || q.bits[c] > 16)) return -1;
+            q.hstride = std::max(q.hstride, 1 << std::min(16, std::max(0, q.bits[c])));
+        }
+        q.mm_at = ints; ints += 2 * C;
+        q.hist_at = ints; ints += q.dct ? 0 : 2LL * C * q.hstride;
+    }
+    // scratch: [ints] int32, then sse 2 x kMaxOut / 3 u64, the off-grid count u64, moments nl x 3 nb f64
+    const size_t o_sse = ((size_t)ints * 4 + 15) / 16 * 16;
+    const size_t o_cnt = o_sse + 2 * (kMaxOut / 3) * 8;
+    const size_t o_mom = o_cnt + 8;
+    const size_t bytes = o_mom + (size_t)nl * 3 * nb * 8;
+    if (bytes > I.stats_cap) { dfree(I.stats_buf); I.stats_buf = dalloc<char>(bytes); I.stats_cap = bytes; }
+    int* ibuf = reinterpret_cast<int*>(I.stats_buf);
+    auto* sse = reinterpret_cast<unsigned long long*>(I.stats_buf + o_sse);
+    auto* cnt = reinterpret_cast<unsigned long long*>(I.stats_buf + o_cnt);
+    auto* mom = reinterpret_cast<double*>(I.stats_buf + o_mom);
+    float* zq = I.ztmp;
+
+    timed(I, "print_stats", 0, [&] {
+        for (int l = 0; l < nl; l++) {
+            const Plan& q = plan[l];
+            const auto& L = d.lv[l];
+            const long long ntex = (long long)L.W * L.H, off = I.dm.lv[l].off;
+            if (q.dct) {
+                NTCB_CHECK(cudaMemcpyAsync(zq + off, I.zdec + off, (size_t)ntex * L.C * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+            } else {
+                if (q.mode == 0) { launch_level_minmax(I.stream, I.z + off, ntex, L.C, ibuf + q.mm_at); I.launches += 2; }
+                LevelQuantArgs a{};
+                a.z = I.z + off; a.zd = I.zdec + off; a.zq = zq + off;
+                a.W = L.W; a.H = L.H; a.C = L.C; a.mode = q.mode;
+                for (int c = 0; c < L.C; c++) {
+                    a.bits[c] = q.bits[c];
+                    if (q.mode == 2) { a.lo[c] = I.qes_host.lo[l][c]; a.range[c] = I.qes_host.range[l][c]; }
+                }
+                a.minmax = ibuf + q.mm_at;
+                a.dpcm = l > 0 ? 1 : 0;
+                a.hist = ibuf + q.hist_at; a.rhist = a.hist + (long long)L.C * q.hstride; a.hstride = q.hstride;
+                launch_level_quant(I.stream, a);
+                I.launches += 1;
+            }
+            launch_lat_moments(I.stream, I.z + off, ntex * L.C, mom + (size_t)l * 3 * nb);
+            I.launches += 1;
+        }
+        if (d.qat > 0) { launch_qat_offgrid(I.stream, I.z, I.n0, d.lv[0].C, I.qat_bits, I.qat_grid, cnt); I.launches += 1; }
+        else NTCB_CHECK(cudaMemsetAsync(cnt, 0, 8, I.stream));
+        if (ew <= 0 || ew > d.W) ew = d.W;
+        if (eh <= 0 || eh > d.H) eh = d.H;
+        launch_decode(I.stream, I.shape, I.dm, I.w, I.zdec, I.img);
+        launch_mse8(I.stream, I.tgt, I.img, d.W, ew, eh, d.nout, sse);
+        launch_decode(I.stream, I.shape, I.dm, I.w, zq, I.img);
+        launch_mse8(I.stream, I.tgt, I.img, d.W, ew, eh, d.nout, sse + kMaxOut / 3);
+        I.launches += 4;
+    });
+    std::vector<char> h(bytes);
+    NTCB_CHECK(cudaMemcpyAsync(h.data(), I.stats_buf, bytes, cudaMemcpyDeviceToHost, I.stream));
+    if (zq_out) NTCB_CHECK(cudaMemcpyAsync(zq_out, zq, (size_t)I.nz * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
+    sync(I);
+    const int* hi = reinterpret_cast<const int*>(h.data());
+    const auto* hsse = reinterpret_cast<const unsigned long long*>(h.data() + o_sse);
+    const auto* hcnt = reinterpret_cast<const unsigned long long*>(h.data() + o_cnt);
+    const auto* hmom = reinterpret_cast<const double*>(h.data() + o_mom);
+
+    ntcb_progress_stats s;
+    memset(&s, 0, sizeof(s));
+    // mse_of (main.cpp:1779-1787)
+    const int T = d.nout / 3;
+    const double npe = (double)ew * eh;
+    for (int k = 0; k < 2; k++) {
+        double* tex = k ? s.mse_q_tex : s.mse_tex;
+        double ws = 0.0;
+        for (int t = 0; t < T; t++) {
+            const double e = (double)hsse[k * (kMaxOut / 3) + t];
+            tex[t] = e / (3.0 * npe);
+            ws += (double)d.cw[3 * t] * e;
+        }
+        (k ? s.mse_q : s.mse) = ws / (3.0 * d.wsum * npe);
+    }
+    // bitrate_stats (main.cpp:2272-2352), progress-print form
+    const double npix = (double)d.W * d.H;
+    s.bits_mlp = I.P * 16.0;
+    s.bpp_fp32 = ((double)I.nz * 32.0 + I.P * 32.0) / npix;
+    double ent_bits = 0, header_bits = 0, raw_bits = 0, ctx_bits = 0, est_bits = 0;
+    for (int l = 0; l < nl; l++) {
+        const Plan& q = plan[l];
+        const auto& L = d.lv[l];
+        const double ntex = (double)L.W * L.H;
+        if (q.dct) { s.level0_dct = 1; continue; }
+        const bool fixed = q.mode == 1, qes = q.mode == 2;
+        if (!fixed && !qes) raw_bits += (double)((long long)L.W * L.H * L.C) * (double)q.bits[0];
+        for (int c = 0; c < L.C; c++) {
+            const int levels = (1 << q.bits[c]) - 1;
+            if (fixed || qes) raw_bits += ntex * (double)q.bits[c];
+            const int* hist = hi + q.hist_at + (long long)c * q.hstride;
+            const int* rh = hi + q.hist_at + (long long)(L.C + c) * q.hstride;
+            double h0 = 0;
+            for (int qv = 0; qv <= levels; qv++)
+                if (hist[qv]) h0 -= hist[qv] * std::log2(hist[qv] / ntex);
+            ent_bits += h0;
+            if (l == 0) { ctx_bits += h0; s.bpp_ctx_level0 += h0 / npix; }
+            else ctx_bits += h0;
+            if (l == 0) est_bits += h0;
+            else {
+                double hr = 0;
+                for (int qv = 0; qv <= levels; qv++) if (rh[qv]) hr -= rh[qv] * std::log2(rh[qv] / ntex);
+                est_bits += hr;
+            }
+        }
+        if (!fixed) header_bits += L.C * 2 * 32.0;
+    }
+    s.bpp_q8 = (raw_bits + header_bits + s.bits_mlp) / npix;
+    s.bpp_q8_ent = (ent_bits + header_bits + s.bits_mlp) / npix;
+    s.bpp_q8_ctx = (ctx_bits + header_bits + s.bits_mlp) / npix;
+    s.bpp_est = (est_bits + header_bits + s.bits_mlp) / npix;
+    s.bits_raw_latent = raw_bits; s.bits_header = header_bits;
+    // latent_stats (main.cpp:2212-2217), block partials summed in block order
+    for (int l = 0; l < nl; l++) {
+        const double* m = hmom + (size_t)l * 3 * nb;
+        double sum = 0, s2 = 0, mx = 0;
+        for (int b = 0; b < nb; b++) { sum += m[3 * b]; s2 += m[3 * b + 1]; mx = std::max(mx, m[3 * b + 2]); }
+        const double n = (double)((long long)d.lv[l].W * d.lv[l].H * d.lv[l].C);
+        s.lat_mean[l] = (float)(sum / n);
+        s.lat_sd[l] = (float)std::sqrt(std::max(0.0, s2 / n - (sum / n) * (sum / n)));
+        s.lat_max[l] = (float)mx;
+    }
+    s.qat_off_grid = (long long)*hcnt;
+    if (out) *out = s;
+    return 0;
+}
+
 static size_t dct_probe_impl(Impl& I, uint8_t* codes, float* gains, size_t cap) {
     require_ready(I); set_device(I);
     const int BW = I.d.W / 8, BH = I.d.H / 8, C = I.d.lv[0].C;
@@ -947,6 +1104,12 @@ void ntcb_shard_lat_install(ntcb_trainer* t, int level, const float* level_dev) 
 }
 size_t ntcb_cpp_dct_probe(void* cpp_trainer, uint8_t* codes, float* gains, size_t cap) {
     return dct_probe_impl(*static_cast<ntc_cuda::Trainer*>(cpp_trainer)->im, codes, gains, cap);
+}
+int ntcb_print_stats(ntcb_trainer* t, const int* level_bits, int eval_w, int eval_h, float* zq, ntcb_progress_stats* out) {
+    return print_stats_impl(t->impl, level_bits, eval_w, eval_h, zq, out);
+}
+int ntcb_cpp_print_stats(void* cpp_trainer, const int* level_bits, int eval_w, int eval_h, float* zq, ntcb_progress_stats* out) {
+    return print_stats_impl(*static_cast<ntc_cuda::Trainer*>(cpp_trainer)->im, level_bits, eval_w, eval_h, zq, out);
 }
 void ntcb_set_pop_kernel(ntcb_trainer* t, int tensor) { t->impl.tensor_pop = tensor != 0; }
 int ntcb_pop_kernel(const ntcb_trainer* t) { return (t->impl.tensor_pop && t->impl.shape != 0) ? 1 : 0; }

@@ -50,8 +50,10 @@ int pop_tc_rows();
 bool launch_lat_eval_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                         long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
                         long long p_begin, long long p_end, long long pstride, int* err);
-// Sum the chunk partials of every candidate in order, normalise, and write (lp, lm) pairs to fit[2*i], fit[2*i+1].
-void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit);
+// Sum the chunk partials of every candidate in order, normalise, and write (lp, lm) pairs to fit[2*i], fit[2*i+1];
+// with dl / lsum non-null also dl[i] = lp - lm and lsum[i] = (lp + lm) / 2 (launch_es_reduce's values).
+void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit,
+                       double* dl = nullptr, double* lsum = nullptr);
 // ES: dl, lsum from the fitness of all N pairs; FD: dl, hh.
 void launch_es_reduce(cudaStream_t s, const double* fit, int N, double* dl, double* lsum);
 void launch_fd_reduce(cudaStream_t s, const double* fit, const float* w0, float h, int P, double* dl, double* hh);
@@ -86,5 +88,30 @@ void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* 
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
                 const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end,
                 int max_bits);
+
+// ---- progress-print statistics (kernels_stats.cu) ----
+// Channel min / max of a level [ntex][C] as order-preserving int keys, mm[2 c] / mm[2 c + 1].
+void launch_level_minmax(cudaStream_t s, const float* z, long long ntex, int C, int* mm);
+struct LevelQuantArgs {
+    const float* z;            // training latent of the level [W * H][C]
+    const float* zd;           // decode buffer of the level
+    float* zq;                 // out: the quantized copy
+    int W, H, C;
+    int mode;                  // 0 post-hoc min / max grid, 1 --qat grid (zq = z), 2 --qes grid (zq = zd)
+    int bits[kMaxCh];          // depth per channel
+    float lo[kMaxCh], range[kMaxCh];   // mode 2: the fitted --qes table
+    const int* minmax;         // mode 0: launch_level_minmax's keys
+    int dpcm;                  // also the DPCM residual histogram
+    int *hist, *rhist;         // [C][hstride] each
+    int hstride;
+};
+void launch_level_quant(cudaStream_t s, const LevelQuantArgs& a);
+// Integer 8-bit squared error per texture (sse[kMaxOut / 3]) of images a, b ([H][W][nc]) over ew x eh.
+void launch_mse8(cudaStream_t s, const float* a, const float* b, int W, int ew, int eh, int nc, unsigned long long* sse);
+int lat_moment_blocks();
+// Per-block (sum, sum of squares, max |v|) of n values, part[3 * lat_moment_blocks()].
+void launch_lat_moments(cudaStream_t s, const float* z, long long n, double* part);
+void launch_qat_offgrid(cudaStream_t s, const float* z, long long n, int C, const int* bits, const float* grid,
+                        unsigned long long* count);
 
 }  // namespace ntcb

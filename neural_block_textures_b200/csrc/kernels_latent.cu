@@ -4,6 +4,7 @@
 #include "mlp_tile.cuh"
 #include "latent_features.cuh"
 #include "noise.cuh"
+#include "quant.cuh"
 
 namespace ntcb {
 
@@ -184,13 +185,6 @@ void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* 
 }
 
 // ------------------------------------------------------------------ --qat selector search
-// qat_index (main.cpp:2060-2064): the grid index of an on-grid value, lround((v + 1) / 2 * levels), clamped.
-__device__ __forceinline__ int qat_index(float v, int bits) {
-    const int levels = (1 << bits) - 1;
-    const int k = (int)lroundf((v + 1.0f) * 0.5f * (float)levels);
-    return max(0, min(levels, k));
-}
-
 // qat_search (main.cpp:2088-2139) for the fixed shapes: G consecutive lanes of a warp share one level-0
 // texel; lane gi evaluates the candidate pairs gi, gi + G, ... (grid values 2q and 2q + 1 as one packed-FP32
 // row pair). A candidate's cell loss is accumulated in double over the texel's pixels in raster order by

@@ -229,18 +229,28 @@ void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs
 }
 
 // fit[2i] = (sum over chunks of the + partials) / norm, fit[2i+1] likewise for - (k_mlp_es_finish's order).
-__global__ void k_pop_finish(const double* __restrict__ part, int ncand, int chunks, double norm, double* __restrict__ fit) {
+// With dl / lsum given (a population evaluated whole on one trainer) the ES reduction of k_es_reduce is
+// applied to the same values in the same launch.
+__global__ void k_pop_finish(const double* __restrict__ part, int ncand, int chunks, double norm, double* __restrict__ fit,
+                             double* __restrict__ dl, double* __restrict__ lsum) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= ncand) return;
     double lp = 0.0, lm = 0.0;
     const double* p = part + (long long)i * 2 * chunks;
     for (int j = 0; j < chunks; j++) { lp += p[j]; lm += p[chunks + j]; }
-    fit[2 * i] = lp / norm;
-    fit[2 * i + 1] = lm / norm;
+    lp /= norm;
+    lm /= norm;
+    fit[2 * i] = lp;
+    fit[2 * i + 1] = lm;
+    if (dl) {
+        dl[i] = lp - lm;
+        lsum[i] = 0.5 * (lp + lm);
+    }
 }
-void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit) {
+void launch_pop_finish(cudaStream_t s, const double* part, int ncand, int chunks, double norm, double* fit, double* dl,
+                       double* lsum) {
     if (ncand <= 0) return;
-    k_pop_finish<<<blocks_for(ncand, 128), 128, 0, s>>>(part, ncand, chunks, norm, fit);
+    k_pop_finish<<<blocks_for(ncand, 128), 128, 0, s>>>(part, ncand, chunks, norm, fit, dl, lsum);
     NTCB_CHECK(cudaGetLastError());
 }
 
@@ -282,6 +292,8 @@ __global__ void k_es_grad_partial(const double* __restrict__ dl, const float* __
     if (k >= P) return;
     const int i0 = seg * seglen, i1 = min(N, i0 + seglen);
     float g = 0.0f;
+    // unrolled so that 16 independent eps loads are in flight (the FMA chain stays in pair order)
+#pragma unroll 16
     for (int i = i0; i < i1; i++) {
         const float w = (float)dl[i] * scale;
         g = fmaf(w, __ldg(eps + (long long)i * P + k), g);
@@ -309,6 +321,7 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
     const int k = blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= P) return;
     float g = gpart[k];
+#pragma unroll 16
     for (int sg = 1; sg < nseg; sg++) g += gpart[(long long)sg * P + k];
     grad[k] = g;
     float th = theta[k], mm = m[k], vv = v[k];
@@ -317,7 +330,7 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
 }
 void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2) {
-    k_es_grad_adam<<<blocks_for(P, 256), 256, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
+    k_es_grad_adam<<<blocks_for(P, 64), 64, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
     NTCB_CHECK(cudaGetLastError());
 }
 

@@ -8,6 +8,7 @@
 // patterns, copied.
 #include "kernels_snap.h"
 #include "noise.cuh"
+#include "quant.cuh"
 
 namespace ntcb {
 
@@ -16,12 +17,6 @@ inline unsigned blocks_for(long long n, int tpb) { return (unsigned)((n + tpb - 
 }
 
 // ------------------------------------------------------------------ --qes
-// qes_index (main.cpp:448-453): round-half-even of ((v - lo) / range) * levels, clamped in float.
-__device__ __forceinline__ int qes_index_dev(float v, float lo, float range, int levels) {
-    const float r = rintf(__fmul_rn(__fdiv_rn(__fsub_rn(v, lo), range), (float)levels));
-    return r <= 0.0f ? 0 : (r >= (float)levels ? levels : (int)r);
-}
-
 // qes_snap_level over every level (main.cpp:485-496; copies for levels without --qes bits), with the
 // frozen clamp of the shadow written back.
 __global__ void k_qes_snap(DevModel m, const QesTables* __restrict__ q, float* __restrict__ z, float* __restrict__ zq,

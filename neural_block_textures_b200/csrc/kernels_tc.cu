@@ -121,11 +121,11 @@ __device__ __forceinline__ float rcp_approx(float x) {
 __device__ __forceinline__ float out_act_fast(float s, int clamp_out) {
     return clamp_out ? fminf(fmaxf(s, 0.0f), 1.0f) : rcp_approx(1.0f + __expf(-s));
 }
-// Leaky ReLU of a pair; for 0 <= leak <= 1, max(x, leak x) equals the select for every float.
-__device__ __forceinline__ float2 leaky_pair(float2 x, float leak, bool leak_unit) {
+// Leaky ReLU of a pair; for 0 <= leak <= 1 (the only slopes the compiled shapes admit) max(x, leak x)
+// equals the reference's select for every float.
+__device__ __forceinline__ float2 leaky_pair(float2 x, float leak) {
     const float2 t = __fmul2_rn(x, make_float2(leak, leak));
-    if (leak_unit) return make_float2(fmaxf(x.x, t.x), fmaxf(x.y, t.y));
-    return make_float2(x.x > 0.0f ? x.x : t.x, x.y > 0.0f ? x.y : t.y);
+    return make_float2(fmaxf(x.x, t.x), fmaxf(x.y, t.y));
 }
 
 // Split N (multiple of 8) values into hi / lo and store them to TMEM columns [ch, ch + N) / [cl, cl + N).
@@ -151,7 +151,7 @@ __device__ __forceinline__ void store_split(uint32_t trow, int ch, int cl, const
 // output, float error sum over the channels.
 template <class S>
 __device__ __forceinline__ float out_layer_error(const DevModel& m, const float* ws, const float* h, const float* t,
-                                                 float leak, bool leak_unit) {
+                                                 float leak) {
     using T = TcShape<S>;
     float2 acc[S::NOUT];
 #pragma unroll
@@ -159,8 +159,8 @@ __device__ __forceinline__ float out_layer_error(const DevModel& m, const float*
 #pragma unroll
     for (int j = 0; j < S::H2; j += 4) {
         const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
-        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak, leak_unit);
-        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak, leak_unit);
+        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak);
+        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
 #pragma unroll
         for (int c = 0; c < S::NOUT; c++) {
             const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + c * S::H2 + j);
@@ -247,7 +247,6 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
     const uint32_t sb0 = tc::smem_addr(sw), sb1 = sb0 + (uint32_t)(T::SIGN * 4);
     const float leak = m.leak;
-    const bool leak_unit = leak >= 0.0f && leak <= 1.0f;
     uint32_t waited = 0, waited3 = 0;   // completed phases this thread has observed on bar / bar3
     bool ok = true;
 
@@ -331,7 +330,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 tc::wait_ld();
 #pragma unroll
                 for (int j = 0; j < S::H1; j += 2) {
-                    const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak, leak_unit);
+                    const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak);
                     h[j] = v.x; h[j + 1] = v.y;
                 }
                 store_split<T::K2>(trow, T::cHh, T::cHl, h);
@@ -353,8 +352,8 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
 #pragma unroll
                     for (int j = 0; j < S::H2; j += 4) {
                         const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
-                        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak, leak_unit);
-                        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak, leak_unit);
+                        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak);
+                        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
                         h[j] = h0.x; h[j + 1] = h0.y; h[j + 2] = h1.x; h[j + 3] = h1.y;
                     }
                     store_split<T::K3>(trow, T::cHh, T::cHl, h);
@@ -396,7 +395,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                         issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
                     }
                     // output layer and error of this unit, overlapping the tensor core's next layer 1
-                    const double e = valid ? (double)out_layer_error<S>(m, ws, h, t, leak, leak_unit) : 0.0;
+                    const double e = valid ? (double)out_layer_error<S>(m, ws, h, t, leak) : 0.0;
                     if (sg == 0) acc_p += e; else acc_m += e;
                 }
             }
@@ -478,7 +477,6 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
     const uint32_t sb = tc::smem_addr(sw);
     const float leak = m.leak;
-    const bool leak_unit = leak >= 0.0f && leak <= 1.0f;
     uint32_t waited = 0;
     bool ok = true;
     auto wait_mma = [&]() {
@@ -522,7 +520,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::wait_ld();
 #pragma unroll
         for (int j = 0; j < S::H1; j += 2) {
-            const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak, leak_unit);
+            const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak);
             h[j] = v.x; h[j + 1] = v.y;
         }
         store_split<T::K2>(trow, T::cHh, T::cHl, h);
@@ -559,7 +557,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
         if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
-        const float ep = out_layer_error<S>(m, sw, h, t, leak, leak_unit);
+        const float ep = out_layer_error<S>(m, sw, h, t, leak);
         // - unit
         layer1_to_layer2();
         if (!ok) break;
@@ -572,7 +570,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
         if (more && warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
-        const float em = out_layer_error<S>(m, sw, h, t, leak, leak_unit);
+        const float em = out_layer_error<S>(m, sw, h, t, leak);
         {
             const int k = (int)(item / ntiles);
             const long long p = p_begin + (item - (long long)k * ntiles) * kTcRows + tid;

@@ -61,8 +61,11 @@ struct FixedShape {
         k -= NOUT * H2;
         return oB2 + k;
     }
+    // The compiled kernels form the leaky ReLU as max(x, leak x), which equals the reference's select
+    // (x > 0 ? x : leak x) for 0 <= leak <= 1 only; other slopes run the runtime-shaped kernels.
     static bool matches(const DevModel& m) {
-        return m.nin == NIN && m.nhidden == 2 && m.hidden[0] == H1 && m.hidden[1] == H2 && m.nout == NOUT;
+        return m.nin == NIN && m.nhidden == 2 && m.hidden[0] == H1 && m.hidden[1] == H2 && m.nout == NOUT &&
+               m.leak >= 0.0f && m.leak <= 1.0f;
     }
 };
 
@@ -74,12 +77,11 @@ struct GenericShape {
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
-__device__ __forceinline__ float2 leaky2(float2 s, float leak, bool leak_unit) {
-    // For 0 <= leak <= 1, max(x, leak x) equals (x > 0 ? x : leak x) for every float, signed zeros and
-    // NaN included; other slopes take the select.
+__device__ __forceinline__ float2 leaky2(float2 s, float leak) {
+    // For 0 <= leak <= 1 (the only slopes FixedShape::matches admits), max(x, leak x) equals
+    // (x > 0 ? x : leak x) for every float, signed zeros and NaN included.
     const float2 t = __fmul2_rn(s, f2(leak));
-    if (leak_unit) return make_float2(fmaxf(s.x, t.x), fmaxf(s.y, t.y));
-    return make_float2(s.x > 0.0f ? s.x : t.x, s.y > 0.0f ? s.y : t.y);
+    return make_float2(fmaxf(s.x, t.x), fmaxf(s.y, t.y));
 }
 
 // Stage the flat weights wg (reference layout) into shared memory as one duplicated FixedShape set.
@@ -98,7 +100,6 @@ __device__ __forceinline__ void load_weights_x2(const float* __restrict__ wg, in
 template <class S, int R2>
 __device__ __forceinline__ void fixed_forward_x2(const float* __restrict__ w, const float2 (&x)[R2][S::NIN],
                                                  float2 (&o)[R2][S::NOUT], float leak, int clamp_out) {
-    const bool leak_unit = leak >= 0.0f && leak <= 1.0f;
     float2 a[R2][S::H1];
 #pragma unroll
     for (int j = 0; j < S::H1; j += 2) {
@@ -122,7 +123,7 @@ __device__ __forceinline__ void fixed_forward_x2(const float* __restrict__ w, co
 #pragma unroll
     for (int q = 0; q < R2; q++)
 #pragma unroll
-        for (int j = 0; j < S::H1; j++) a[q][j] = leaky2(a[q][j], leak, leak_unit);
+        for (int j = 0; j < S::H1; j++) a[q][j] = leaky2(a[q][j], leak);
 
 #pragma unroll
     for (int q = 0; q < R2; q++)
@@ -154,7 +155,7 @@ __device__ __forceinline__ void fixed_forward_x2(const float* __restrict__ w, co
         }
 #pragma unroll
         for (int q = 0; q < R2; q++) {
-            const float2 h = leaky2(s[q], leak, leak_unit);
+            const float2 h = leaky2(s[q], leak);
 #pragma unroll
             for (int k = 0; k < S::NOUT; k++) o[q][k] = __ffma2_rn(wo[k], h, o[q][k]);
         }

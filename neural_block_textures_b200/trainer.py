@@ -186,6 +186,19 @@ class Trainer:
         self.lib.ntcb_dct_probe(self.h, codes.ctypes.data_as(C.POINTER(C.c_uint8)), _ptr(gains, C.c_float), n)
         return codes, gains
 
+    def print_stats(self, level_bits=None, eval_w: int = 0, eval_h: int = 0, want_zq: bool = False):
+        """The progress print's statistics on the device (ntcb_print_stats): (ProgressStats, zq or None).
+        level_bits: post-hoc depth per level (default 8, the reference's --qbits)."""
+        lb = np.full(abi.MAX_LEVELS, 8, np.int32)
+        if level_bits is not None:
+            lb[: len(level_bits)] = level_bits
+        out = abi.ProgressStats()
+        zq = np.empty(self.nz, np.float32) if want_zq else None
+        rc = self.lib.ntcb_print_stats(self.h, _ptr(lb, C.c_int), eval_w, eval_h, _fptr(zq), C.byref(out))
+        if rc != 0:
+            raise ValueError("ntcb_print_stats: a post-hoc depth outside 1..16")
+        return out, zq
+
     def set_pop_kernel(self, tensor: bool) -> None:
         """True: ES pairs on the tensor-core (3xTF32) kernel; False: the bit-exact packed-FP32 kernel."""
         self.lib.ntcb_set_pop_kernel(self.h, 1 if tensor else 0)

@@ -226,6 +226,11 @@ def refcpu_lib() -> C.CDLL:
     lib.ref_qes_fit_level.argtypes = [C.c_void_p, C.c_int, C.c_int]
     lib.ref_es_fitness.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_int, C.c_int, _ip, C.c_int, _dp, _dp]
     lib.ref_fd_dl.argtypes = [C.c_void_p, C.c_float, _ip, C.c_int, _ip, C.c_int, _dp]
+    lib.ref_bitrate_stats.argtypes = [C.c_void_p, C.c_int, _dp, _fp]
+    lib.ref_mse_of.restype = C.c_double
+    lib.ref_mse_of.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, _dp]
+    lib.ref_latent_stats.argtypes = [C.c_void_p, C.c_int, _fp]
+    lib.ref_qes_tables.argtypes = [C.c_void_p, C.c_int, _fp, _fp, _fp, _fp]
     return lib
 
 
@@ -347,6 +352,37 @@ class RefSession:
         code = np.zeros(n, np.uint8)
         self.lib.ref_dct_state(C.c_void_p(self.h), None, code.ctypes.data_as(C.POINTER(C.c_uint8)), None, None, None, None, None, None, None)
         return code
+
+    BITRATE_FIELDS = ("bpp_fp32", "bpp_q8", "bpp_q8_ent", "bpp_q8_ctx", "bpp_ctx_level0", "bpp_est", "bits_mlp",
+                      "bits_raw_latent", "bits_header")
+
+    def bitrate_stats(self, qbits: int = 8):
+        """bitrate_stats as the progress print calls it (main.cpp:4171): (fields dict, quantized copy zq)."""
+        out = np.zeros(9)
+        zq = np.zeros(self.spec.nz, np.float32)
+        self.lib.ref_bitrate_stats(C.c_void_p(self.h), qbits, out.ctypes.data_as(_dp), zq.ctypes.data_as(_fp))
+        return dict(zip(self.BITRATE_FIELDS, out.tolist())), zq
+
+    def mse_of(self, img, ew: int = 0, eh: int = 0):
+        """mse_of (main.cpp:1764-1788) of an image against the session target: (weighted, per-texture array)."""
+        tex = np.zeros(4)
+        img = np.ascontiguousarray(img, np.float32)
+        w = self.lib.ref_mse_of(C.c_void_p(self.h), img.ctypes.data_as(_fp), ew, eh, tex.ctypes.data_as(_dp))
+        return w, tex[: self.spec.T].copy()
+
+    def latent_stats(self, l: int):
+        """latent_stats (main.cpp:2212-2217) of level l: (mean, sd, max) as float32."""
+        msm = np.zeros(3, np.float32)
+        self.lib.ref_latent_stats(C.c_void_p(self.h), l, msm.ctypes.data_as(_fp))
+        return tuple(msm.tolist())
+
+    def qes_tables(self, l: int, C_: int, bits: int):
+        """The fitted --qes table of level l: (lo, hi, range, grid [C][2^bits])."""
+        lo = np.zeros(C_, np.float32); hi = np.zeros(C_, np.float32); rg = np.zeros(C_, np.float32)
+        grid = np.zeros(C_ << bits, np.float32)
+        self.lib.ref_qes_tables(C.c_void_p(self.h), l, lo.ctypes.data_as(_fp), hi.ctypes.data_as(_fp), rg.ctypes.data_as(_fp),
+                                grid.ctypes.data_as(_fp))
+        return lo, hi, rg, grid
 
     def zdec(self):
         z = np.zeros(self.spec.nz, np.float32)

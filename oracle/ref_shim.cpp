@@ -241,6 +241,37 @@ double ref_psnr_of_decode(void* h, const float* img) {
     return psnr_of(mse_of(s->target, a, s->o.weights, s->D.wsum).weighted);
 }
 
+// ---- the progress print's statistics (main.cpp:4155-4205) ----
+// bitrate_stats (main.cpp:2272-2352) as the print calls it (g_ctx_stats off) on the session's model. out receives
+// bpp_fp32, bpp_q8, bpp_q8_ent, bpp_q8_ctx, bpp_ctx_level0, bpp_est, bits_mlp, bits_raw_latent, bits_header; zq the
+// returned quantized copy (nz floats).
+void ref_bitrate_stats(void* h, int qbits, double* out, float* zq) {
+    auto* s = static_cast<RefSession*>(h);
+    std::vector<float> zpost;
+    g_ctx_stats = false;
+    const BitrateStats b = bitrate_stats(s->D, qbits, zpost);
+    g_ctx_stats = true;
+    const double v[9] = { b.bpp_fp32, b.bpp_q8, b.bpp_q8_ent, b.bpp_q8_ctx, b.bpp_ctx_level0, b.bpp_est, b.bits_mlp,
+                          b.bits_raw_latent, b.bits_header };
+    std::copy(v, v + 9, out);
+    if (zq) std::copy(zpost.begin(), zpost.end(), zq);
+}
+// mse_of (main.cpp:1764-1788) of an image shaped like the target, over the extent ew x eh (0 = whole image);
+// tex receives the per-texture figures. Returns the weighted one.
+double ref_mse_of(void* h, const float* img, int ew, int eh, double* tex) {
+    auto* s = static_cast<RefSession*>(h);
+    Image a; a.w = s->D.W; a.h = s->D.H; a.nc = s->D.mlp.nout;
+    a.rgb.assign(img, img + (size_t)a.w * a.h * a.nc);
+    const Mse m = mse_of(s->target, a, s->o.weights, s->D.wsum, ew, eh);
+    if (tex) for (int t = 0; t < a.nc / 3; t++) tex[t] = m.tex[t];
+    return m.weighted;
+}
+// latent_stats (main.cpp:2212-2217) of level l's training values: msm = mean, sd, max |v|.
+void ref_latent_stats(void* h, int l, float* msm) {
+    auto* s = static_cast<RefSession*>(h);
+    latent_stats(s->D.lat.lv[l], s->D.lat.level(l), msm[0], msm[1], msm[2]);
+}
+
 // ---- --qes (QES region, main.cpp:414-496) ----
 int ref_qes_index(float v, float lo, float range, int levels) { return qes_index(v, lo, range, levels); }
 // Fit the ranges of level `l` at `bits` from the shadow, freeze them and snap every level (Decoder::qes_fit_all).

@@ -104,6 +104,24 @@ def test_ctypes_layout_matches_c_header(tmp_path):
         assert getattr(cls, f).offset == off, key
 
 
+def test_progress_stats_layout_matches_c_header(tmp_path):
+    """ctypes ProgressStats against ntcb_progress_stats as the C compiler lays it out."""
+    if not shutil.which("gcc"):
+        pytest.skip("no gcc")
+    fields = [f for f, _ in abi.ProgressStats._fields_]
+    src = tmp_path / "ps.c"
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"%s\"\nint main(void) {\n"
+                   "  printf(\"sizeof %%zu\\n\", sizeof(ntcb_progress_stats));\n%s  return 0;\n}\n"
+                   % (ROOT / "include" / "ntc_b200.h",
+                      "".join('  printf("%s %%zu\\n", offsetof(ntcb_progress_stats, %s));\n' % (f, f) for f in fields)))
+    exe = tmp_path / "ps"
+    subprocess.run(["gcc", "-std=c11", "-o", str(exe), str(src)], check=True)
+    out = dict(ln.split() for ln in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines())
+    assert int(out["sizeof"]) == C.sizeof(abi.ProgressStats)
+    for f in fields:
+        assert getattr(abi.ProgressStats, f).offset == int(out[f]), f
+
+
 def test_init_without_gpu_reports_a_reason(tmp_path):
     """On a machine without a CUDA device init() returns false with a reason instead of crashing (run in a child)."""
     import torch

@@ -62,6 +62,21 @@ def test_mlp_es_fitness(name, cuda_device):
     assert np.array_equal(p2, p), "lr 0 leaves the weights unchanged"
 
 
+@pytest.mark.parametrize("leak", [1.5, -0.25])
+def test_leak_outside_unit_interval(leak, cuda_device):
+    """A benchmark shape with a slope outside [0, 1] (where max(x, leak x) is not the reference's select) runs
+    the runtime-shaped kernels: decode and ES fitness against the oracle."""
+    spec, tgt, z, p, tr, orc = make("cfg2", cuda_device, leak=leak)
+    assert np.abs(tr.decode_full() - orc.decode_full(p, z)).max() < 1e-5
+    N, M, it = 8, 256, 4
+    tr.mlp_step(it, SIGMA, 0.0, N, M)
+    bidx = tr.debug_last_batch()
+    lp, lm = tr.debug_last_fitness()
+    olp, olm = orc.es_fitness(p, z, spec.seed, it, SIGMA, 0, N, bidx)
+    assert rel_err(lp, olp) < FIT_RTOL and rel_err(lm, olm) < FIT_RTOL
+    tr.close()
+
+
 @pytest.mark.parametrize("name", ["cfg1", "cfg2", "generic"])
 def test_mlp_es_step_updates(name, cuda_device):
     """One ES step with lr > 0: gradient (segmented pair sums) and Adam against the oracle's serial ones."""
