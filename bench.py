@@ -179,6 +179,42 @@ def cpu_baseline_leg(cfg, budget_s=12.0):
                       f"and selector search): {dec / 1e6:.2f} M decodes each, {t_all:.1f} s"}
 
 
+def progress_print_leg(tr, cfg, with_reference: bool, reps=5):
+    """The progress print's statistics (main.cpp:4155-4205) once per print, wall clock: ntcb_print_stats on the
+    device, and the reference's print path with this backend (download_model, then on the host bitrate_stats,
+    mse_of of two device decodes downloaded through decode_full, latent_stats; the reference's own functions
+    through oracle/_ref)."""
+    spec = cfg.spec
+    lb = [8] * len(spec.levels)
+    tr.print_stats(lb)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        st, _ = tr.print_stats(lb)
+    out = {"device_ms": (time.perf_counter() - t0) / reps * 1e3, "mse": st.mse, "mse_q": st.mse_q, "bpp_q8": st.bpp_q8,
+           "bpp_est": st.bpp_est}
+    from oracle.oracle import RefSession, refcpu_available
+    if not with_reference or not refcpu_available():
+        return out
+    sess = RefSession(spec, cfg.target())
+    t_all = 0.0
+    for _ in range(2):
+        t0 = time.perf_counter()
+        z, p = tr.download_model()
+        sess.set_model(z, p)
+        rw, _ = sess.mse_of(tr.decode_full())
+        rs, zq = sess.bitrate_stats(8)
+        rq, _ = sess.mse_of(tr.decode_full(zq))
+        for l in range(min(2, len(spec.levels))):
+            sess.latent_stats(l)
+        t_all = time.perf_counter() - t0
+    sess.close()
+    out["reference_path_ms"] = t_all * 1e3
+    out["reference_path"] = "download_model + host bitrate_stats / mse_of x2 / latent_stats + 2 decode_full downloads"
+    out["agrees"] = bool(abs(rw - st.mse) <= 1e-12 * rw and abs(rq - st.mse_q) <= 1e-12 * rq and
+                         abs(rs["bpp_q8"] - st.bpp_q8) <= 1e-12 * rs["bpp_q8"])
+    return out
+
+
 def tf32_peak_tflops(n=8192, reps=20):
     """cuBLAS TF32 GEMM throughput on this GPU (the denominator for the tensor-core population kernel)."""
     import torch
@@ -465,6 +501,8 @@ def main():
             "fd_phase": fd_line,
             "clocks": clk.summary(),
         }
+        if world == 1:
+            line["progress_print"] = progress_print_leg(tr, cfg, not args.no_cpu_baseline)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_leg(cfg)
         if world == 1 and not args.no_ref_cuda:
