@@ -292,12 +292,16 @@ __global__ void k_es_grad_partial(const double* __restrict__ dl, const float* __
     if (k >= P) return;
     const int i0 = seg * seglen, i1 = min(N, i0 + seglen);
     float g = 0.0f;
-    // unrolled so that 16 independent eps loads are in flight (the FMA chain stays in pair order)
-#pragma unroll 16
-    for (int i = i0; i < i1; i++) {
-        const float w = (float)dl[i] * scale;
-        g = fmaf(w, __ldg(eps + (long long)i * P + k), g);
+    int i = i0;
+    // eight pairs' loads issued together, then their FMAs in pair order (the same chain as one at a time)
+    for (; i + 8 <= i1; i += 8) {
+        float e[8], w[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) { e[j] = __ldg(eps + (long long)(i + j) * P + k); w[j] = (float)dl[i + j]; }
+#pragma unroll
+        for (int j = 0; j < 8; j++) g = fmaf(w[j] * scale, e[j], g);
     }
+    for (; i < i1; i++) g = fmaf((float)dl[i] * scale, __ldg(eps + (long long)i * P + k), g);
     gpart[(long long)seg * P + k] = g;
 }
 void launch_es_grad_partial(cudaStream_t s, const double* dl, const float* eps, int N, int P, float scale, int seglen, float* gpart) {
@@ -321,8 +325,15 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
     const int k = blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= P) return;
     float g = gpart[k];
-#pragma unroll 16
-    for (int sg = 1; sg < nseg; sg++) g += gpart[(long long)sg * P + k];
+    int sg = 1;
+    for (; sg + 8 <= nseg; sg += 8) {   // eight segments' loads together, summed in segment order
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = gpart[(long long)(sg + j) * P + k];
+#pragma unroll
+        for (int j = 0; j < 8; j++) g += v[j];
+    }
+    for (; sg < nseg; sg++) g += gpart[(long long)sg * P + k];
     grad[k] = g;
     float th = theta[k], mm = m[k], vv = v[k];
     adam_update(th, g, mm, vv, lr, c1, c2);
@@ -330,7 +341,7 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
 }
 void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2) {
-    k_es_grad_adam<<<blocks_for(P, 64), 64, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
+    k_es_grad_adam<<<blocks_for(P, 256), 256, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
     NTCB_CHECK(cudaGetLastError());
 }
 
