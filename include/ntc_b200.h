@@ -200,6 +200,41 @@ typedef struct ntcb_progress_stats {
 int ntcb_print_stats(ntcb_trainer* t, const int* level_bits, int eval_w, int eval_h, float* zq, ntcb_progress_stats* out);
 /* The same for a drop-in C++ trainer: cpp_trainer points at an initialised ntc_cuda::Trainer. */
 int ntcb_cpp_print_stats(void* cpp_trainer, const int* level_bits, int eval_w, int eval_h, float* zq, ntcb_progress_stats* out);
+
+/* ---- .ntcb containers (the reference's --write-ntcb output, layout versions 1 and 2) decoded on the device: the
+ * inference-side neighbour of the trainer, replacing the reference's CPU decoder ntc_decode.cpp for this format. */
+typedef struct ntcb_container_desc {
+    int version, img_w, img_h, src_w, src_h, T, nlevels;
+    int nin, nout, nhidden; int hidden[NTCB_MAX_HIDDEN];
+    float leak; int clamp_out;
+    int lv_W[NTCB_MAX_LEVELS], lv_H[NTCB_MAX_LEVELS], lv_C[NTCB_MAX_LEVELS], lv_nearest[NTCB_MAX_LEVELS];
+    int lv_mode[NTCB_MAX_LEVELS];   /* 0 post-hoc grid, 1 --qes grid, 2 --qat palette, 3 DCT symbols */
+    int lv_bits[NTCB_MAX_LEVELS];   /* index depth of channel 0 (0 for DCT) */
+    int npos; int pos_kind[NTCB_MAX_POS];
+    long long nz, nweights;
+} ntcb_container_desc;
+typedef struct ntcb_decoder ntcb_decoder;
+/* Parse and validate a container on the host (no GPU needed): every header field and range, the file length and
+ * hash, each section header, sync marker and length, the DCT token stream and the fp16 weights (the refusals of
+ * ntcb_read_header / ntcb_restore, main.cpp:2521-2629 and 2762-2855). Returns 0, or -1 with the first problem in
+ * err (err_cap bytes, may be null). */
+int ntcb_container_info(const uint8_t* bytes, size_t n, ntcb_container_desc* info, char* err, size_t err_cap);
+/* Parse, upload and reconstruct the latent of a container on the current device (grid indices unpacked by the
+ * device, a DCT-coded level 0 reconstructed from its symbols). Null with the reason in err on refusal. */
+ntcb_decoder* ntcb_decoder_open(const uint8_t* bytes, size_t n, char* err, size_t err_cap);
+void ntcb_decoder_get_info(const ntcb_decoder* d, ntcb_container_desc* info);
+/* The reconstructed latent (nz floats) and the weights (nweights floats, the fp16 values) on the host; either may be null. */
+void ntcb_decoder_model(ntcb_decoder* d, float* z, float* w);
+/* Decode the image and quantize it as the reference writes its PNGs (lround(clamp(v, 0, 1) * 255)): out receives T
+ * planes [crop_h][crop_w][3] (texture-major), the top-left crop (0 = the header's source size). Returns the byte
+ * count (out may be null to ask for it), 0 on a bad crop. */
+size_t ntcb_decoder_rgb8(ntcb_decoder* d, int crop_w, int crop_h, uint8_t* out, size_t cap);
+/* The same into device memory on `stream` (null = the decoder's own), without synchronising. Returns 0 or -1. */
+int ntcb_decoder_rgb8_device(ntcb_decoder* d, int crop_w, int crop_h, uint8_t* out_dev, void* stream);
+void ntcb_decoder_close(ntcb_decoder* d);
+/* The DCT tables the reconstruction uses, from their definitions: basis [64], zigzag [64] and the 16 step tables
+ * [16][64] of one channel at quality q (dct_build_steps, main.cpp:747-781); any pointer may be null. */
+void ntcb_dct_tables(int q, int dc_step, float* basis, int* zigzag, int* steps);
 /* Number of kernels this trainer has launched since creation. */
 long long ntcb_launch_count(const ntcb_trainer* t);
 /* Which kernels evaluate the ES decodes (mlp_step / ntcb_shard_mlp_eval pairs and the lat_step pass). tensor = 1
