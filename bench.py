@@ -215,6 +215,61 @@ def progress_print_leg(tr, cfg, with_reference: bool, reps=5):
     return out
 
 
+def ntcb_decode_leg(reps=20):
+    """The .ntcb decoder at the config-5 size: a 2048 x 2048 container (--qat 2 level 0 at 1024 x 1024 x 2, 8-bit level 1
+    at 256 x 256 x 4) written by the reference's own CPU trainer (oracle/_ref/ntc_cpu --write-ntcb, one iteration),
+    decoded to RGB8 on the device (CUDA events over `reps` decodes, and once end to end into host memory) and by the
+    reference's own CPU decoder (oracle/_ref/ntc_decode --exact --bench on every host thread)."""
+    import re
+    import tempfile
+    import torch
+    from neural_block_textures_b200 import ntcb, synth
+    ref = ROOT / "oracle" / "_ref"
+    if not (ref / "ntc_cpu").exists() or not (ref / "ntc_decode").exists():
+        return None
+    with tempfile.TemporaryDirectory() as t:
+        t = Path(t)
+        synth.write_png(t / "img.png", synth.synth_rgb8(2048, 2048, 5))
+        r = subprocess.run([str(ref / "ntc_cpu"), str(t / "img.png"), *"--latent 1024 1024 2 --latent2 256 256 4 --filter nearest,bilinear "
+                            "--qat 2 --mlp-pairs 8 --mlp-batch 1024 --iters 1 --seed 5 --rng hash --print-every 1000000 "
+                            "--write-ntcb".split(), "--out", str(t / "o")], capture_output=True, text=True, timeout=600)
+        if r.returncode != 0:
+            return {"unavailable": "the reference trainer did not write the container"}
+        data = (t / "o" / "model.ntcb").read_bytes()
+        threads = len(os.sched_getaffinity(0))
+        d = subprocess.run([str(ref / "ntc_decode"), str(t / "o" / "model.ntcb"), "-o", str(t / "dec"), "--exact", "--bench",
+                            "--threads", str(min(threads, 64))], capture_output=True, text=True, timeout=600)
+        m = re.search(r"^exact\s+(\d+)\s+[\d.]+\s+[\d.]+\s+[\d.]+\s+([\d.]+)", d.stdout, re.M)
+        ref_rgb = synth.read_png(t / "dec.png") if (t / "dec.png").exists() else None
+    with ntcb.NtcbDecoder(data) as dec:
+        W, H = dec.info.src_w, dec.info.src_h
+        out = torch.empty(W * H * 3, dtype=torch.uint8, device="cuda")
+        s = torch.cuda.Stream()
+        for _ in range(3):
+            dec.rgb8_device(out.data_ptr(), 0, 0, s.cuda_stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.synchronize()
+        e0.record(s)
+        for _ in range(reps):
+            dec.rgb8_device(out.data_ptr(), 0, 0, s.cuda_stream)
+        e1.record(s)
+        e1.synchronize()
+        dev_ms = e0.elapsed_time(e1) / reps
+        t0 = time.perf_counter()
+        rgb = dec.rgb8()
+        host_ms = (time.perf_counter() - t0) * 1e3
+    line = {"workload": "2048x2048 container, --qat 2 level 0 1024x1024x2 + 8-bit level 1 256x256x4, (8, 24, 24, 3) MLP",
+            "bytes": len(data), "device_ms": dev_ms, "device_mtexel_s": W * H / dev_ms / 1e3,
+            "e2e_host_ms": host_ms, "e2e_host_mtexel_s": W * H / host_ms / 1e3}
+    if m:
+        line["reference_cpu_mtexel_s"] = float(m.group(2))
+        line["reference_cpu_threads"] = int(m.group(1))
+        line["reference"] = "ntc_decode --exact --bench (the reference's SSE4.1 decoder), min-time rate"
+    if ref_rgb is not None:
+        line["bytes_equal_to_reference"] = float(np.mean(rgb[0] == ref_rgb))
+    return line
+
+
 def tf32_peak_tflops(n=8192, reps=20):
     """cuBLAS TF32 GEMM throughput on this GPU (the denominator for the tensor-core population kernel)."""
     import torch
@@ -505,6 +560,7 @@ def main():
             line["progress_print"] = progress_print_leg(tr, cfg, not args.no_cpu_baseline)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_leg(cfg)
+            line["ntcb_decode"] = ntcb_decode_leg()
         if world == 1 and not args.no_ref_cuda:
             tr.close()
             line["ref_cuda_backend"] = ref_cuda_leg(cfg)

@@ -73,6 +73,19 @@ class DctDesc(C.Structure):
     ]
 
 
+class ContainerDesc(C.Structure):
+    """ntcb_container_desc: a parsed .ntcb header."""
+    _fields_ = [
+        ("version", C.c_int), ("img_w", C.c_int), ("img_h", C.c_int), ("src_w", C.c_int), ("src_h", C.c_int),
+        ("T", C.c_int), ("nlevels", C.c_int), ("nin", C.c_int), ("nout", C.c_int), ("nhidden", C.c_int),
+        ("hidden", C.c_int * MAX_HIDDEN), ("leak", C.c_float), ("clamp_out", C.c_int),
+        ("lv_W", C.c_int * MAX_LEVELS), ("lv_H", C.c_int * MAX_LEVELS), ("lv_C", C.c_int * MAX_LEVELS),
+        ("lv_nearest", C.c_int * MAX_LEVELS), ("lv_mode", C.c_int * MAX_LEVELS), ("lv_bits", C.c_int * MAX_LEVELS),
+        ("npos", C.c_int), ("pos_kind", C.c_int * MAX_POS),
+        ("nz", C.c_longlong), ("nweights", C.c_longlong),
+    ]
+
+
 class ProgressStats(C.Structure):
     """ntcb_progress_stats: the progress print's figures (main.cpp:4155-4205)."""
     _fields_ = [
@@ -130,6 +143,14 @@ SIGNATURES = {
     "ntcb_cpp_dct_probe": (C.c_size_t, [_vp, C.POINTER(C.c_uint8), _fp, C.c_size_t]),
     "ntcb_print_stats": (C.c_int, [_vp, C.POINTER(C.c_int), C.c_int, C.c_int, _fp, C.POINTER(ProgressStats)]),
     "ntcb_cpp_print_stats": (C.c_int, [_vp, C.POINTER(C.c_int), C.c_int, C.c_int, _fp, C.POINTER(ProgressStats)]),
+    "ntcb_container_info": (C.c_int, [_u8p, C.c_size_t, C.POINTER(ContainerDesc), C.c_char_p, C.c_size_t]),
+    "ntcb_decoder_open": (_vp, [_u8p, C.c_size_t, C.c_char_p, C.c_size_t]),
+    "ntcb_decoder_get_info": (None, [_vp, C.POINTER(ContainerDesc)]),
+    "ntcb_decoder_model": (None, [_vp, _fp, _fp]),
+    "ntcb_decoder_rgb8": (C.c_size_t, [_vp, C.c_int, C.c_int, _u8p, C.c_size_t]),
+    "ntcb_decoder_rgb8_device": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp]),
+    "ntcb_decoder_close": (None, [_vp]),
+    "ntcb_dct_tables": (None, [C.c_int, C.c_int, _fp, _ip, _ip]),
     "ntcb_pop_kernel": (C.c_int, [_vp]),
     "ntcb_fp32_peak_tflops": (C.c_double, []),
     "ntcb_footprint_ranges": (C.c_int, [C.c_int, C.c_int, C.c_int, _ip, _ip]),
