@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--fd-steps", type=int, default=100, help="FD-phase iterations timed after the ES ones (0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-cuda", action="store_true", help="skip timing the reference's own CUDA backend (oracle/_ref/ntc_ref)")
+    ap.add_argument("--shard-driver", default="native", choices=["native", "python"],
+                    help="N > 1: one library call per iteration with in-place NCCL all-gathers on the library's own communicator "
+                         "(native), or the per-phase entry points around torch.distributed all-gathers (python)")
     ap.add_argument("--pop-kernel", default="tensor", choices=["tensor", "ffma"],
                     help="ES population kernel: tcgen05 3xTF32 (default) or the bit-exact packed-FP32 one")
     return ap.parse_args()
@@ -316,11 +319,12 @@ def pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_av
     return base
 
 
-def ref_cuda_leg(cfg, n1=20, n2=120):
+def ref_cuda_leg(cfg, n1=20, span_s=6.0):
     """The reference's own CUDA backend (cuda/ntc_cuda.cu built unmodified for sm_100a, linked into the reference
-    CLI as oracle/_ref/ntc_ref) on the same configuration and GPU. Two runs of n1 and n2 ES iterations with no
-    intermediate prints: the CLI reports the elapsed time at the last iteration before its final print, so
-    (t(n2) - t(n1)) / (n2 - n1) is the per-iteration time without initialisation or printing."""
+    CLI as oracle/_ref/ntc_ref) on the same configuration and GPU. Runs of n1 and n2 ES iterations with no
+    intermediate prints: the CLI reports the elapsed time (0.1 s resolution) at the last iteration before its final
+    print, so (t(n2) - t(n1)) / (n2 - n1) is the per-iteration time without initialisation or printing. n2 is sized
+    from a first 100-iteration difference so that the difference spans about span_s seconds."""
     import re
     import tempfile
     from neural_block_textures_b200 import synth
@@ -344,20 +348,31 @@ def ref_cuda_leg(cfg, n1=20, n2=120):
             if f in ("--mlp-fd", "--iters"):
                 skip = 1; continue
             out.append(f)
-        ts = {}
-        for n in (n1, n2):
+
+        def elapsed(n):
             r = subprocess.run([str(exe), *paths, *out, "--iters", str(n), "--print-every", "100000000", "--rng", "hash", "--cuda",
                                 "--out", str(Path(d) / f"o{n}")], capture_output=True, text=True, timeout=900)
             if r.returncode != 0:
-                return {"unavailable": f"ntc_ref exited {r.returncode}: {(r.stdout + r.stderr)[-300:]}"}
+                raise RuntimeError(f"ntc_ref exited {r.returncode}: {(r.stdout + r.stderr)[-300:]}")
             m = re.findall(rf"iter\s+{n}\s.*\|\s+([0-9.]+)s \(", r.stdout)
             if not m:
-                return {"unavailable": "could not parse the reference CLI's timing line"}
-            ts[n] = float(m[-1])
-    ms = 1e3 * (ts[n2] - ts[n1]) / (n2 - n1)
+                raise RuntimeError("could not parse the reference CLI's timing line")
+            return float(m[-1])
+        try:
+            t1 = elapsed(n1)
+            t2 = elapsed(n1 + 100)
+            est = max((t2 - t1) / 100, 5e-4)
+            n2 = n1 + max(100, int(span_s / est))
+            if n2 > n1 + 100:
+                t2 = elapsed(n2)
+            else:
+                n2 = n1 + 100
+        except RuntimeError as e:
+            return {"unavailable": str(e)}
+    ms = 1e3 * (t2 - t1) / (n2 - n1)
     dec = sum(cfg.decodes_per_iter().values())
     return {"value": dec / (ms * 1e-3), "unit": "decodes/s", "ms_per_step": ms, "kind": "reference CUDA backend (ntc_ref, sm_100a)",
-            "method": f"wall clock of the reference CLI, ({n2} - {n1}) ES iterations, same synthetic input"}
+            "method": f"wall clock of the reference CLI, ({n2} - {n1}) ES iterations (0.1 s print resolution), same synthetic input"}
 
 
 def main():
@@ -391,16 +406,27 @@ def main():
     per = pair_range(N, world, rank)[1] - pair_range(N, world, rank)[0]
     L0 = spec.levels[0]
     has_lat = len(spec.levels) > 1 or not spec.qat_bits
-    sharded = None
-    if world > 1:
-        sharded = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K if has_lat else 0, image=(spec.W, spec.H),
+    sharded = native = None
+    qat = bool(spec.qat_bits)
+    Kl = K if has_lat else 0
+    if world > 1 and args.shard_driver == "native":
+        from neural_block_textures_b200.shard import NativeShardedES
+        native = NativeShardedES(tr, dist, device="cuda")
+        for mode in (1, 2):
+            ok, _, _, why = native.plan(mode, N, M, Kl, qat)
+            if not ok:
+                raise SystemExit(f"native sharded iteration does not apply: {why}")
+    elif world > 1:
+        sharded = ShardedES(tr, dist, N, device="cuda", stream=stream, K=Kl, image=(spec.W, spec.H),
                             level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None, P=spec.P)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     dec = cfg.decodes_per_iter()
     decodes = sum(dec.values())
 
     def step(it):
-        if sharded is None:
+        if native is not None:
+            native.iteration(it, 1, cfg.mlp_sigma, cfg.mlp_lr, N, M, Kl, cfg.lat_sigma, cfg.lat_lr, qat)
+        elif sharded is None:
             tr.mlp_step(it, cfg.mlp_sigma, cfg.mlp_lr, N, M)
             if has_lat:
                 tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
@@ -414,7 +440,9 @@ def main():
                 sharded.qat_search()
 
     def fd_step(it):
-        if sharded is None:
+        if native is not None:
+            native.iteration(it, 2, cfg.fd_h, cfg.mlp_lr, N, M, Kl, cfg.lat_sigma, cfg.lat_lr, qat)
+        elif sharded is None:
             tr.mlp_step_fd(it, cfg.fd_h, cfg.mlp_lr, M)
             if has_lat:
                 tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)

@@ -294,6 +294,38 @@ void ntcb_shard_lat_install(ntcb_trainer* t, int level, const float* level_dev);
 void ntcb_shard_qat(ntcb_trainer* t, int trow_begin, int trow_end, float* level0_dev);
 void ntcb_shard_qat_apply(ntcb_trainer* t, const float* level0_all_dev);
 
+/* Native sharded iteration (addition; no counterpart in the reference, whose backend runs on one GPU).
+ * One call runs the body of the reference trainer's CUDA loop (main.cpp:4121-4137: mlp_step or mlp_step_fd,
+ * lat_step, qat_search) over `world` ranks, one process and one GPU per rank, with the library's own NCCL
+ * communicator: the same per-rank work as the ntcb_shard_* pairs above, each exchange an in-place NCCL
+ * all-gather on the trainer's stream into the trainer's own buffers (the ES blocks, the updated latent level
+ * or the loss-difference planes, level 0), so nothing crosses the host. The ranks end bit-identical to one GPU
+ * running the plain steps.
+ *
+ * NCCL is loaded with dlopen("libnccl.so.2") on first use. Rank 0 makes an id with ntcb_comm_unique_id and
+ * hands its NTCB_COMM_ID_BYTES bytes to the other ranks (any host channel); every rank then calls
+ * ntcb_comm_create with the device of its trainer current. Both return 0 / NULL with a reason on failure.
+ * NCCL errors inside an iteration print and exit the process, like every other runtime failure. */
+#define NTCB_COMM_ID_BYTES 128
+typedef struct ntcb_comm ntcb_comm;
+int ntcb_comm_unique_id(unsigned char* id, char* why, size_t why_cap);
+ntcb_comm* ntcb_comm_create(const unsigned char* id, int world, int rank, char* why, size_t why_cap);
+void ntcb_comm_destroy(ntcb_comm* c);
+int ntcb_nccl_version(void);
+/* Whether ntcb_shard_iteration applies (1) or not (0, reason in why), and which exchange it uses:
+ * *mlp_exchange 1 = per-rank blocks of fitness + ES gradient segments (each rank's pair range a whole number of
+ * 64-pair segments, N > 256), 2 = fitness only (every rank regenerates all N pairs' noise for the gradient);
+ * *lat_exchange 1 = texel rows (ntcb_shard_lat_plan applies), 2 = pixel rows (the image height splits evenly),
+ * 0 = no latent step. mlp_mode: 0 none, 1 ES (mlp_step), 2 FD (mlp_step_fd). K = 0 skips the latent step, which
+ * is also skipped when no level is ES-trained (--qat with one level); qat != 0 runs the selector search. */
+int ntcb_shard_iteration_plan(const ntcb_trainer* t, int world, int rank, int mlp_mode, int N, int M, int K, int qat,
+                              int* mlp_exchange, int* lat_exchange, char* why, size_t why_cap);
+/* One iteration: mlp_mode 1 = mlp_step(it, mlp_sigma, mlp_lr, N, M), 2 = mlp_step_fd(it, h = mlp_sigma, mlp_lr, M);
+ * then lat_step(it, lat_sigma, lat_lr, K) and qat_search() as above. The communicator's device must be the
+ * trainer's. Asynchronous on the trainer's stream like the single-GPU steps. */
+void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, float mlp_sigma, float mlp_lr, int N, int M, int K,
+                          float lat_sigma, float lat_lr, int qat);
+
 #ifdef __cplusplus
 }
 #endif

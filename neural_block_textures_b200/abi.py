@@ -171,7 +171,17 @@ SIGNATURES = {
     "ntcb_shard_lat_apply": (None, [_vp, C.c_int, C.c_float, C.c_float, C.c_int, _vp, C.c_int]),
     "ntcb_shard_qat": (None, [_vp, C.c_int, C.c_int, _vp]),
     "ntcb_shard_qat_apply": (None, [_vp, _vp]),
+    "ntcb_comm_unique_id": (C.c_int, [C.POINTER(C.c_ubyte), C.c_char_p, C.c_size_t]),
+    "ntcb_comm_create": (_vp, [C.POINTER(C.c_ubyte), C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
+    "ntcb_comm_destroy": (None, [_vp]),
+    "ntcb_nccl_version": (C.c_int, []),
+    "ntcb_shard_iteration_plan": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _ip, _ip, C.c_char_p,
+                                            C.c_size_t]),
+    "ntcb_shard_iteration": (None, [_vp, _vp, C.c_int, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float,
+                                    C.c_int]),
 }
+
+COMM_ID_BYTES = 128   # NTCB_COMM_ID_BYTES
 
 _lib = None
 

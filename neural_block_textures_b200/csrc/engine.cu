@@ -19,6 +19,7 @@
 #include "../../include/ntc_cuda.h"
 #include "kernels.h"
 #include "kernels_snap.h"
+#include "nccl_link.h"
 
 // The C description structs are the C++ ones byte for byte (main.cpp fills the C++ ones; FFI callers the C ones).
 static_assert(sizeof(ntcb_level_desc) == sizeof(ntc_cuda::LevelDesc), "LevelDesc layout");
@@ -79,6 +80,7 @@ struct Trainer::Impl {
     bool tensor_pop = true;
     int* tc_err = nullptr;   // device flag the tensor-core kernel sets when an MMA completion wait times out
     float* gpart = nullptr; long long gpart_cap = 0;
+    char* xbuf = nullptr; long long xbuf_cap = 0;   // exchange blocks of the native sharded iteration ([rank][block])
     float* qat_grid = nullptr; int* qat_bits = nullptr;
     // progress-print statistics: the last set_qes description (host copy) and a device scratch buffer
     ntc_cuda::QesDesc qes_host{};
@@ -208,6 +210,12 @@ void ensure_lat(Impl& I, int K) {
         NTCB_CHECK(cudaMemsetAsync(I.ddbits, 0, (size_t)I.ddbits_cap * sizeof(int32_t), I.stream));
     }
 }
+void ensure_xbuf(Impl& I, long long bytes) {
+    if (bytes <= I.xbuf_cap) return;
+    dfree(I.xbuf);
+    I.xbuf = dalloc<char>((size_t)bytes);
+    I.xbuf_cap = bytes;
+}
 void ensure_gpart(Impl& I, long long need) {
     if (need <= I.gpart_cap) return;
     dfree(I.gpart);
@@ -252,7 +260,7 @@ void free_all(Impl& I) {
     dfree(I.dsym); dfree(I.dcode); dfree(I.dsteps); dfree(I.dlam); dfree(I.dbits); dfree(I.ddbits); dfree(I.dcnt);
     dfree(I.w); dfree(I.wgrad); dfree(I.wm); dfree(I.wv); dfree(I.tgt); dfree(I.img);
     dfree(I.bidx); dfree(I.feat_t); dfree(I.tgt_t); dfree(I.mlp_eps); dfree(I.part);
-    dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart); dfree(I.tc_err);
+    dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart); dfree(I.xbuf); I.xbuf_cap = 0; dfree(I.tc_err);
     dfree(I.qat_grid); dfree(I.qat_bits); dfree(I.stats_buf); I.stats_cap = 0;
     for (auto& p : I.pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     I.pending.clear();
@@ -532,9 +540,9 @@ void fd_eval_part(Impl& I, int it, float h, int M, int j0, int j1, double* fit) 
     timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, j1 - j0, chunks, norm, fit); });
 }
 
-// FD gradient from the (lp, lm) of all P weights in I.fit and the Adam step.
-void fd_apply(Impl& I, float h, float lr) {
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_fd_reduce(I.stream, I.fit, I.w, h, I.P, I.dl, I.hh); });
+// FD gradient from the (lp, lm) of all P weights (weight order; I.fit unless given) and the Adam step.
+void fd_apply(Impl& I, float h, float lr, const double* fit = nullptr) {
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_fd_reduce(I.stream, fit ? fit : I.fit, I.w, h, I.P, I.dl, I.hh); });
     timed(I, "mlp_grad", 1, [&] {
         I.mlp_t++;
         float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
@@ -795,6 +803,72 @@ size_t copy_out(const Impl& I, const T* dev, size_t count, T* out, size_t cap) {
         check_tc_err(I);
     }
     return count;
+}
+
+// ---------------------------------------------------------------------- population sharding (one rank's part)
+// Size of a rank's ES block for pairs [p0, p1): 2 doubles per pair + P floats per gradient segment; -1 when the
+// range is not aligned to the segments (or the population is one segment).
+long long es_block_bytes(const Impl& I, int N, int p0, int p1) {
+    const int seglen = es_seglen(N), n = p1 - p0;
+    if (!I.ready || N <= 256 || n <= 0 || p0 % seglen || n % seglen) return -1;
+    return 16LL * n + 4LL * (n / seglen) * I.P;
+}
+
+// Pairs [p0, p1) of step `it`: minibatch, noise, population, and this rank's block = [fitness | segment sums].
+void shard_mlp_eval_grad_impl(Impl& I, int it, float sigma, int N, int M, int p0, int p1, void* block) {
+    const int n = p1 - p0, seglen = es_seglen(N);
+    double* fit = static_cast<double*>(block);
+    float* part = reinterpret_cast<float*>(static_cast<char*>(block) + 16LL * n);
+    draw_batch(I, it, M);
+    es_eval_pairs(I, it, sigma, M, p0, p1, fit);
+    // this rank's pairs' loss differences and their gradient segments (the noise of these pairs is in mlp_eps)
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit, n, I.dl, I.lsum); });
+    const float scale = 1.0f / (2.0f * (float)N * sigma);
+    timed(I, "mlp_grad", 1, [&] { ntcb::launch_es_grad_partial(I.stream, I.dl, I.mlp_eps, n, I.P, scale, seglen, part); });
+}
+
+// All ranks' blocks ([rank][block], rank order = pair order) -> the fitness of all N pairs, the segment sums in
+// order, the ES gradient and Adam.
+void shard_mlp_apply_grad_impl(Impl& I, float lr, int N, const void* blocks, int world) {
+    const int n = N / world, seglen = es_seglen(N);
+    const long long bytes = es_block_bytes(I, N, 0, n);
+    const size_t fit_bytes = 16 * (size_t)n, part_bytes = (size_t)bytes - fit_bytes;
+    const int nseg = N / seglen;
+    ensure_gpart(I, (long long)nseg * I.P);
+    const char* src = static_cast<const char*>(blocks);
+    // [rank][fitness | partials] -> fitness of all N pairs in pair order, partials of all segments in order
+    NTCB_CHECK(cudaMemcpy2DAsync(I.fit, fit_bytes, src, (size_t)bytes, fit_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
+    NTCB_CHECK(cudaMemcpy2DAsync(I.gpart, part_bytes, src + fit_bytes, (size_t)bytes, part_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
+    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, I.fit, N, I.dl, I.lsum); });
+    timed(I, "mlp_grad", 1, [&] {
+        I.mlp_t++;
+        float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
+        ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
+    });
+    I.last_N = N; I.last_fd = false; I.last_pairs = N;
+}
+
+// Texel-row latent step of one rank (plan from lat_rows_plan): pixel rows [pa, pb) of all K pairs, gathers and
+// Adam of texel rows [ta, tb) of level lvl, in place in the latent. Returns the float offset of those rows.
+long long shard_lat_rows_impl(Impl& I, float sigma, float lr, int K, int lvl, int ta, int tb, int pa, int pb) {
+    const auto& L = I.d.lv[lvl];
+    ensure_lat(I, K);
+    const long long W = I.d.W;
+    lat_eval_part(I, sigma, K, (long long)pa * W, (long long)pb * W, I.dpix, (long long)(pb - pa) * W);
+    const long long off = (long long)L.off + (long long)ta * L.W * L.C, n = (long long)(tb - ta) * L.W * L.C;
+    NTCB_CHECK(cudaMemsetAsync(I.zgrad + off, 0, n * sizeof(float), I.stream));
+    const float scale = 1.0f / (2.0f * (float)K * sigma);
+    timed(I, "lat_gather", 1, [&] {
+        ntcb::launch_lat_gather(I.stream, I.dm, lvl, I.lvl_xr[lvl], I.lvl_yr[lvl], I.dpix, I.lat_eps, I.nz, K, scale,
+                                ntcb::RateTerm{nullptr, 0.0f, 0, 0}, I.zgrad, pb - pa, ta, tb, pa);
+    });
+    timed(I, "adam", 1, [&] {
+        I.lat_t++;
+        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
+        ntcb::launch_adam(I.stream, I.z + off, I.zgrad + off, I.zm + off, I.zv + off, n, lr, c1, c2);
+    });
+    I.lat_step_no++;
+    return off;
 }
 
 }  // namespace
@@ -1076,23 +1150,8 @@ void ntcb_shard_lat_step_rows(ntcb_trainer* t, int it, float sigma, float lr, in
     require_ready(I); set_device(I);
     int lvl, ta, tb, pa, pb;
     if (K < 1 || !lat_rows_plan(I, world, rank, lvl, ta, tb, pa, pb)) die("shard_lat_step_rows: the texel-row plan does not apply");
-    const auto& L = I.d.lv[lvl];
-    ensure_lat(I, K);
-    const long long W = I.d.W;
-    lat_eval_part(I, sigma, K, (long long)pa * W, (long long)pb * W, I.dpix, (long long)(pb - pa) * W);
-    const long long off = (long long)L.off + (long long)ta * L.W * L.C, n = (long long)(tb - ta) * L.W * L.C;
-    NTCB_CHECK(cudaMemsetAsync(I.zgrad + off, 0, n * sizeof(float), I.stream));
-    const float scale = 1.0f / (2.0f * (float)K * sigma);
-    timed(I, "lat_gather", 1, [&] {
-        ntcb::launch_lat_gather(I.stream, I.dm, lvl, I.lvl_xr[lvl], I.lvl_yr[lvl], I.dpix, I.lat_eps, I.nz, K, scale,
-                                ntcb::RateTerm{nullptr, 0.0f, 0, 0}, I.zgrad, pb - pa, ta, tb, pa);
-    });
-    timed(I, "adam", 1, [&] {
-        I.lat_t++;
-        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
-        ntcb::launch_adam(I.stream, I.z + off, I.zgrad + off, I.zm + off, I.zv + off, n, lr, c1, c2);
-    });
-    I.lat_step_no++;
+    const long long off = shard_lat_rows_impl(I, sigma, lr, K, lvl, ta, tb, pa, pb);
+    const long long n = (long long)(tb - ta) * I.d.lv[lvl].W * I.d.lv[lvl].C;
     NTCB_CHECK(cudaMemcpyAsync(zblock_dev, I.z + off, n * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
 }
 void ntcb_shard_lat_install(ntcb_trainer* t, int level, const float* level_dev) {
@@ -1190,48 +1249,22 @@ void ntcb_shard_fd_apply(ntcb_trainer* t, float h, float lr, const double* fit_a
     fd_apply(I, h, lr);
 }
 long long ntcb_shard_es_block_bytes(const ntcb_trainer* t, int N, int pair_begin, int pair_end) {
-    const Impl& I = t->impl;
-    const int seglen = es_seglen(N), n = pair_end - pair_begin;
-    if (!I.ready || N <= 256 || n <= 0 || pair_begin % seglen || n % seglen) return -1;
-    return 16LL * n + 4LL * (n / seglen) * I.P;
+    return es_block_bytes(t->impl, N, pair_begin, pair_end);
 }
 void ntcb_shard_mlp_eval_grad(ntcb_trainer* t, int it, float sigma, int N, int M, int pair_begin, int pair_end, void* block_dev) {
     Impl& I = t->impl;
     require_ready(I); set_device(I);
-    if (ntcb_shard_es_block_bytes(t, N, pair_begin, pair_end) < 0 || N > I.pairs_cap || M > I.Mcap || M < 1)
+    if (es_block_bytes(I, N, pair_begin, pair_end) < 0 || N > I.pairs_cap || M > I.Mcap || M < 1)
         die("shard_mlp_eval_grad: pair range not aligned to gradient segments, or sizes outside the buffers sized at init");
-    const int n = pair_end - pair_begin, seglen = es_seglen(N);
-    double* fit = static_cast<double*>(block_dev);
-    float* part = reinterpret_cast<float*>(static_cast<char*>(block_dev) + 16LL * n);
-    draw_batch(I, it, M);
-    es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit);
-    // this rank's pairs' loss differences and their gradient segments (the noise of these pairs is in mlp_eps)
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit, n, I.dl, I.lsum); });
-    const float scale = 1.0f / (2.0f * (float)N * sigma);
-    timed(I, "mlp_grad", 1, [&] { ntcb::launch_es_grad_partial(I.stream, I.dl, I.mlp_eps, n, I.P, scale, seglen, part); });
+    shard_mlp_eval_grad_impl(I, it, sigma, N, M, pair_begin, pair_end, block_dev);
 }
 void ntcb_shard_mlp_apply_grad(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const void* blocks_dev, int world) {
     (void)it; (void)sigma; (void)M;
     Impl& I = t->impl;
     require_ready(I); set_device(I);
     if (world < 1 || N % world || N > I.pairs_cap) die("shard_mlp_apply_grad: N must split evenly over the ranks and fit the buffers");
-    const int n = N / world, seglen = es_seglen(N);
-    const long long bytes = ntcb_shard_es_block_bytes(t, N, 0, n);
-    if (bytes < 0) die("shard_mlp_apply_grad: the ranks' pair ranges are not aligned to gradient segments");
-    const size_t fit_bytes = 16 * (size_t)n, part_bytes = (size_t)bytes - fit_bytes;
-    const int nseg = N / seglen;
-    ensure_gpart(I, (long long)nseg * I.P);
-    const char* src = static_cast<const char*>(blocks_dev);
-    // [rank][fitness | partials] -> fitness of all N pairs in pair order, partials of all segments in order
-    NTCB_CHECK(cudaMemcpy2DAsync(I.fit, fit_bytes, src, (size_t)bytes, fit_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
-    NTCB_CHECK(cudaMemcpy2DAsync(I.gpart, part_bytes, src + fit_bytes, (size_t)bytes, part_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, I.fit, N, I.dl, I.lsum); });
-    timed(I, "mlp_grad", 1, [&] {
-        I.mlp_t++;
-        float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
-        ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
-    });
-    I.last_N = N; I.last_fd = false; I.last_pairs = N;
+    if (es_block_bytes(I, N, 0, N / world) < 0) die("shard_mlp_apply_grad: the ranks' pair ranges are not aligned to gradient segments");
+    shard_mlp_apply_grad_impl(I, lr, N, blocks_dev, world);
 }
 void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N, int M, const double* fit_all_dev) {
     Impl& I = t->impl;
@@ -1240,6 +1273,140 @@ void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N,
     (void)M;
     NTCB_CHECK(cudaMemcpyAsync(I.fit, fit_all_dev, 2 * (size_t)N * sizeof(double), cudaMemcpyDeviceToDevice, I.stream));
     es_apply(I, it, sigma, lr, N, I.fit, true);
+}
+
+// ---------------------------------------------------------------------- native sharded iteration (NCCL)
+struct ntcb_comm { void* nc = nullptr; int world = 1, rank = 0, device = -1; };
+
+static void set_why(char* why, size_t cap, const std::string& r) {
+    if (why && cap) { strncpy(why, r.c_str(), cap - 1); why[cap - 1] = 0; }
+}
+int ntcb_comm_unique_id(unsigned char* id, char* why, size_t why_cap) {
+    std::string r;
+    if (!id) { set_why(why, why_cap, "null id buffer"); return 0; }
+    if (!ntcb::nccl::unique_id(id, r)) { set_why(why, why_cap, r); return 0; }
+    return 1;
+}
+ntcb_comm* ntcb_comm_create(const unsigned char* id, int world, int rank, char* why, size_t why_cap) {
+    if (!id || world < 1 || rank < 0 || rank >= world) { set_why(why, why_cap, "bad id, world size or rank"); return nullptr; }
+    int dev = -1;
+    NTCB_CHECK(cudaGetDevice(&dev));
+    std::string r;
+    void* nc = ntcb::nccl::comm_init(id, world, rank, r);
+    if (!nc) { set_why(why, why_cap, r); return nullptr; }
+    ntcb_comm* c = new ntcb_comm();
+    c->nc = nc; c->world = world; c->rank = rank; c->device = dev;
+    return c;
+}
+void ntcb_comm_destroy(ntcb_comm* c) {
+    if (!c) return;
+    int prev = -1;
+    NTCB_CHECK(cudaGetDevice(&prev));
+    NTCB_CHECK(cudaSetDevice(c->device));
+    ntcb::nccl::comm_destroy(c->nc);
+    NTCB_CHECK(cudaSetDevice(prev));
+    delete c;
+}
+int ntcb_nccl_version(void) { return ntcb::nccl::version(); }
+
+// Which exchange each phase of ntcb_shard_iteration uses for this model and world size (0 = refused, reason in
+// why): mlp 1 = segment blocks (fitness + ES gradient segments), 2 = fitness only (every rank regenerates all
+// noise for the gradient); latent 1 = texel rows (the updated level), 2 = pixel rows (the K loss-difference
+// planes); FD and selector search have one form each.
+static int iteration_plan(const Impl& I, int world, int rank, int mlp_mode, int N, int M, int K, int qat, int& mlp_x, int& lat_x,
+                          std::string& why) {
+    mlp_x = 0; lat_x = 0;
+    if (!I.ready) { why = "trainer not initialised"; return 0; }
+    if (world < 1 || rank < 0 || rank >= world) { why = "bad world size or rank"; return 0; }
+    if (mlp_mode < 0 || mlp_mode > 2) { why = "mlp mode must be 0 (none), 1 (ES) or 2 (FD)"; return 0; }
+    if (mlp_mode != 0 && (M < 1 || M > I.Mcap)) { why = "minibatch outside the buffers sized at init"; return 0; }
+    if (mlp_mode == 1) {
+        if (N < 1 || N > I.pairs_cap || N % world) { why = "the ES pairs must split evenly over the ranks and fit the buffers sized at init"; return 0; }
+        mlp_x = es_block_bytes(I, N, rank * (N / world), (rank + 1) * (N / world)) > 0 ? 1 : 2;
+    }
+    if (K > 0 && lat_mask(I)) {
+        int lvl, ta, tb, pa, pb;
+        if (lat_rows_plan(I, world, rank, lvl, ta, tb, pa, pb)) lat_x = 1;
+        else if (I.d.H % world == 0) lat_x = 2;
+        else { why = "the image height does not split evenly over the ranks"; return 0; }
+    }
+    if (qat) {
+        if (I.d.qat <= 0) { why = "selector search requested for a model without --qat"; return 0; }
+        if (I.d.lv[0].H % world) { why = "the level-0 rows do not split evenly over the ranks"; return 0; }
+    }
+    return 1;
+}
+
+int ntcb_shard_iteration_plan(const ntcb_trainer* t, int world, int rank, int mlp_mode, int N, int M, int K, int qat, int* mlp_exchange,
+                              int* lat_exchange, char* why, size_t why_cap) {
+    int mx = 0, lx = 0;
+    std::string r;
+    const int ok = iteration_plan(t->impl, world, rank, mlp_mode, N, M, K, qat, mx, lx, r);
+    if (mlp_exchange) *mlp_exchange = mx;
+    if (lat_exchange) *lat_exchange = lx;
+    if (!ok) set_why(why, why_cap, r);
+    return ok;
+}
+
+void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, float mlp_sigma, float mlp_lr, int N, int M, int K,
+                          float lat_sigma, float lat_lr, int qat) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (!c || c->device != I.device) die("shard_iteration: no communicator, or one made on another device");
+    const int G = c->world, r = c->rank;
+    int mx = 0, lx = 0;
+    std::string why;
+    if (!iteration_plan(I, G, r, mlp_mode, N, M, K, qat, mx, lx, why)) die(("shard_iteration: " + why).c_str());
+    auto gather = [&](void* buf, size_t bytes) {
+        timed(I, "exchange", 0, [&] { ntcb::nccl::all_gather_inplace(c->nc, buf, bytes, r, I.stream); });
+    };
+    // MLP step (mlp_step / mlp_step_fd)
+    if (mlp_mode == 1) {
+        const int n = N / G, p0 = r * n;
+        if (mx == 1) {
+            const long long block = es_block_bytes(I, N, p0, p0 + n);
+            ensure_xbuf(I, block * G);
+            shard_mlp_eval_grad_impl(I, it, mlp_sigma, N, M, p0, p0 + n, I.xbuf + (long long)r * block);
+            gather(I.xbuf, (size_t)block);
+            shard_mlp_apply_grad_impl(I, mlp_lr, N, I.xbuf, G);
+        } else {
+            const size_t bytes = 16 * (size_t)n;
+            ensure_xbuf(I, (long long)bytes * G);
+            draw_batch(I, it, M);
+            es_eval_pairs(I, it, mlp_sigma, M, p0, p0 + n, reinterpret_cast<double*>(I.xbuf + (size_t)r * bytes));
+            gather(I.xbuf, bytes);
+            es_apply(I, it, mlp_sigma, mlp_lr, N, reinterpret_cast<const double*>(I.xbuf), true);
+        }
+    } else if (mlp_mode == 2) {
+        const int B = (I.P + G - 1) / G, j0 = std::min(r * B, I.P), j1 = std::min((r + 1) * B, I.P);
+        const size_t bytes = 2 * (size_t)B * sizeof(double);
+        ensure_xbuf(I, (long long)bytes * G);
+        fd_eval_part(I, it, mlp_sigma, M, j0, j1, reinterpret_cast<double*>(I.xbuf + (size_t)r * bytes));
+        gather(I.xbuf, bytes);
+        fd_apply(I, mlp_sigma, mlp_lr, reinterpret_cast<const double*>(I.xbuf));
+    }
+    // latent ES step (lat_step)
+    if (lx == 1) {
+        int lvl, ta, tb, pa, pb;
+        lat_rows_plan(I, G, r, lvl, ta, tb, pa, pb);
+        shard_lat_rows_impl(I, lat_sigma, lat_lr, K, lvl, ta, tb, pa, pb);
+        const auto& L = I.d.lv[lvl];
+        gather(I.z + L.off, (size_t)(tb - ta) * L.W * L.C * sizeof(float));
+    } else if (lx == 2) {
+        const int rows = I.d.H / G;
+        const long long plane = (long long)rows * I.d.W;
+        ensure_lat(I, K);
+        lat_eval_part(I, lat_sigma, K, (long long)r * plane, (long long)(r + 1) * plane, I.dpix + (long long)r * K * plane, plane);
+        gather(I.dpix, (size_t)K * plane * sizeof(float));
+        lat_apply_part(I, lat_sigma, lat_lr, K, I.dpix, rows);
+    }
+    // selector search (qat_search)
+    if (qat) {
+        const long long LW = I.d.lv[0].W, LC = I.d.lv[0].C, rows = I.d.lv[0].H / G;
+        qat_rows_part(I, r * rows * LW, (r + 1) * rows * LW);
+        gather(I.zdec + I.dm.lv[0].off, (size_t)(rows * LW * LC) * sizeof(float));
+        qat_copy_back(I);
+    }
 }
 
 }  // extern "C"

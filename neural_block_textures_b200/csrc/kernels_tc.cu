@@ -228,6 +228,10 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
     __shared__ uint32_t tbase;
     __shared__ double red[NS][4];
     const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
+    // The warp that issues a stream's MMAs: local warp g % 4, i.e. global warp 4 g + g % 4, so the streams'
+    // issue work spreads over the SM's four schedulers (warp w runs on scheduler w % 4) instead of all
+    // landing on scheduler 0.
+    const int issuer = g & 3;
     const int bar_id = 1 + g;
     float* sw = dyn + g * 2 * T::SIGN;
     uint64_t* bar = &bars[g];
@@ -305,7 +309,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb0 + T::oB1h * 4, sb0 + T::oB1l * 4, bar);
+        if (warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb0 + T::oB1h * 4, sb0 + T::oB1l * 4, bar);
 
 #pragma unroll 1
         for (int base = row0; base < row1; base += kTcRows) {
@@ -338,7 +342,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 tc::fence_before_sync();
                 ok = stream_sync_and(bar_id, ok);
                 if (!ok) break;
-                if (warp == 0) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+                if (warp == issuer) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
                 // layer 2 result -> registers
                 wait_mma();
 #pragma unroll
@@ -362,7 +366,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     tc::fence_before_sync();
                     ok = stream_sync_and(bar_id, ok);
                     if (!ok) break;
-                    if (warp == 0) {
+                    if (warp == issuer) {
                         issue3<T::K3, T::N3>(tb + T::cD3, tb + T::cHh, tb + T::cHl, sb + T::oB3h * 4, sb + T::oB3l * 4, bar3);
                         if (next) {
                             const uint32_t nb = sg ? sb0 : sb1;
@@ -390,7 +394,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     tc::fence_before_sync();
                     ok = stream_sync_and(bar_id, ok);
                     if (!ok) break;
-                    if (next && warp == 0) {
+                    if (next && warp == issuer) {
                         const uint32_t nb = sg ? sb0 : sb1;
                         issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
                     }
@@ -460,6 +464,10 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
     __shared__ __align__(8) uint64_t bars[T::STREAMS];
     __shared__ uint32_t tbase;
     const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
+    // The warp that issues a stream's MMAs: local warp g % 4, i.e. global warp 4 g + g % 4, so the streams'
+    // issue work spreads over the SM's four schedulers (warp w runs on scheduler w % 4) instead of all
+    // landing on scheduler 0.
+    const int issuer = g & 3;
     const int bar_id = 1 + g;
     uint64_t* bar = &bars[g];
 
@@ -527,7 +535,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
-        if (ok && warp == 0) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+        if (ok && warp == issuer) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
     };
 
     if (i0 < i1) {
@@ -536,7 +544,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        if (warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
     }
 #pragma unroll 1
     for (long long item = i0; item < i1 && ok; item++) {
@@ -556,7 +564,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
-        if (warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        if (warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
         const float ep = out_layer_error<S>(m, sw, h, t, leak);
         // - unit
         layer1_to_layer2();
@@ -569,7 +577,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
-        if (more && warp == 0) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        if (more && warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
         const float em = out_layer_error<S>(m, sw, h, t, leak);
         {
             const int k = (int)(item / ntiles);

@@ -151,3 +151,33 @@ class ShardedES:
         with self._ctx():
             self.dist.all_gather_into_tensor(self.l0, self.l0[a:b])
         self.t.shard_qat_apply(self.l0)
+
+
+class NativeShardedES:
+    """One ES training iteration per call in the library (ntcb_shard_iteration): the same per-rank work and
+    exchanges as ShardedES, but every exchange is an in-place NCCL all-gather the library issues on the trainer's
+    stream into the trainer's own buffers, on a communicator of its own. torch.distributed only carries the
+    128-byte NCCL id from rank 0 to the others (any backend)."""
+
+    def __init__(self, trainer, dist, device=None):
+        import torch
+        from .trainer import Comm
+        self.t, self.dist = trainer, dist
+        self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        uid = torch.zeros(128, dtype=torch.uint8, device=device or "cpu")
+        if self.rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(Comm.unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        self.comm = Comm(bytes(uid.cpu().numpy().tobytes()), self.world, self.rank)
+
+    def plan(self, mlp_mode: int, N: int, M: int, K: int, qat: bool):
+        return self.t.shard_iteration_plan(self.world, self.rank, mlp_mode, N, M, K, qat)
+
+    def iteration(self, it: int, mlp_mode: int, mlp_sigma: float, mlp_lr: float, N: int, M: int, K: int, lat_sigma: float,
+                  lat_lr: float, qat: bool) -> None:
+        """mlp_mode 1: mlp_step (sigma, lr, N pairs, M rows), 2: mlp_step_fd (h = mlp_sigma); then lat_step (K pairs; 0
+        skips it) and, with qat, qat_search."""
+        self.t.shard_iteration(self.comm, it, mlp_mode, mlp_sigma, mlp_lr, N, M, K, lat_sigma, lat_lr, qat)
+
+    def close(self) -> None:
+        self.comm.close()

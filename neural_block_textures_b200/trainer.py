@@ -262,6 +262,54 @@ class Trainer:
     def shard_qat_apply(self, level0_all_dev) -> None:
         self.lib.ntcb_shard_qat_apply(self.h, C.c_void_p(_dptr(level0_all_dev)))
 
+    # ---- native sharded iteration (addition): one call per iteration, the library's own NCCL communicator
+    def shard_iteration_plan(self, world: int, rank: int, mlp_mode: int, N: int, M: int, K: int, qat: bool):
+        """(ok, mlp_exchange, lat_exchange, reason) of ntcb_shard_iteration for this model (include/ntc_b200.h)."""
+        mx, lx = C.c_int(0), C.c_int(0)
+        why = C.create_string_buffer(256)
+        ok = self.lib.ntcb_shard_iteration_plan(self.h, world, rank, mlp_mode, N, M, K, int(qat), C.byref(mx), C.byref(lx), why, 256)
+        return bool(ok), mx.value, lx.value, why.value.decode()
+
+    def shard_iteration(self, comm: "Comm", it: int, mlp_mode: int, mlp_sigma: float, mlp_lr: float, N: int, M: int, K: int,
+                        lat_sigma: float, lat_lr: float, qat: bool) -> None:
+        self.lib.ntcb_shard_iteration(self.h, comm.h, it, mlp_mode, mlp_sigma, mlp_lr, N, M, K, lat_sigma, lat_lr, int(qat))
+
+
+class Comm:
+    """The library's NCCL communicator (ntcb_comm_*): `uid` is the id rank 0 made with Comm.unique_id(), handed to
+    every rank; create it with the rank's device current."""
+
+    def __init__(self, uid: bytes, world: int, rank: int) -> None:
+        self.lib = abi.load_library()
+        if len(uid) != abi.COMM_ID_BYTES:
+            raise ValueError("NCCL unique id must be %d bytes" % abi.COMM_ID_BYTES)
+        why = C.create_string_buffer(256)
+        buf = (C.c_ubyte * abi.COMM_ID_BYTES).from_buffer_copy(uid)
+        self.h = self.lib.ntcb_comm_create(buf, world, rank, why, 256)
+        if not self.h:
+            raise RuntimeError("ntcb_comm_create: " + why.value.decode())
+        self.world, self.rank = world, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        lib = abi.load_library()
+        buf = (C.c_ubyte * abi.COMM_ID_BYTES)()
+        why = C.create_string_buffer(256)
+        if not lib.ntcb_comm_unique_id(buf, why, 256):
+            raise RuntimeError("ntcb_comm_unique_id: " + why.value.decode())
+        return bytes(buf)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.ntcb_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
 
 def _dptr(x) -> int:
     return x if isinstance(x, int) else x.data_ptr()

@@ -1,7 +1,10 @@
-"""Population / weight (FD) / image / texel-row sharding on 2 GPUs over NCCL (neural_block_textures_b200.shard.ShardedES, the code
-bench.py runs with torchrun): two ranks must end with the same weights and latent as one GPU running the plain
-Trainer steps, bit for bit (every per-pair, per-pixel and per-texel value is computed by the same kernels
-whichever rank computes it, and the gradient sums keep their order). Needs >= 2 GPUs; skipped otherwise."""
+"""Population / weight (FD) / image / texel-row sharding over NCCL, through both drivers bench.py can use under
+torchrun: ShardedES (per-phase entry points around torch.distributed all-gathers) and NativeShardedES (one
+ntcb_shard_iteration call per iteration, in-place all-gathers on the library's own NCCL communicator). The ranks
+must end with the same weights and latent as one GPU running the plain Trainer steps, bit for bit (every per-pair,
+per-pixel and per-texel value is computed by the same kernels whichever rank computes it, and the gradient sums
+keep their order). The two-rank cases need >= 2 GPUs and are skipped otherwise; the one-rank native case runs on
+one GPU."""
 import os
 import socket
 
@@ -29,7 +32,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, driver="python"):
     import datetime
     import torch
     import torch.distributed as dist
@@ -48,15 +51,26 @@ def _rank_main(rank, world, port, out_dir):
         stream = torch.cuda.Stream()
         tr.set_stream(stream.cuda_stream)
         L0 = spec.levels[0]
-        es = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K, image=(spec.W, spec.H), level0=(L0.W, L0.H, L0.C),
-                       P=spec.P)
-        assert es.block > 0
-        for it in range(1, ITERS + 1):
-            es.step(it, 0.02, 0.005, M)
-            es.lat_step(it, 0.05, 0.02, K)
-            es.qat_search()
-        es.fd_step(ITERS + 1, 1e-3, 0.005, M)
-        zz, pp = tr.download_model()
+        if driver == "native":
+            from neural_block_textures_b200.shard import NativeShardedES
+            nat = NativeShardedES(tr, dist, device="cuda")
+            ok, mx, lx, why = nat.plan(1, N, M, K, True)
+            assert ok and mx == 1 and lx == 1, why
+            for it in range(1, ITERS + 1):
+                nat.iteration(it, 1, 0.02, 0.005, N, M, K, 0.05, 0.02, True)
+            nat.iteration(ITERS + 1, 2, 1e-3, 0.005, N, M, 0, 0.0, 0.0, False)
+            zz, pp = tr.download_model()
+            nat.close()
+        else:
+            es = ShardedES(tr, dist, N, device="cuda", stream=stream, K=K, image=(spec.W, spec.H), level0=(L0.W, L0.H, L0.C),
+                           P=spec.P)
+            assert es.block > 0
+            for it in range(1, ITERS + 1):
+                es.step(it, 0.02, 0.005, M)
+                es.lat_step(it, 0.05, 0.02, K)
+                es.qat_search()
+            es.fd_step(ITERS + 1, 1e-3, 0.005, M)
+            zz, pp = tr.download_model()
         np.save(os.path.join(out_dir, f"z{rank}.npy"), zz)
         np.save(os.path.join(out_dir, f"p{rank}.npy"), pp)
         tr.close()
@@ -65,19 +79,8 @@ def _rank_main(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device):
-    import torch
-    import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    ctx = mp.get_context("spawn")
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
-    for pr in procs:
-        pr.start()
-    for pr in procs:
-        pr.join(timeout=300)
-        assert pr.exitcode == 0
+def _one_gpu_reference():
+    """Weights and latent after the plain single-GPU steps the sharded runs must reproduce."""
     from neural_block_textures_b200 import Trainer
     spec = _spec()
     z, p = spec.init_params()
@@ -90,6 +93,65 @@ def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device):
             tr.qat_search()
         tr.mlp_step_fd(ITERS + 1, 1e-3, 0.005, M)
         z1, p1 = tr.download_model()
+    return z, p, z1, p1
+
+
+def test_native_iteration_one_rank_matches_plain_steps(cuda_device):
+    """ntcb_shard_iteration on a one-rank communicator (its all-gathers are identities) runs the same kernels as the
+    plain steps; the result must be identical."""
+    from neural_block_textures_b200 import Trainer
+    from neural_block_textures_b200.trainer import Comm
+    z, p, z1, p1 = _one_gpu_reference()
+    spec = _spec()
+    comm = Comm(Comm.unique_id(), 1, 0)
+    try:
+        with Trainer() as tr:
+            ok, why = tr.init(spec.model_desc(), z, p, _target(spec))
+            assert ok, why
+            ok, mx, lx, why = tr.shard_iteration_plan(1, 0, 1, N, M, K, True)
+            assert ok and mx == 1 and lx == 1, why
+            for it in range(1, ITERS + 1):
+                tr.shard_iteration(comm, it, 1, 0.02, 0.005, N, M, K, 0.05, 0.02, True)
+            tr.shard_iteration(comm, ITERS + 1, 2, 1e-3, 0.005, N, M, 0, 0.0, 0.0, False)
+            zz, pp = tr.download_model()
+    finally:
+        comm.close()
+    assert np.array_equal(pp, p1) and np.array_equal(zz, z1)
+
+
+def test_native_iteration_plan_refusals(cuda_device):
+    """The plan names the exchange per phase and refuses ranks that cannot split the work evenly."""
+    from neural_block_textures_b200 import Trainer
+    spec = _spec()
+    z, p = spec.init_params()
+    with Trainer() as tr:
+        ok, why = tr.init(spec.model_desc(), z, p, _target(spec))
+        assert ok, why
+        ok, mx, lx, _ = tr.shard_iteration_plan(2, 1, 1, N, M, K, True)
+        assert ok and (mx, lx) == (1, 1)
+        ok, mx, _, _ = tr.shard_iteration_plan(2, 0, 1, 96, M, K, True)      # 48 pairs per rank: fitness-only exchange
+        assert ok and mx == 2
+        ok, _, _, why = tr.shard_iteration_plan(3, 0, 1, N, M, K, True)      # 512 pairs over 3 ranks
+        assert not ok and "split evenly" in why
+        ok, _, _, why = tr.shard_iteration_plan(2, 0, 1, N, 10 * M, K, True)  # minibatch above the init size
+        assert not ok and "minibatch" in why
+
+
+@pytest.mark.parametrize("driver", ["python", "native"])
+def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device, driver):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path), driver)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=300)
+        assert pr.exitcode == 0
+    z, p, z1, p1 = _one_gpu_reference()
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"p{r}.npy"), p1), f"rank {r} weights"
         assert np.array_equal(np.load(tmp_path / f"z{r}.npy"), z1), f"rank {r} latent"
