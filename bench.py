@@ -462,7 +462,10 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    # Inside the timed region only the population kernel carries CUDA events (the roofline's launch time): events
+    # around every launch cost host calls that, on several GPUs, can outlast the device work of a step.
     tr.kernel_timing(True)
+    tr.kernel_timing_only("mlp_eval")
     launches0 = tr.launch_count()
     evs = []
     with ClockSampler(local) as clk:
@@ -481,20 +484,29 @@ def main():
     launches = tr.launch_count() - launches0
     ms = sum(a.elapsed_time(b) for a, b in evs)
     eval_ms, eval_n = tr.kernel_time("mlp_eval")
-    lat_ms, lat_n = tr.kernel_time("lat_eval")
-    qat_ms, qat_n = tr.kernel_time("qat")
-    # every other kernel class the library times (device time of this library's kernels; the rest of a step
-    # is collectives and idle gaps)
-    other = {}
-    for cls in ("batch", "noise", "mlp_finish", "mlp_grad", "lat_noise", "lat_gather", "dct_rate", "adam", "snap"):
-        ms_c, n_c = tr.kernel_time(cls)
-        if n_c:
-            other[cls] = ms_c / args.steps
     tr.kernel_timing(False)
     if dist:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+
+    # ---- per-phase breakdown: a separate pass with every kernel class timed (device time of this library's
+    # kernels and, under the native sharded driver, of the NCCL all-gathers; the rest of a step is idle gaps)
+    nb = min(args.steps, 100)
+    tr.kernel_timing_only(None)
+    tr.kernel_timing(True)
+    for _ in range(nb):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        step(it); it += 1
+    stream.synchronize()
+    breakdown = {}
+    for cls in ("mlp_eval", "lat_eval", "qat", "batch", "noise", "mlp_finish", "mlp_grad", "lat_noise", "lat_gather", "dct_rate",
+                "adam", "snap", "exchange"):
+        ms_c, n_c = tr.kernel_time(cls)
+        if n_c:
+            breakdown[cls] = ms_c / nb
+    tr.kernel_timing(False)
     value = decodes * args.steps / (ms * 1e-3)
 
     # ---- FD-phase iterations (mlp_step_fd + lat_step + qat_search), same timing rules
@@ -576,8 +588,8 @@ def main():
                        "pop_kernel": kernel,
                        "l2": "flushed between steps (256 MiB memset outside the timed events)"},
             "roofline": pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks),
-            "phase_ms_per_step": {"mlp_eval": eval_ms / args.steps, "lat_eval": lat_ms / args.steps, "qat": qat_ms / args.steps,
-                                  **other, "kernels_total": (eval_ms + lat_ms + qat_ms) / args.steps + sum(other.values())},
+            "phase_ms_per_step": {**breakdown, "kernels_total": sum(v for k, v in breakdown.items() if k != "exchange"),
+                                  "note": f"separate pass of {nb} steps with every kernel class timed (events around each launch)"},
             "e2e": {"value": e2e_value, "unit": "decodes/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
             "gpu_launches": launches,

@@ -135,6 +135,9 @@ void ntcb_set_stream(ntcb_trainer* t, void* stream);
  * count of one kernel class since the last read ("mlp_eval", "lat_eval", "lat_gather", "qat", "mlp_grad", "decode",
  * "noise", "batch", "fd_eval"). Reading synchronises the stream. */
 void ntcb_kernel_timing(ntcb_trainer* t, int enable);
+/* While timing is enabled, time only kernel class `kernel` (NULL or "": every class). Every timed launch costs two
+ * event records and the host calls that create them; timing one class keeps a measured loop close to untimed. */
+void ntcb_kernel_timing_only(ntcb_trainer* t, const char* kernel);
 void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int* launches);
 /* Fills n draws of the counter-based noise on the current CUDA device (no trainer needed): gauss_host[i] and
  * u32_host[i] for index index0 + i of (seed, stream, step, pair); either pointer may be NULL. For tests. */
@@ -325,6 +328,17 @@ int ntcb_shard_iteration_plan(const ntcb_trainer* t, int world, int rank, int ml
  * trainer's. Asynchronous on the trainer's stream like the single-GPU steps. */
 void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, float mlp_sigma, float mlp_lr, int N, int M, int K,
                           float lat_sigma, float lat_lr, int qat);
+/* Peer-memory exchanges for ntcb_shard_iteration (addition): instead of NCCL, each exchange is one kernel that writes
+ * this rank's block into every peer's staging buffer over NVLink, signals each peer with a system-scope flag, waits
+ * (bounded, a few seconds) for every peer's signal and copies the staged blocks into place. Set-up: every rank calls
+ * ntcb_p2p_export for the (world, N, K, qat) it will iterate with, which allocates its exchange buffer and writes the
+ * buffer's CUDA IPC handle (NTCB_P2P_HANDLE_BYTES bytes); the caller gathers the handles of all ranks in rank order
+ * (any host channel) and every rank calls ntcb_p2p_import. Both return 0 with a reason on failure (then the
+ * iteration keeps using NCCL). A wait that runs out makes the next synchronising call print and exit. The ranks
+ * must all have finished their last iteration (a barrier) before any of them destroys its trainer. */
+#define NTCB_P2P_HANDLE_BYTES 64
+int ntcb_p2p_export(ntcb_trainer* t, int world, int rank, int N, int K, int qat, unsigned char* handle, char* why, size_t why_cap);
+int ntcb_p2p_import(ntcb_trainer* t, const unsigned char* handles, int world, int rank, char* why, size_t why_cap);
 
 #ifdef __cplusplus
 }

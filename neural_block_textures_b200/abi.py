@@ -137,6 +137,7 @@ SIGNATURES = {
     "ntcb_set_stream": (None, [_vp, _vp]),
     "ntcb_kernel_timing": (None, [_vp, C.c_int]),
     "ntcb_kernel_time": (None, [_vp, C.c_char_p, _dp, _ip]),
+    "ntcb_kernel_timing_only": (None, [_vp, C.c_char_p]),
     "ntcb_launch_count": (C.c_longlong, [_vp]),
     "ntcb_set_pop_kernel": (None, [_vp, C.c_int]),
     "ntcb_dct_probe": (C.c_size_t, [_vp, C.POINTER(C.c_uint8), _fp, C.c_size_t]),
@@ -179,9 +180,12 @@ SIGNATURES = {
                                             C.c_size_t]),
     "ntcb_shard_iteration": (None, [_vp, _vp, C.c_int, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float,
                                     C.c_int]),
+    "ntcb_p2p_export": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_ubyte), C.c_char_p, C.c_size_t]),
+    "ntcb_p2p_import": (C.c_int, [_vp, C.POINTER(C.c_ubyte), C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
 }
 
 COMM_ID_BYTES = 128   # NTCB_COMM_ID_BYTES
+P2P_HANDLE_BYTES = 64   # NTCB_P2P_HANDLE_BYTES
 
 _lib = None
 

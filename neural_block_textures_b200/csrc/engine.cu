@@ -20,6 +20,7 @@
 #include "kernels.h"
 #include "kernels_snap.h"
 #include "nccl_link.h"
+#include "p2p_exchange.h"
 
 // The C description structs are the C++ ones byte for byte (main.cpp fills the C++ ones; FFI callers the C ones).
 static_assert(sizeof(ntcb_level_desc) == sizeof(ntc_cuda::LevelDesc), "LevelDesc layout");
@@ -81,6 +82,11 @@ struct Trainer::Impl {
     int* tc_err = nullptr;   // device flag the tensor-core kernel sets when an MMA completion wait times out
     float* gpart = nullptr; long long gpart_cap = 0;
     char* xbuf = nullptr; long long xbuf_cap = 0;   // exchange blocks of the native sharded iteration ([rank][block])
+    // peer-memory exchange of the native sharded iteration (ntcb_p2p_export / ntcb_p2p_import)
+    ntcb::P2PArgs p2p{};
+    char* p2p_buf = nullptr;   // this rank's exchange buffer (flags, counters, staging)
+    bool p2p_ready = false;
+    uint32_t p2p_epoch = 0;
     float* qat_grid = nullptr; int* qat_bits = nullptr;
     // progress-print statistics: the last set_qes description (host copy) and a device scratch buffer
     ntc_cuda::QesDesc qes_host{};
@@ -88,9 +94,13 @@ struct Trainer::Impl {
     // counters
     int mlp_t = 0, lat_t = 0, lat_step_no = 0;
     int last_N = 0, last_M = 0, last_pairs = 0; bool last_fd = false;
+    // pairs whose dl / lsum (read only by mlp_stats and debug_last_dl) are still to be reduced from fit: the sharded
+    // ES step defers that launch until one of them asks
+    mutable int dl_pending = 0;
     long long launches = 0;
     // timing
     bool timing = false;
+    std::string timing_only;   // non-empty: only this kernel class is timed (the others launch without events)
     struct Pending { std::string cls; cudaEvent_t a, b; };
     std::vector<Pending> pending;
     std::map<std::string, std::pair<double, int>> totals;
@@ -118,7 +128,7 @@ void dfree(T*& p) { if (p) { cudaFree(p); p = nullptr; } }
 // Records CUDA events around one launch of kernel class `cls` when timing is on.
 template <class F>
 void timed(Impl& I, const char* cls, int nlaunch, F&& launch) {
-    if (!I.timing) { launch(); I.launches += nlaunch; return; }
+    if (!I.timing || (!I.timing_only.empty() && I.timing_only != cls)) { launch(); I.launches += nlaunch; return; }
     Impl::Pending p{cls, nullptr, nullptr};
     NTCB_CHECK(cudaEventCreate(&p.a)); NTCB_CHECK(cudaEventCreate(&p.b));
     NTCB_CHECK(cudaEventRecord(p.a, I.stream));
@@ -147,7 +157,8 @@ void check_tc_err(const Impl& I) {
     int e = 0;
     NTCB_CHECK(cudaMemcpy(&e, I.tc_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
-        fprintf(stderr, "ntc_b200: a tensor-core population CTA timed out waiting for its MMAs\n");
+        fprintf(stderr, e == 2 ? "ntc_b200: a peer exchange timed out waiting for another rank\n"
+                               : "ntc_b200: a tensor-core population CTA timed out waiting for its MMAs\n");
         exit(1);
     }
 }
@@ -262,6 +273,11 @@ void free_all(Impl& I) {
     dfree(I.bidx); dfree(I.feat_t); dfree(I.tgt_t); dfree(I.mlp_eps); dfree(I.part);
     dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart); dfree(I.xbuf); I.xbuf_cap = 0; dfree(I.tc_err);
     dfree(I.qat_grid); dfree(I.qat_bits); dfree(I.stats_buf); I.stats_cap = 0;
+    if (I.p2p_ready)
+        for (int q = 0; q < I.p2p.world; q++)
+            if (q != I.p2p.rank && I.p2p.base[q]) cudaIpcCloseMemHandle(I.p2p.base[q]);
+    I.p2p = ntcb::P2PArgs{}; I.p2p_ready = false;
+    dfree(I.p2p_buf);
     for (auto& p : I.pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
     I.pending.clear();
     if (I.own_stream) { cudaStreamDestroy(I.own_stream); I.own_stream = nullptr; }
@@ -507,7 +523,14 @@ void es_apply(Impl& I, int it, float sigma, float lr, int N, const double* fit_a
         float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
         ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
     });
-    I.last_N = N; I.last_fd = false; I.last_pairs = N;
+    I.last_N = N; I.last_fd = false; I.last_pairs = N; I.dl_pending = 0;
+}
+
+// The deferred dl / lsum reduction of a sharded ES step (k_es_reduce over the gathered fitness in fit).
+void ensure_dl(const Impl& I) {
+    if (I.dl_pending <= 0) return;
+    ntcb::launch_es_reduce(I.stream, I.fit, I.dl_pending, I.dl, I.lsum);
+    I.dl_pending = 0;
 }
 
 void mlp_step_impl(Impl& I, int it, float sigma, float lr, int N, int M) {
@@ -548,7 +571,7 @@ void fd_apply(Impl& I, float h, float lr, const double* fit = nullptr) {
         float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
         ntcb::launch_fd_grad_adam(I.stream, I.dl, I.hh, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
     });
-    I.last_N = I.P; I.last_fd = true; I.last_pairs = 0;
+    I.last_N = I.P; I.last_fd = true; I.last_pairs = 0; I.dl_pending = 0;
 }
 
 void mlp_step_fd_impl(Impl& I, int it, float h, float lr, int M) {
@@ -565,6 +588,7 @@ void mlp_stats_impl(Impl& I, double& batch_loss, double& diff_std) {
     require_ready(I); set_device(I);
     if (I.last_N == 0) { batch_loss = 0; diff_std = 0; return; }
     if (!I.last_fd) {
+        ensure_dl(I);
         std::vector<double> dl(I.last_N), ls(I.last_N);
         NTCB_CHECK(cudaMemcpyAsync(dl.data(), I.dl, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
         NTCB_CHECK(cudaMemcpyAsync(ls.data(), I.lsum, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
@@ -820,9 +844,8 @@ void shard_mlp_eval_grad_impl(Impl& I, int it, float sigma, int N, int M, int p0
     double* fit = static_cast<double*>(block);
     float* part = reinterpret_cast<float*>(static_cast<char*>(block) + 16LL * n);
     draw_batch(I, it, M);
-    es_eval_pairs(I, it, sigma, M, p0, p1, fit);
-    // this rank's pairs' loss differences and their gradient segments (the noise of these pairs is in mlp_eps)
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, fit, n, I.dl, I.lsum); });
+    // this rank's pairs' fitness, loss differences (in the same launch) and gradient segments (their noise is in mlp_eps)
+    es_eval_pairs(I, it, sigma, M, p0, p1, fit, true);
     const float scale = 1.0f / (2.0f * (float)N * sigma);
     timed(I, "mlp_grad", 1, [&] { ntcb::launch_es_grad_partial(I.stream, I.dl, I.mlp_eps, n, I.P, scale, seglen, part); });
 }
@@ -839,13 +862,13 @@ void shard_mlp_apply_grad_impl(Impl& I, float lr, int N, const void* blocks, int
     // [rank][fitness | partials] -> fitness of all N pairs in pair order, partials of all segments in order
     NTCB_CHECK(cudaMemcpy2DAsync(I.fit, fit_bytes, src, (size_t)bytes, fit_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
     NTCB_CHECK(cudaMemcpy2DAsync(I.gpart, part_bytes, src + fit_bytes, (size_t)bytes, part_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_es_reduce(I.stream, I.fit, N, I.dl, I.lsum); });
     timed(I, "mlp_grad", 1, [&] {
         I.mlp_t++;
         float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
         ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
     });
     I.last_N = N; I.last_fd = false; I.last_pairs = N;
+    I.dl_pending = N;   // dl / lsum of all N pairs from I.fit when mlp_stats / debug_last_dl ask
 }
 
 // Texel-row latent step of one rank (plan from lat_rows_plan): pixel rows [pa, pb) of all K pairs, gathers and
@@ -934,6 +957,7 @@ size_t ntcb_debug_last_batch(const ntcb_trainer* t, int* out, size_t cap) {
 size_t ntcb_debug_last_dl(const ntcb_trainer* t, double* out, size_t cap) {
     const Impl& I = t->impl;
     if (!I.ready) return 0;
+    if (!I.last_fd) ensure_dl(I);
     return copy_out(I, I.dl, (size_t)I.last_N, out, cap);
 }
 size_t ntcb_debug_last_zgrad(const ntcb_trainer* t, float* out, size_t cap) {
@@ -958,6 +982,11 @@ void ntcb_kernel_timing(ntcb_trainer* t, int enable) {
     Impl& I = t->impl;
     flush_timing(I);
     I.timing = enable != 0;
+}
+void ntcb_kernel_timing_only(ntcb_trainer* t, const char* kernel) {
+    Impl& I = t->impl;
+    flush_timing(I);
+    I.timing_only = kernel ? kernel : "";
 }
 void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int* launches) {
     Impl& I = t->impl;
@@ -1348,6 +1377,77 @@ int ntcb_shard_iteration_plan(const ntcb_trainer* t, int world, int rank, int ml
     return ok;
 }
 
+// Largest block one rank contributes to any exchange of ntcb_shard_iteration for (world, N, K) and both MLP modes.
+static size_t max_exchange_block(const Impl& I, int world, int rank, int N, int K, int qat, int mx, int lx) {
+    size_t cap = 0;
+    const int n = N / world;
+    cap = std::max(cap, mx == 1 ? (size_t)es_block_bytes(I, N, rank * n, (rank + 1) * n) : 16 * (size_t)n);
+    cap = std::max(cap, 2 * (size_t)((I.P + world - 1) / world) * sizeof(double));
+    if (lx == 1) {
+        int lvl, ta, tb, pa, pb;
+        lat_rows_plan(I, world, rank, lvl, ta, tb, pa, pb);
+        cap = std::max(cap, (size_t)(tb - ta) * I.d.lv[lvl].W * I.d.lv[lvl].C * sizeof(float));
+    } else if (lx == 2) {
+        cap = std::max(cap, (size_t)K * (I.d.H / world) * I.d.W * sizeof(float));
+    }
+    if (qat) cap = std::max(cap, (size_t)(I.d.lv[0].H / world) * I.d.lv[0].W * I.d.lv[0].C * sizeof(float));
+    return (cap + 255) / 256 * 256;
+}
+
+int ntcb_p2p_export(ntcb_trainer* t, int world, int rank, int N, int K, int qat, unsigned char* handle, char* why, size_t why_cap) {
+    Impl& I = t->impl;
+    std::string r;
+    int mx = 0, lx = 0;
+    if (!I.ready) { set_why(why, why_cap, "trainer not initialised"); return 0; }
+    set_device(I);
+    if (world < 1 || world > ntcb::kP2PMaxRanks) { set_why(why, why_cap, "peer exchange supports 1-8 ranks"); return 0; }
+    if (!iteration_plan(I, world, rank, 1, N, 1, K, qat, mx, lx, r)) { set_why(why, why_cap, r); return 0; }
+    if (I.p2p_buf) { set_why(why, why_cap, "peer exchange already set up for this trainer"); return 0; }
+    const size_t cap = max_exchange_block(I, world, rank, N, K, qat, mx, lx);
+    const size_t total = ntcb::kP2PHeader + 2 * (size_t)world * cap;
+    I.p2p_buf = dalloc<char>(total);
+    NTCB_CHECK(cudaMemset(I.p2p_buf, 0, total));
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, I.p2p_buf) != cudaSuccess) {
+        cudaGetLastError();
+        dfree(I.p2p_buf);
+        set_why(why, why_cap, "cudaIpcGetMemHandle failed");
+        return 0;
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    I.p2p = ntcb::P2PArgs{};
+    I.p2p.world = world; I.p2p.rank = rank; I.p2p.cap = cap;
+    I.p2p.base[rank] = I.p2p_buf;
+    return 1;
+}
+
+int ntcb_p2p_import(ntcb_trainer* t, const unsigned char* handles, int world, int rank, char* why, size_t why_cap) {
+    Impl& I = t->impl;
+    if (!I.p2p_buf || I.p2p.world != world || I.p2p.rank != rank || I.p2p_ready) {
+        set_why(why, why_cap, "ntcb_p2p_export with the same world size and rank must come first, once");
+        return 0;
+    }
+    set_device(I);
+    for (int q = 0; q < world; q++) {
+        if (q == rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + 64 * (size_t)q, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            for (int j = 0; j < q; j++) if (j != rank && I.p2p.base[j]) { cudaIpcCloseMemHandle(I.p2p.base[j]); I.p2p.base[j] = nullptr; }
+            set_why(why, why_cap, std::string("cudaIpcOpenMemHandle failed for rank ") + std::to_string(q) + ": " + cudaGetErrorString(e));
+            return 0;
+        }
+        I.p2p.base[q] = static_cast<char*>(p);
+    }
+    I.p2p_ready = true;
+    I.p2p_epoch = 0;
+    return 1;
+}
+
 void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, float mlp_sigma, float mlp_lr, int N, int M, int K,
                           float lat_sigma, float lat_lr, int qat) {
     Impl& I = t->impl;
@@ -1357,8 +1457,15 @@ void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, f
     int mx = 0, lx = 0;
     std::string why;
     if (!iteration_plan(I, G, r, mlp_mode, N, M, K, qat, mx, lx, why)) die(("shard_iteration: " + why).c_str());
+    const bool p2p = I.p2p_ready && I.p2p.world == G && I.p2p.rank == r;
     auto gather = [&](void* buf, size_t bytes) {
-        timed(I, "exchange", 0, [&] { ntcb::nccl::all_gather_inplace(c->nc, buf, bytes, r, I.stream); });
+        if (p2p) {
+            if (bytes > I.p2p.cap) die("shard_iteration: an exchange block is larger than the peer buffers set up for it");
+            I.p2p_epoch++;
+            timed(I, "exchange", 1, [&] { ntcb::launch_p2p_allgather(I.stream, I.p2p, buf, bytes, I.p2p_epoch, I.tc_err); });
+        } else {
+            timed(I, "exchange", 0, [&] { ntcb::nccl::all_gather_inplace(c->nc, buf, bytes, r, I.stream); });
+        }
     };
     // MLP step (mlp_step / mlp_step_fd)
     if (mlp_mode == 1) {
@@ -1450,6 +1557,7 @@ void Trainer::debug_last_batch(std::vector<int>& bidx) const {
 }
 void Trainer::debug_last_dl(std::vector<double>& dl) const {
     dl.resize(im->last_N);
+    if (im->ready && !im->last_fd) ensure_dl(*im);
     if (im->ready) copy_out(*im, im->dl, dl.size(), dl.data(), dl.size());
 }
 void Trainer::debug_last_zgrad(std::vector<float>& g) const {

@@ -71,7 +71,10 @@ struct TcShape {
     static constexpr int ob2 = oW2 + S::NOUT * S::H2;         // b2 [NOUTP]
     static_assert(S::H2 % 4 == 0, "output-layer rows are read as float4");
     static constexpr int oB3h = round_up(ob2 + NOUTP, 4), oB3l = oB3h + N3 * K3;   // W2 as an MMA B operand
-    static constexpr int SIGN = round_up(oB3l + N3 * K3, 32);
+    // b1 as an extra K step of layer 2: B block [N2][8] K-major with b1 in k = 0 (hi / lo), against a constant
+    // A block (column 0 = 1, columns 1-7 = 0) that every stream of the CTA shares
+    static constexpr int oBbh = oB3l + N3 * K3, oBbl = oBbh + N2 * 8;
+    static constexpr int SIGN = round_up(oBbl + N2 * 8, 32);
     // TMEM columns: D (layers 1 and 2), D3 (output layer), X hi / lo, H hi / lo
     // The output layer runs on the tensor core for wide outputs (12: measured 1.33 vs 1.52 ms at config 3)
     // and on the FP32 pipe for 3 outputs (0.86 vs 1.03 ms at config 2), where 16-wide MMAs are mostly padding.
@@ -84,6 +87,10 @@ struct TcShape {
     static constexpr int STREAMS = kTmemCols / COLS >= 5 ? 5 : 4;
     static constexpr int TPB = kTcRows * STREAMS;
     static_assert(STREAMS * COLS <= kTmemCols, "TMEM columns");
+    // Layer-2 bias on the tensor core when the streams leave 8 TMEM columns for the constant block (every 3-output
+    // shape); otherwise (12 outputs: all 512 columns in use) it is added in the epilogue.
+    static constexpr bool B1TC = !L3TC && STREAMS * COLS + 8 <= kTmemCols;
+    static constexpr int cOne = STREAMS * COLS;   // the constant block's first column (from the CTA's TMEM base)
 
     // Writes flat reference weight k (value w) to every place a kernel variant reads it from: MMA B operands
     // as hi / lo, biases and the row-major output layer as plain floats.
@@ -95,7 +102,7 @@ struct TcShape {
         k -= S::H1;
         if (k < S::H2 * S::H1) { const int j = k / S::H1, i = k - j * S::H1; sw[oB2h + kmajor(j, i, K2)] = hi; sw[oB2l + kmajor(j, i, K2)] = lo; return; }
         k -= S::H2 * S::H1;
-        if (k < S::H2) { sw[ob1 + k] = w; return; }
+        if (k < S::H2) { sw[ob1 + k] = w; sw[oBbh + kmajor(k, 0, 8)] = hi; sw[oBbl + kmajor(k, 0, 8)] = lo; return; }
         k -= S::H2;
         if (k < S::NOUT * S::H2) {
             const int o = k / S::H2, j = k - o * S::H2;
@@ -158,9 +165,15 @@ __device__ __forceinline__ float out_layer_error(const DevModel& m, const float*
     for (int c = 0; c < S::NOUT; c++) acc[c] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int j = 0; j < S::H2; j += 4) {
-        const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
-        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak);
-        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
+        float2 h0, h1;
+        if constexpr (T::B1TC) {   // b1 already in the accumulator
+            h0 = leaky_pair(make_float2(h[j], h[j + 1]), leak);
+            h1 = leaky_pair(make_float2(h[j + 2], h[j + 3]), leak);
+        } else {
+            const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
+            h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak);
+            h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
+        }
 #pragma unroll
         for (int c = 0; c < S::NOUT; c++) {
             const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + c * S::H2 + j);
@@ -191,6 +204,49 @@ __device__ __forceinline__ void issue3(uint32_t d, uint32_t a_hi, uint32_t a_lo,
     }
     if (elect_one()) tc::commit(bar);
     __syncwarp();
+}
+
+// Layer 2 of a shape with B1TC: the 3xTF32 product over K, then D += 1 * b1_lo + 1 * b1_hi from the constant A
+// block `one` (its lo part is zero), then commit.
+template <int K, int N>
+__device__ __forceinline__ void issue3_bias(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo, uint32_t one,
+                                            uint32_t bb_hi, uint32_t bb_lo, uint64_t* bar) {
+    constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
+    constexpr uint32_t sbo = (uint32_t)K * 32u;
+    tc::fence_after_sync();
+#pragma unroll
+    for (int s = 0; s < K / 8; s++) {
+        if (elect_one()) tc::mma_tf32_ts(d, a_lo + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, s > 0 ? 1u : 0u);
+        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_lo + 256 * s, 128, sbo), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, 1u);
+    }
+    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc(bb_lo, 128, 256), id, 1u);
+    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc(bb_hi, 128, 256), id, 1u);
+    if (elect_one()) tc::commit(bar);
+    __syncwarp();
+}
+
+// Layer 2 of unit (A = H hi / lo of the stream, B = the sign's W1 and b1 blocks).
+template <class T>
+__device__ __forceinline__ void issue_layer2(uint32_t tbase, uint32_t tb, uint32_t sb, uint64_t* bar) {
+    if constexpr (T::B1TC)
+        issue3_bias<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, tbase + T::cOne,
+                                  sb + T::oBbh * 4, sb + T::oBbl * 4, bar);
+    else
+        issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+}
+
+// The constant A block of the layer-2 bias step: TMEM column cOne = 1, cOne + 1 .. + 7 = 0 on all 128 lanes,
+// written by the 128 threads of stream 0 (thread t of warp w reaches lane 32 w + t).
+template <class T>
+__device__ __forceinline__ void init_one_block(uint32_t tbase, int g, int warp) {
+    if constexpr (T::B1TC) {
+        if (g == 0) {
+            const float v[8] = {1.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            tc::st_x8(tbase + T::cOne + ((uint32_t)(warp * 32) << 16), v);
+            tc::wait_st();
+        }
+    }
 }
 
 // Named barrier over the 128 threads of one stream (ids 1..STREAMS; 0 is __syncthreads), AND-reducing v.
@@ -243,6 +299,10 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
     if (threadIdx.x < 32) tc::tmem_alloc(&tbase, kTmemCols);
     if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init(bar3, 1); tc::mbar_init_fence(); }
     for (int i = threadIdx.x; i < NS * 2 * T::SIGN; i += T::TPB) dyn[i] = 0.0f;   // padding stays zero
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    init_one_block<T>(tbase, g, warp);
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -342,7 +402,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 tc::fence_before_sync();
                 ok = stream_sync_and(bar_id, ok);
                 if (!ok) break;
-                if (warp == issuer) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+                if (warp == issuer) issue_layer2<T>(tbase, tb, sb, bar);
                 // layer 2 result -> registers
                 wait_mma();
 #pragma unroll
@@ -477,6 +537,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
     __syncthreads();
     for (int k = threadIdx.x; k < m.P; k += T::TPB) T::store(sw, k, wg[k]);
     tc::fence_proxy_async_smem();
+    init_one_block<T>(tbase, g, warp);
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -535,7 +596,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
-        if (ok && warp == issuer) issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+        if (ok && warp == issuer) issue_layer2<T>(tbase, tb, sb, bar);
     };
 
     if (i0 < i1) {

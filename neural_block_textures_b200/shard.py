@@ -159,7 +159,9 @@ class NativeShardedES:
     stream into the trainer's own buffers, on a communicator of its own. torch.distributed only carries the
     128-byte NCCL id from rank 0 to the others (any backend)."""
 
-    def __init__(self, trainer, dist, device=None):
+    def __init__(self, trainer, dist, device=None, p2p: tuple[int, int, bool] | None = None):
+        """p2p = (N, K, qat): also set up the peer-memory exchanges (ntcb_p2p_export / import) for iterations with N
+        ES pairs, K latent pairs and the selector search on or off; without it every exchange goes through NCCL."""
         import torch
         from .trainer import Comm
         self.t, self.dist = trainer, dist
@@ -169,6 +171,14 @@ class NativeShardedES:
             uid.copy_(torch.frombuffer(bytearray(Comm.unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         self.comm = Comm(bytes(uid.cpu().numpy().tobytes()), self.world, self.rank)
+        self.p2p = False
+        if p2p is not None and self.world > 1:
+            N, K, qat = p2p
+            mine = trainer.p2p_export(self.world, self.rank, N, K, qat)
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine)
+            trainer.p2p_import(b"".join(allh), self.world, self.rank)
+            self.p2p = True
 
     def plan(self, mlp_mode: int, N: int, M: int, K: int, qat: bool):
         return self.t.shard_iteration_plan(self.world, self.rank, mlp_mode, N, M, K, qat)

@@ -170,6 +170,10 @@ class Trainer:
     def kernel_timing(self, enable: bool) -> None:
         self.lib.ntcb_kernel_timing(self.h, 1 if enable else 0)
 
+    def kernel_timing_only(self, kernel: str | None) -> None:
+        """Time only this kernel class while timing is on (None: every class)."""
+        self.lib.ntcb_kernel_timing_only(self.h, kernel.encode() if kernel else None)
+
     def kernel_time(self, kernel: str) -> tuple[float, int]:
         ms, n = C.c_double(), C.c_int()
         self.lib.ntcb_kernel_time(self.h, kernel.encode(), C.byref(ms), C.byref(n))
@@ -273,6 +277,24 @@ class Trainer:
     def shard_iteration(self, comm: "Comm", it: int, mlp_mode: int, mlp_sigma: float, mlp_lr: float, N: int, M: int, K: int,
                         lat_sigma: float, lat_lr: float, qat: bool) -> None:
         self.lib.ntcb_shard_iteration(self.h, comm.h, it, mlp_mode, mlp_sigma, mlp_lr, N, M, K, lat_sigma, lat_lr, int(qat))
+
+
+    def p2p_export(self, world: int, rank: int, N: int, K: int, qat: bool) -> bytes:
+        """Allocates this rank's peer-exchange buffer and returns its IPC handle (ntcb_p2p_export)."""
+        h = (C.c_ubyte * abi.P2P_HANDLE_BYTES)()
+        why = C.create_string_buffer(256)
+        if not self.lib.ntcb_p2p_export(self.h, world, rank, N, K, int(qat), h, why, 256):
+            raise RuntimeError("ntcb_p2p_export: " + why.value.decode())
+        return bytes(h)
+
+    def p2p_import(self, handles: bytes, world: int, rank: int) -> None:
+        """Maps every peer's exchange buffer (handles of all ranks in rank order, ntcb_p2p_import)."""
+        if len(handles) != world * abi.P2P_HANDLE_BYTES:
+            raise ValueError("need one handle per rank")
+        buf = (C.c_ubyte * len(handles)).from_buffer_copy(handles)
+        why = C.create_string_buffer(256)
+        if not self.lib.ntcb_p2p_import(self.h, buf, world, rank, why, 256):
+            raise RuntimeError("ntcb_p2p_import: " + why.value.decode())
 
 
 class Comm:
