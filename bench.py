@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--shard-driver", default="native", choices=["native", "python"],
                     help="N > 1: one library call per iteration with in-place NCCL all-gathers on the library's own communicator "
                          "(native), or the per-phase entry points around torch.distributed all-gathers (python)")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="native driver: the library's peer-memory exchange kernel over CUDA IPC (p2p) or NCCL all-gathers")
     ap.add_argument("--pop-kernel", default="tensor", choices=["tensor", "ffma"],
                     help="ES population kernel: tcgen05 3xTF32 (default) or the bit-exact packed-FP32 one")
     return ap.parse_args()
@@ -411,7 +413,7 @@ def main():
     Kl = K if has_lat else 0
     if world > 1 and args.shard_driver == "native":
         from neural_block_textures_b200.shard import NativeShardedES
-        native = NativeShardedES(tr, dist, device="cuda")
+        native = NativeShardedES(tr, dist, device="cuda", p2p=(N, Kl, qat) if args.exchange == "p2p" else None)
         for mode in (1, 2):
             ok, _, _, why = native.plan(mode, N, M, Kl, qat)
             if not ok:
@@ -585,6 +587,8 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg.name, "cli": cfg.cli, "decodes_per_step": dec, "parallelism": f"population x{world}",
+                       "exchange": ("none" if world == 1 else "torch.distributed NCCL all-gathers" if sharded is not None else
+                                    "peer-memory exchange kernel (CUDA IPC, NVLink)" if native.p2p else "NCCL in-place all-gathers"),
                        "pop_kernel": kernel,
                        "l2": "flushed between steps (256 MiB memset outside the timed events)"},
             "roofline": pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks),
@@ -605,6 +609,8 @@ def main():
             tr.close()
             line["ref_cuda_backend"] = ref_cuda_leg(cfg)
         print(json.dumps(line))
+    if native is not None:
+        native.close()
     tr.close()
     if dist:
         dist.barrier()

@@ -339,6 +339,9 @@ void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, f
 #define NTCB_P2P_HANDLE_BYTES 64
 int ntcb_p2p_export(ntcb_trainer* t, int world, int rank, int N, int K, int qat, unsigned char* handle, char* why, size_t why_cap);
 int ntcb_p2p_import(ntcb_trainer* t, const unsigned char* handles, int world, int rank, char* why, size_t why_cap);
+/* Unmaps the peers' exchange buffers after this rank's stream has drained (the iteration falls back to NCCL). Call it
+ * on every rank, then a barrier, before any rank destroys its trainer: a buffer is freed only when no peer maps it. */
+void ntcb_p2p_release(ntcb_trainer* t);
 
 #ifdef __cplusplus
 }

@@ -182,6 +182,7 @@ SIGNATURES = {
                                     C.c_int]),
     "ntcb_p2p_export": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_ubyte), C.c_char_p, C.c_size_t]),
     "ntcb_p2p_import": (C.c_int, [_vp, C.POINTER(C.c_ubyte), C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
+    "ntcb_p2p_release": (None, [_vp]),
 }
 
 COMM_ID_BYTES = 128   # NTCB_COMM_ID_BYTES

@@ -1403,7 +1403,7 @@ int ntcb_p2p_export(ntcb_trainer* t, int world, int rank, int N, int K, int qat,
     if (world < 1 || world > ntcb::kP2PMaxRanks) { set_why(why, why_cap, "peer exchange supports 1-8 ranks"); return 0; }
     if (!iteration_plan(I, world, rank, 1, N, 1, K, qat, mx, lx, r)) { set_why(why, why_cap, r); return 0; }
     if (I.p2p_buf) { set_why(why, why_cap, "peer exchange already set up for this trainer"); return 0; }
-    const size_t cap = max_exchange_block(I, world, rank, N, K, qat, mx, lx);
+    const size_t cap = (ntcb::p2p_stage_bytes(max_exchange_block(I, world, rank, N, K, qat, mx, lx)) + 255) / 256 * 256;
     const size_t total = ntcb::kP2PHeader + 2 * (size_t)world * cap;
     I.p2p_buf = dalloc<char>(total);
     NTCB_CHECK(cudaMemset(I.p2p_buf, 0, total));
@@ -1448,6 +1448,16 @@ int ntcb_p2p_import(ntcb_trainer* t, const unsigned char* handles, int world, in
     return 1;
 }
 
+void ntcb_p2p_release(ntcb_trainer* t) {
+    Impl& I = t->impl;
+    if (!I.p2p_ready) return;
+    set_device(I);
+    NTCB_CHECK(cudaStreamSynchronize(I.stream));
+    for (int q = 0; q < I.p2p.world; q++)
+        if (q != I.p2p.rank && I.p2p.base[q]) { cudaIpcCloseMemHandle(I.p2p.base[q]); I.p2p.base[q] = nullptr; }
+    I.p2p_ready = false;
+}
+
 void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, float mlp_sigma, float mlp_lr, int N, int M, int K,
                           float lat_sigma, float lat_lr, int qat) {
     Impl& I = t->impl;
@@ -1460,7 +1470,8 @@ void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, f
     const bool p2p = I.p2p_ready && I.p2p.world == G && I.p2p.rank == r;
     auto gather = [&](void* buf, size_t bytes) {
         if (p2p) {
-            if (bytes > I.p2p.cap) die("shard_iteration: an exchange block is larger than the peer buffers set up for it");
+            if (bytes % 4 || ntcb::p2p_stage_bytes(bytes) > I.p2p.cap)
+                die("shard_iteration: an exchange block does not fit the peer buffers set up for it");
             I.p2p_epoch++;
             timed(I, "exchange", 1, [&] { ntcb::launch_p2p_allgather(I.stream, I.p2p, buf, bytes, I.p2p_epoch, I.tc_err); });
         } else {

@@ -151,7 +151,16 @@ __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, 
         for (int py = y0; py < y1; py++) {
             const int pr = py - row_base;
             const float* row = dpix + (pr / rpb) * block + k * plane + (long long)(pr % rpb) * m.W;
-            for (int px = x0; px < x1; px++) d += row[px];
+            int px = x0;
+            // up to 16 values of the row loaded together, then added in raster order (the same float chain)
+            for (; px < x1; px += 16) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] = px + j < x1 ? row[px + j] : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (px + j < x1) d += v[j];
+            }
         }
         dsum[tl * K + k] = d;
     }

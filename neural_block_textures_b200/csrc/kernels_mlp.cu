@@ -57,6 +57,7 @@ void launch_batch(cudaStream_t s, const DevModel& m, uint64_t seed, int it, int 
 // eps[i][k] = gauss(seed, MLP stream, it, pair_begin + i, k): every pair's perturbation, generated once
 // per step and read by both the population kernel and the gradient (the reference regenerates it in
 // each of its per-chunk CTAs and again per weight in the gradient).
+// One CTA row per pair (blockIdx.y), the block sized to P rounded up to a warp so few threads idle.
 __global__ void k_mlp_noise(uint64_t seed, int it, int pair_begin, int npairs, int P, float* __restrict__ eps) {
     const int i = blockIdx.y;
     const uint64_t key = stream_key(seed, kStreamMlp, (uint32_t)it, (uint32_t)(pair_begin + i));
@@ -80,8 +81,9 @@ void launch_noise_fill(cudaStream_t s, uint64_t seed, uint32_t stream, uint32_t 
 
 void launch_mlp_noise(cudaStream_t s, uint64_t seed, int it, int pair_begin, int npairs, int P, float* eps) {
     if (npairs <= 0) return;
-    dim3 grid(blocks_for(P, 256), (unsigned)npairs);
-    k_mlp_noise<<<grid, 256, 0, s>>>(seed, it, pair_begin, npairs, P, eps);
+    const int tpb = std::min(1024, (P + 31) / 32 * 32);
+    dim3 grid(blocks_for(P, tpb), (unsigned)npairs);
+    k_mlp_noise<<<grid, tpb, 0, s>>>(seed, it, pair_begin, npairs, P, eps);
     NTCB_CHECK(cudaGetLastError());
 }
 
@@ -293,13 +295,15 @@ __global__ void k_es_grad_partial(const double* __restrict__ dl, const float* __
     const int i0 = seg * seglen, i1 = min(N, i0 + seglen);
     float g = 0.0f;
     int i = i0;
-    // eight pairs' loads issued together, then their FMAs in pair order (the same chain as one at a time)
-    for (; i + 8 <= i1; i += 8) {
-        float e[8], w[8];
+    // 32 pairs' loads issued together (the kernel is bound by loads in flight, not by its FMAs), then their FMAs in
+    // pair order: the same chain as one pair at a time
+    constexpr int U = 32;
+    for (; i + U <= i1; i += U) {
+        float e[U];
 #pragma unroll
-        for (int j = 0; j < 8; j++) { e[j] = __ldg(eps + (long long)(i + j) * P + k); w[j] = (float)dl[i + j]; }
+        for (int j = 0; j < U; j++) e[j] = __ldg(eps + (long long)(i + j) * P + k);
 #pragma unroll
-        for (int j = 0; j < 8; j++) g = fmaf(w[j] * scale, e[j], g);
+        for (int j = 0; j < U; j++) g = fmaf((float)__ldg(dl + i + j) * scale, e[j], g);
     }
     for (; i < i1; i++) g = fmaf((float)dl[i] * scale, __ldg(eps + (long long)i * P + k), g);
     gpart[(long long)seg * P + k] = g;
@@ -326,12 +330,13 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
     if (k >= P) return;
     float g = gpart[k];
     int sg = 1;
-    for (; sg + 8 <= nseg; sg += 8) {   // eight segments' loads together, summed in segment order
-        float v[8];
+    constexpr int U = 32;
+    for (; sg + U <= nseg; sg += U) {   // 32 segments' loads together, summed in segment order
+        float v[U];
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = gpart[(long long)(sg + j) * P + k];
+        for (int j = 0; j < U; j++) v[j] = gpart[(long long)(sg + j) * P + k];
 #pragma unroll
-        for (int j = 0; j < 8; j++) g += v[j];
+        for (int j = 0; j < U; j++) g += v[j];
     }
     for (; sg < nseg; sg++) g += gpart[(long long)sg * P + k];
     grad[k] = g;
@@ -341,7 +346,7 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
 }
 void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2) {
-    k_es_grad_adam<<<blocks_for(P, 256), 256, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
+    k_es_grad_adam<<<blocks_for(P, 64), 64, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
     NTCB_CHECK(cudaGetLastError());
 }
 

@@ -190,4 +190,10 @@ class NativeShardedES:
         self.t.shard_iteration(self.comm, it, mlp_mode, mlp_sigma, mlp_lr, N, M, K, lat_sigma, lat_lr, qat)
 
     def close(self) -> None:
+        """Collective: every rank unmaps its peers' exchange buffers, then all wait, so no buffer is freed while a
+        peer still maps it; then the communicator goes."""
+        if self.p2p:
+            self.t.p2p_release()
+            self.dist.barrier()
+            self.p2p = False
         self.comm.close()

@@ -297,6 +297,11 @@ class Trainer:
             raise RuntimeError("ntcb_p2p_import: " + why.value.decode())
 
 
+    def p2p_release(self) -> None:
+        """Unmaps the peers' exchange buffers (ntcb_p2p_release); every rank, then a barrier, before destroying."""
+        self.lib.ntcb_p2p_release(self.h)
+
+
 class Comm:
     """The library's NCCL communicator (ntcb_comm_*): `uid` is the id rank 0 made with Comm.unique_id(), handed to
     every rank; create it with the rank's device current."""

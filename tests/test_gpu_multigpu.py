@@ -1,6 +1,7 @@
 """Population / weight (FD) / image / texel-row sharding over NCCL, through both drivers bench.py can use under
 torchrun: ShardedES (per-phase entry points around torch.distributed all-gathers) and NativeShardedES (one
-ntcb_shard_iteration call per iteration, in-place all-gathers on the library's own NCCL communicator). The ranks
+ntcb_shard_iteration call per iteration, in-place all-gathers on the library's own NCCL communicator, or its own
+peer-memory exchange kernel over CUDA IPC mappings of every rank's exchange buffer). The ranks
 must end with the same weights and latent as one GPU running the plain Trainer steps, bit for bit (every per-pair,
 per-pixel and per-texel value is computed by the same kernels whichever rank computes it, and the gradient sums
 keep their order). The two-rank cases need >= 2 GPUs and are skipped otherwise; the one-rank native case runs on
@@ -51,9 +52,10 @@ def _rank_main(rank, world, port, out_dir, driver="python"):
         stream = torch.cuda.Stream()
         tr.set_stream(stream.cuda_stream)
         L0 = spec.levels[0]
-        if driver == "native":
+        if driver in ("native", "native_p2p"):
             from neural_block_textures_b200.shard import NativeShardedES
-            nat = NativeShardedES(tr, dist, device="cuda")
+            nat = NativeShardedES(tr, dist, device="cuda", p2p=(N, K, True) if driver == "native_p2p" else None)
+            assert nat.p2p == (driver == "native_p2p")
             ok, mx, lx, why = nat.plan(1, N, M, K, True)
             assert ok and mx == 1 and lx == 1, why
             for it in range(1, ITERS + 1):
@@ -137,7 +139,7 @@ def test_native_iteration_plan_refusals(cuda_device):
         assert not ok and "minibatch" in why
 
 
-@pytest.mark.parametrize("driver", ["python", "native"])
+@pytest.mark.parametrize("driver", ["python", "native", "native_p2p"])
 def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device, driver):
     import torch
     import torch.multiprocessing as mp
