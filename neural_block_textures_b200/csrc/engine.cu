@@ -483,12 +483,20 @@ void draw_batch(Impl& I, int it, int M) {
     I.last_M = M;
 }
 
-// Evaluates the ES pairs [p0, p1) of step `it` on the current minibatch; writes (lp, lm) per pair to fit, and
-// with `reduce` (the whole population on this trainer) dl and lsum as well.
-void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* fit, bool reduce = false) {
+// Evaluates the ES pairs [p0, p1) of step `it` on the current minibatch (with `draw`, the minibatch of step `it`
+// is drawn first, in the noise kernel's launch); writes (lp, lm) per pair to fit, and with `reduce` (the whole
+// population on this trainer) dl and lsum as well.
+void es_eval_pairs(Impl& I, int it, float sigma, int M, int p0, int p1, double* fit, bool reduce = false, bool draw = false) {
     const int n = p1 - p0;
+    if (draw) {
+        timed(I, "batch", 1, [&] {
+            ntcb::launch_batch_noise(I.stream, I.dm, I.d.seed, it, M, I.mstride, I.zdec, I.tgt, I.bidx, I.feat_t, I.tgt_t, p0, std::max(n, 0),
+                                     I.P, I.mlp_eps);
+        });
+        I.last_M = M;
+    }
     if (n <= 0) return;
-    timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, p0, n, I.P, I.mlp_eps); });
+    if (!draw) timed(I, "noise", 1, [&] { ntcb::launch_mlp_noise(I.stream, I.d.seed, it, p0, n, I.P, I.mlp_eps); });
     ntcb::PopArgs a{};
     a.mode = 0; a.it = it; a.sigma = sigma; a.fd_h = 0.0f; a.cand_begin = p0; a.ncand = n;
     a.M = M; a.mstride = I.mstride; a.chunk = pop_chunk(I, M);
@@ -539,8 +547,7 @@ void mlp_step_impl(Impl& I, int it, float sigma, float lr, int N, int M) {
         fprintf(stderr, "ntc_b200: MLP step with %d pairs / %d pixels exceeds the buffers sized at init (%d / %d)\n", N, M, I.pairs_cap, I.Mcap);
         exit(1);
     }
-    draw_batch(I, it, M);
-    es_eval_pairs(I, it, sigma, M, 0, N, I.fit, true);
+    es_eval_pairs(I, it, sigma, M, 0, N, I.fit, true, true);
     es_apply(I, it, sigma, lr, N, I.fit, false, true);
 }
 
@@ -641,7 +648,6 @@ void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_e
 // dpix in blocks of rows_per_block image rows, each [K][rows_per_block * W] (one block of H rows: [K][W * H]).
 void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix, int rows_per_block) {
     const unsigned mask = lat_mask(I);
-    NTCB_CHECK(cudaMemsetAsync(I.zgrad, 0, I.nz * sizeof(float), I.stream));
     const bool rate = I.dct_live && I.rate_es;
     if (rate) NTCB_CHECK(cudaMemsetAsync(I.dcnt + 2, 0, sizeof(int), I.stream));
     I.dct_evals = rate ? (int)(I.dct_n * K) : 0;
@@ -655,20 +661,22 @@ void lat_apply_part(Impl& I, float sigma, float lr, int K, const float* dpix, in
             I.dct_last_K = K;
         }
         const float scale = 1.0f / (2.0f * (float)K * sigma);
+        // Adam runs inside each ES-trained level's gather; a level that is never ES-trained (the --qat level) has a
+        // zero gradient and zero moments, which leave it unchanged, so skipping it there is exact.
+        I.lat_t++;
+        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
+        const ntcb::LatAdam adam{I.z, I.zm, I.zv, lr, c1, c2};
         for (int l = 0; l < I.d.nlev; l++) {
             if (!(mask & (1u << l))) continue;
             const ntcb::RateTerm r = (l == 0) ? rt : ntcb::RateTerm{nullptr, 0.0f, 0, 0};
             timed(I, "lat_gather", 1, [&] {
                 ntcb::launch_lat_gather(I.stream, I.dm, l, I.lvl_xr[l], I.lvl_yr[l], dpix, I.lat_eps, I.nz, K, scale, r, I.zgrad, rows_per_block,
-                                        0, I.d.lv[l].H, 0);
+                                        0, I.d.lv[l].H, 0, adam);
             });
         }
-    }
-    timed(I, "adam", 1, [&] {
+    } else {
         I.lat_t++;
-        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
-        ntcb::launch_adam(I.stream, I.z, I.zgrad, I.zm, I.zv, I.nz, lr, c1, c2);
-    });
+    }
     snap_latent_impl(I);
     I.lat_step_no++;
 }
@@ -843,9 +851,9 @@ void shard_mlp_eval_grad_impl(Impl& I, int it, float sigma, int N, int M, int p0
     const int n = p1 - p0, seglen = es_seglen(N);
     double* fit = static_cast<double*>(block);
     float* part = reinterpret_cast<float*>(static_cast<char*>(block) + 16LL * n);
-    draw_batch(I, it, M);
-    // this rank's pairs' fitness, loss differences (in the same launch) and gradient segments (their noise is in mlp_eps)
-    es_eval_pairs(I, it, sigma, M, p0, p1, fit, true);
+    // minibatch and this rank's pairs' noise (one launch), fitness with the loss differences (one launch), and the
+    // gradient segments of these pairs
+    es_eval_pairs(I, it, sigma, M, p0, p1, fit, true, true);
     const float scale = 1.0f / (2.0f * (float)N * sigma);
     timed(I, "mlp_grad", 1, [&] { ntcb::launch_es_grad_partial(I.stream, I.dl, I.mlp_eps, n, I.P, scale, seglen, part); });
 }
@@ -878,17 +886,13 @@ long long shard_lat_rows_impl(Impl& I, float sigma, float lr, int K, int lvl, in
     ensure_lat(I, K);
     const long long W = I.d.W;
     lat_eval_part(I, sigma, K, (long long)pa * W, (long long)pb * W, I.dpix, (long long)(pb - pa) * W);
-    const long long off = (long long)L.off + (long long)ta * L.W * L.C, n = (long long)(tb - ta) * L.W * L.C;
-    NTCB_CHECK(cudaMemsetAsync(I.zgrad + off, 0, n * sizeof(float), I.stream));
+    const long long off = (long long)L.off + (long long)ta * L.W * L.C;
     const float scale = 1.0f / (2.0f * (float)K * sigma);
+    I.lat_t++;
+    float c1, c2; adam_coeffs(I.lat_t, c1, c2);
     timed(I, "lat_gather", 1, [&] {
         ntcb::launch_lat_gather(I.stream, I.dm, lvl, I.lvl_xr[lvl], I.lvl_yr[lvl], I.dpix, I.lat_eps, I.nz, K, scale,
-                                ntcb::RateTerm{nullptr, 0.0f, 0, 0}, I.zgrad, pb - pa, ta, tb, pa);
-    });
-    timed(I, "adam", 1, [&] {
-        I.lat_t++;
-        float c1, c2; adam_coeffs(I.lat_t, c1, c2);
-        ntcb::launch_adam(I.stream, I.z + off, I.zgrad + off, I.zm + off, I.zv + off, n, lr, c1, c2);
+                                ntcb::RateTerm{nullptr, 0.0f, 0, 0}, I.zgrad, pb - pa, ta, tb, pa, ntcb::LatAdam{I.z, I.zm, I.zv, lr, c1, c2});
     });
     I.lat_step_no++;
     return off;
@@ -1230,8 +1234,7 @@ void ntcb_shard_mlp_eval(ntcb_trainer* t, int it, float sigma, int N, int M, int
     require_ready(I); set_device(I);
     if (pair_begin < 0 || pair_end > N || pair_begin > pair_end || N > I.pairs_cap || M > I.Mcap || M < 1)
         die("shard_mlp_eval: pair range or sizes outside the buffers sized at init");
-    draw_batch(I, it, M);
-    es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit_dev);
+    es_eval_pairs(I, it, sigma, M, pair_begin, pair_end, fit_dev, false, true);
 }
 void ntcb_shard_lat_eval(ntcb_trainer* t, float sigma, int K, int row_begin, int row_end, float* block_dev) {
     Impl& I = t->impl;
@@ -1490,8 +1493,7 @@ void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, f
         } else {
             const size_t bytes = 16 * (size_t)n;
             ensure_xbuf(I, (long long)bytes * G);
-            draw_batch(I, it, M);
-            es_eval_pairs(I, it, mlp_sigma, M, p0, p0 + n, reinterpret_cast<double*>(I.xbuf + (size_t)r * bytes));
+            es_eval_pairs(I, it, mlp_sigma, M, p0, p0 + n, reinterpret_cast<double*>(I.xbuf + (size_t)r * bytes), false, true);
             gather(I.xbuf, bytes);
             es_apply(I, it, mlp_sigma, mlp_lr, N, reinterpret_cast<const double*>(I.xbuf), true);
         }

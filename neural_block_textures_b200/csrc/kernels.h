@@ -40,6 +40,9 @@ void launch_batch(cudaStream_t s, const DevModel& m, uint64_t seed, int it, int 
 void launch_noise_fill(cudaStream_t s, uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, long long n,
                        float* gauss, uint32_t* u32);
 void launch_mlp_noise(cudaStream_t s, uint64_t seed, int it, int pair_begin, int npairs, int P, float* eps);
+// launch_batch and launch_mlp_noise (pairs [pair_begin, pair_begin + npairs)) in one launch.
+void launch_batch_noise(cudaStream_t s, const DevModel& m, uint64_t seed, int it, int M, int mstride, const float* zdec,
+                        const float* tgt, int* bidx, float* feat_t, float* tgt_t, int pair_begin, int npairs, int P, float* eps);
 void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs& a);
 // Tensor-core (tcgen05, 3xTF32) population evaluation for the fixed shapes; false when the shape or the
 // chunk size (a multiple of pop_tc_rows()) does not fit it, in which case nothing was launched.
@@ -80,11 +83,16 @@ struct RateTerm {              // DCT rate term of the latent gradient (level 0)
     float rate_scale;
     int BW, C;
 };
+struct LatAdam {              // Adam on the texels a gather produces (latent, moments, host bias corrections)
+    float *z, *m, *v;
+    float lr, c1, c2;
+};
 // Texel rows [ty0, ty1) of the level. dpix: blocks of rows_per_block image rows starting at image row row_base,
-// each block [K][rows_per_block * W] (one block from row 0 = the plain [K][W * H]).
+// each block [K][rows_per_block * W] (one block from row 0 = the plain [K][W * H]). Writes the texels' gradient
+// to grad (not accumulated) and applies the Adam step to them.
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
-                       int rows_per_block, int ty0, int ty1, int row_base);
+                       int rows_per_block, int ty0, int ty1, int row_base, const LatAdam& adam);
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
                 const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end,
                 int max_bits);

@@ -1,5 +1,6 @@
 // Latent ES (all K antithetic pairs in one pass over the image), the footprint gather of the latent
 // gradient, and the exhaustive per-texel selector search of --qat.
+#include "adam.cuh"
 #include "kernels.h"
 #include "mlp_tile.cuh"
 #include "latent_features.cuh"
@@ -135,7 +136,7 @@ void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* 
 // them over the pairs' threads is what sets the speed.
 __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, const int* __restrict__ yr, const float* __restrict__ dpix,
                              const float* __restrict__ eps, long long nz, int K, float scale, RateTerm rate, float* __restrict__ grad,
-                             int rpb, int ty0, int ty1, int row_base, int tpc) {
+                             int rpb, int ty0, int ty1, int row_base, int tpc, LatAdam adam) {
     extern __shared__ float dsum[];   // [tpc][K]
     const DevLevel& L = m.lv[level];
     const long long t0 = (long long)ty0 * L.W + (long long)blockIdx.x * tpc;
@@ -169,27 +170,34 @@ __global__ void k_lat_gather(DevModel m, int level, const int* __restrict__ xr, 
     if ((int)threadIdx.x >= tpc || t >= t_end) return;
     const int tx = (int)(t % L.W), ty = (int)(t / L.W);
     const long long base = L.off + t * L.C;
-    for (int k = 0; k < K; k++) {
-        const float w = dsum[threadIdx.x * K + k] * scale;
-        const float* ek = eps + (long long)k * nz;
-        for (int c = 0; c < L.C; c++) grad[base + c] = fmaf(w, ek[base + c], grad[base + c]);
-        if (rate.dbits) {
-            const long long b = (long long)(ty / 8) * rate.BW + tx / 8;
-            const int* db = rate.dbits + (long long)k * ((long long)(m.H / 8) * rate.BW * rate.C);
-            for (int c = 0; c < L.C; c++)
-                grad[base + c] = fmaf(rate.rate_scale * (float)db[b * rate.C + c] * scale, ek[base + c], grad[base + c]);
+    const long long b = (long long)(ty / 8) * rate.BW + tx / 8;
+    // per channel: the pairs' terms in pair order (mse term, then its rate term), from zero — the chain the
+    // reference's scatter forms on a zeroed gradient — then Adam on the texel
+    for (int c = 0; c < L.C; c++) {
+        float g = 0.0f;
+        for (int k = 0; k < K; k++) {
+            const float e = eps[(long long)k * nz + base + c];
+            g = fmaf(dsum[threadIdx.x * K + k] * scale, e, g);
+            if (rate.dbits) {
+                const int* db = rate.dbits + (long long)k * ((long long)(m.H / 8) * rate.BW * rate.C);
+                g = fmaf(rate.rate_scale * (float)db[b * rate.C + c] * scale, e, g);
+            }
         }
+        grad[base + c] = g;
+        float th = adam.z[base + c], mm = adam.m[base + c], vv = adam.v[base + c];
+        adam_update(th, g, mm, vv, adam.lr, adam.c1, adam.c2);
+        adam.z[base + c] = th; adam.m[base + c] = mm; adam.v[base + c] = vv;
     }
 }
 
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
-                       int rows_per_block, int ty0, int ty1, int row_base) {
+                       int rows_per_block, int ty0, int ty1, int row_base, const LatAdam& adam) {
     const long long ntx = (long long)m.lv[level].W * (ty1 - ty0);
     if (ntx <= 0) return;
     const int tpc = std::max(1, std::min(32, 12288 / std::max(1, K)));
     k_lat_gather<<<blocks_for(ntx, tpc), 128, (size_t)tpc * K * sizeof(float), s>>>(
-        m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block, ty0, ty1, row_base, tpc);
+        m, level, xr, yr, dpix, eps, nz, K, scale, rate, grad, rows_per_block, ty0, ty1, row_base, tpc, adam);
     NTCB_CHECK(cudaGetLastError());
 }
 

@@ -1,5 +1,6 @@
 // MLP population kernels: minibatch draw, ES noise, population evaluation (ES pairs and FD
 // candidates), fitness reduction, ES gradient + Adam, full-image decode.
+#include "adam.cuh"
 #include "kernels.h"
 #include "mlp_tile.cuh"
 #include "noise.cuh"
@@ -32,11 +33,9 @@ int pop_chunks(int M, int chunk) { return (M + chunk - 1) / chunk; }
 // MlpTrainer::draw_batch (main.cpp:1825-1833, hash branch) + the feature / target rows the population
 // kernel reads: slot s draws pixel uniform_below(u32(seed, batch stream, it, 0, s), W H). Features and
 // targets are stored transposed ([feature][slot]) so that a warp's loads of one feature are coalesced.
-__global__ void k_batch(DevModel m, uint64_t seed, int it, int M, int mstride, const float* __restrict__ zdec,
-                        const float* __restrict__ tgt, int* __restrict__ bidx, float* __restrict__ feat_t,
-                        float* __restrict__ tgt_t) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= M) return;
+__device__ __forceinline__ void batch_slot(const DevModel& m, uint64_t seed, int it, int s, int mstride, const float* __restrict__ zdec,
+                                           const float* __restrict__ tgt, int* __restrict__ bidx, float* __restrict__ feat_t,
+                                           float* __restrict__ tgt_t) {
     const uint64_t key = stream_key(seed, kStreamBatchPix, (uint32_t)it, 0);
     const int idx = (int)uniform_below(draw_u32(key, (uint64_t)s), (uint32_t)(m.W * m.H));
     bidx[s] = idx;
@@ -45,6 +44,12 @@ __global__ void k_batch(DevModel m, uint64_t seed, int it, int M, int mstride, c
     for (int i = 0; i < m.nin; i++) feat_t[(long long)i * mstride + s] = f[i];
     const float* t = tgt + (long long)idx * m.nout;
     for (int c = 0; c < m.nout; c++) tgt_t[(long long)c * mstride + s] = t[c];
+}
+__global__ void k_batch(DevModel m, uint64_t seed, int it, int M, int mstride, const float* __restrict__ zdec,
+                        const float* __restrict__ tgt, int* __restrict__ bidx, float* __restrict__ feat_t,
+                        float* __restrict__ tgt_t) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s < M) batch_slot(m, seed, it, s, mstride, zdec, tgt, bidx, feat_t, tgt_t);
 }
 
 void launch_batch(cudaStream_t s, const DevModel& m, uint64_t seed, int it, int M, int mstride, const float* zdec,
@@ -76,6 +81,34 @@ __global__ void k_noise_fill(uint64_t seed, uint32_t stream, uint32_t step, uint
 void launch_noise_fill(cudaStream_t s, uint64_t seed, uint32_t stream, uint32_t step, uint32_t pair, uint64_t index0, long long n,
                        float* gauss, uint32_t* u32) {
     k_noise_fill<<<blocks_for(n, 256), 256, 0, s>>>(seed, stream, step, pair, index0, n, gauss, u32);
+    NTCB_CHECK(cudaGetLastError());
+}
+
+// The minibatch of step `it` and the ES noise of its pairs [pair_begin, pair_begin + npairs) in one launch: the
+// first blocks draw the minibatch slots, the rest fill eps row by row (kBatchNoiseTPB weights per block).
+constexpr int kBatchNoiseTPB = 128;
+__global__ void __launch_bounds__(kBatchNoiseTPB) k_batch_noise(DevModel m, uint64_t seed, int it, int M, int mstride,
+                                                                const float* __restrict__ zdec, const float* __restrict__ tgt,
+                                                                int* __restrict__ bidx, float* __restrict__ feat_t,
+                                                                float* __restrict__ tgt_t, int batch_blocks, int pair_begin, int P,
+                                                                int row_blocks, float* __restrict__ eps) {
+    if ((int)blockIdx.x < batch_blocks) {
+        const int s = blockIdx.x * kBatchNoiseTPB + threadIdx.x;
+        if (s < M) batch_slot(m, seed, it, s, mstride, zdec, tgt, bidx, feat_t, tgt_t);
+        return;
+    }
+    const int b = blockIdx.x - batch_blocks, i = b / row_blocks;
+    const int k = (b - i * row_blocks) * kBatchNoiseTPB + threadIdx.x;
+    if (k >= P) return;
+    const uint64_t key = stream_key(seed, kStreamMlp, (uint32_t)it, (uint32_t)(pair_begin + i));
+    eps[(long long)i * P + k] = gauss_at(key, (uint64_t)k);
+}
+void launch_batch_noise(cudaStream_t s, const DevModel& m, uint64_t seed, int it, int M, int mstride, const float* zdec,
+                        const float* tgt, int* bidx, float* feat_t, float* tgt_t, int pair_begin, int npairs, int P, float* eps) {
+    const int batch_blocks = (int)blocks_for(M, kBatchNoiseTPB), row_blocks = (int)blocks_for(P, kBatchNoiseTPB);
+    const long long blocks = batch_blocks + (long long)row_blocks * std::max(0, npairs);
+    k_batch_noise<<<(unsigned)blocks, kBatchNoiseTPB, 0, s>>>(m, seed, it, M, mstride, zdec, tgt, bidx, feat_t, tgt_t, batch_blocks,
+                                                             pair_begin, P, row_blocks, eps);
     NTCB_CHECK(cudaGetLastError());
 }
 
@@ -313,15 +346,6 @@ void launch_es_grad_partial(cudaStream_t s, const double* dl, const float* eps, 
     dim3 grid(blocks_for(P, 128), (unsigned)nseg);
     k_es_grad_partial<<<grid, 128, 0, s>>>(dl, eps, N, P, scale, seglen, gpart);
     NTCB_CHECK(cudaGetLastError());
-}
-
-// Adam::step (main.cpp:1797-1809): theta -= lr * (m / c1) / (sqrt(v / c2) + eps), c1 / c2 computed on the host.
-__device__ __forceinline__ void adam_update(float& theta, float g, float& m, float& v, float lr, float c1, float c2) {
-    const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
-    m = b1 * m + (1.0f - b1) * g;
-    v = b2 * v + (1.0f - b2) * g * g;
-    const float mh = m / c1, vh = v / c2;
-    theta -= lr * mh / (sqrtf(vh) + eps);
 }
 
 __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P, float* __restrict__ grad, float* __restrict__ theta,
