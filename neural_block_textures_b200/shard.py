@@ -159,11 +159,13 @@ class NativeShardedES:
     stream into the trainer's own buffers, on a communicator of its own. torch.distributed only carries the
     128-byte NCCL id from rank 0 to the others (any backend)."""
 
-    def __init__(self, trainer, dist, device=None, p2p: tuple[int, int, bool] | None = None):
+    def __init__(self, trainer, dist, device=None, p2p: tuple[int, int, bool] | None = None, comm_cls=None):
         """p2p = (N, K, qat): also set up the peer-memory exchanges (ntcb_p2p_export / import) for iterations with N
-        ES pairs, K latent pairs and the selector search on or off; without it every exchange goes through NCCL."""
+        ES pairs, K latent pairs and the selector search on or off; without it every exchange goes through NCCL.
+        comm_cls: the communicator class (neural_block_textures_b200.trainer.Comm unless given)."""
         import torch
-        from .trainer import Comm
+        from .trainer import Comm as _Comm
+        Comm = comm_cls or _Comm
         self.t, self.dist = trainer, dist
         self.world, self.rank = dist.get_world_size(), dist.get_rank()
         uid = torch.zeros(128, dtype=torch.uint8, device=device or "cpu")

@@ -235,3 +235,70 @@ def test_latent_texel_row_sharding_plumbing(tmp_path):
     want = np.array([0.5 * i for i in range(T.LW * T.LH * T.LC)], np.float32)
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"z{r}.npy"), want)
+
+
+# ---- NativeShardedES set-up and teardown (the host side of ntcb_comm_* / ntcb_p2p_*) with stand-ins for the
+# library's communicator and trainer, so the hand-over of the NCCL id and the IPC handles runs on two gloo ranks.
+class FakeComm:
+    def __init__(self, uid, world, rank):
+        self.uid, self.world, self.rank, self.closed = uid, world, rank, False
+
+    @staticmethod
+    def unique_id():
+        return bytes(range(128))
+
+    def close(self):
+        self.closed = True
+
+
+class FakeP2PTrainer:
+    def __init__(self):
+        self.log = []
+
+    def p2p_export(self, world, rank, N, K, qat):
+        self.log.append(("export", world, rank, N, K, qat))
+        return bytes([rank + 1]) * 64
+
+    def p2p_import(self, handles, world, rank):
+        self.log.append(("import", world, rank))
+        self.handles = handles
+
+    def p2p_release(self):
+        self.log.append(("release",))
+
+
+def _native_setup_main(rank, world, port, out_dir):
+    from neural_block_textures_b200.shard import NativeShardedES
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tr = FakeP2PTrainer()
+        nat = NativeShardedES(tr, dist, device="cpu", p2p=(64, 4, True), comm_cls=FakeComm)
+        comm = nat.comm
+        nat.close()
+        np.save(os.path.join(out_dir, f"uid{rank}.npy"), np.frombuffer(comm.uid, np.uint8))
+        np.save(os.path.join(out_dir, f"handles{rank}.npy"), np.frombuffer(tr.handles, np.uint8))
+        with open(os.path.join(out_dir, f"log{rank}.txt"), "w") as f:
+            f.write(repr(tr.log) + "\n" + repr((comm.world, comm.rank, comm.closed, nat.p2p)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_native_driver_setup_two_ranks(tmp_path):
+    """Rank 0's NCCL id reaches every rank unchanged; the IPC handles come back concatenated in rank order;
+    close() releases the peer mappings on every rank before the communicator goes."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_native_setup_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=120)
+        assert pr.exitcode == 0
+    want = bytes([1]) * 64 + bytes([2]) * 64
+    for r in range(2):
+        assert np.load(tmp_path / f"uid{r}.npy").tobytes() == bytes(range(128))
+        assert np.load(tmp_path / f"handles{r}.npy").tobytes() == want
+        log, state = (tmp_path / f"log{r}.txt").read_text().splitlines()
+        assert log == repr([("export", 2, r, 64, 4, True), ("import", 2, r), ("release",)])
+        assert state == repr((2, r, True, False))
