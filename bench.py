@@ -538,7 +538,8 @@ def main():
         fdec = cfg.decodes_per_iter(fd=True)
         fd_line = {"steps": args.fd_steps, "ms_per_step": fms / args.fd_steps, "decodes_per_step": fdec,
                    "value": sum(fdec.values()) * args.fd_steps / (fms * 1e-3), "unit": "decodes/s",
-                   "kernel": "k_pop_eval_x2 (packed FP32, exact) for the 2P + 2 FD candidates"}
+                   "kernel": ("k_pop_eval_tc (tcgen05 3xTF32)" if tr.pop_kernel() == "tensor" else "k_pop_eval_x2 (packed FP32, exact)")
+                             + ": the stats pair and the 2P FD candidates in one launch"}
 
     # ---- end to end through the public API with host buffers (pinned), copies inside the timed region
     zh = torch.empty(spec.nz, dtype=torch.float32, pin_memory=True).numpy()

@@ -555,19 +555,25 @@ void mlp_step_impl(Impl& I, int it, float sigma, float lr, int N, int M) {
 // (cuda/ntc_cuda.cu:1059-1068), then (lp, lm) of every weight j in the range (both signs in one CTA) into fit.
 void fd_eval_part(Impl& I, int it, float h, int M, int j0, int j1, double* fit) {
     draw_batch(I, it, M);
+    const int nw = std::max(0, j1 - j0);
+    // one launch: the unperturbed stats pair first, then weights j0 .. j1 - 1 at w_j +- h; on the tensor-core kernel
+    // unless the exact kernels are selected (the +- candidates of a weight differ in that weight only, so their
+    // 3xTF32 rounding is nearly the same on both sides and cancels in the difference)
     ntcb::PopArgs a{};
-    a.mode = 0; a.it = it; a.sigma = 0.0f; a.cand_begin = 0; a.ncand = 1; a.M = M; a.mstride = I.mstride;
-    a.chunk = pop_chunk(I, M); a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t;
+    a.mode = 1; a.it = it; a.sigma = 0.0f; a.fd_h = h; a.cand_begin = j0; a.ncand = nw + 1; a.stats_first = 1;
+    a.M = M; a.mstride = I.mstride; a.chunk = pop_chunk(I, M);
+    a.w0 = I.w; a.eps = I.mlp_eps; a.feat_t = I.feat_t; a.tgt_t = I.tgt_t; a.tc_err = I.tc_err;
     const int chunks = ntcb::pop_chunks(M, a.chunk);
-    ensure_part(I, (long long)std::max(1, I.P) * 2 * chunks);
+    ensure_part(I, (long long)(nw + 1) * 2 * chunks);
     a.part = I.part;
     const double norm = 3.0 * (double)I.d.wsum * M;
-    timed(I, "fd_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, 1, chunks, norm, I.fit_stats); });
-    if (j1 <= j0) return;
-    a.mode = 1; a.fd_h = h; a.cand_begin = j0; a.ncand = j1 - j0;
-    timed(I, "fd_eval", 1, [&] { ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a); });
-    timed(I, "mlp_finish", 1, [&] { ntcb::launch_pop_finish(I.stream, I.part, j1 - j0, chunks, norm, fit); });
+    timed(I, "fd_eval", 1, [&] {
+        if (!(I.tensor_pop && ntcb::launch_pop_eval_tc(I.stream, I.shape, I.dm, a))) ntcb::launch_pop_eval(I.stream, I.shape, I.dm, a);
+    });
+    timed(I, "mlp_finish", nw > 0 ? 2 : 1, [&] {
+        ntcb::launch_pop_finish(I.stream, I.part, 1, chunks, norm, I.fit_stats);
+        if (nw > 0) ntcb::launch_pop_finish(I.stream, I.part + 2LL * chunks, nw, chunks, norm, fit);
+    });
 }
 
 // FD gradient from the (lp, lm) of all P weights (weight order; I.fit unless given) and the Adam step.

@@ -24,6 +24,8 @@ struct PopArgs {
     float sigma;               // ES sigma (0: the unperturbed weights, no noise read)
     float fd_h;                // FD step
     int cand_begin, ncand;     // ES: global pair index range; FD: weight index range
+    int stats_first;           // FD: candidate 0 is the unperturbed pair (the step's statistics), candidate i >= 1 weight
+                               // cand_begin + i - 1
     int M, mstride;            // minibatch size and the row stride of feat_t / tgt_t
     int chunk;                 // rows per CTA along the batch (multiple of the tile rows)
     const float* w0;           // base weights (flat reference layout)

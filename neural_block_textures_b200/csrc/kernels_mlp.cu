@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(TPB, S::kPopMinBlocks) k_pop_eval_x2(DevModel 
     extern __shared__ __align__(16) float ws[];
     __shared__ double red[TPB / 32];
     constexpr int R = 2 * R2;
-    const int cand = a.cand_begin + blockIdx.x;
+    const int cand = pop_cand(a, blockIdx.x);
     const int chunk = blockIdx.y;
     build_weight_pair_x2<S>(m, a, cand, ws);
     const int row0 = chunk * a.chunk;
@@ -210,7 +210,7 @@ template <int TPB>
 __global__ void __launch_bounds__(TPB) k_pop_eval_generic(DevModel m, PopArgs a, int chunks) {
     extern __shared__ __align__(16) float ws[];
     __shared__ double red[TPB / 32];
-    const int cand = a.cand_begin + blockIdx.x;
+    const int cand = pop_cand(a, blockIdx.x);
     const int chunk = blockIdx.y;
     build_weight_pair_flat(m, a, cand, ws);
     const int row0 = chunk * a.chunk;

@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         const int pl = (int)(item / chunks), chunk = (int)(item - (long long)pl * chunks);
         if (pl != cur) {
             // stage both perturbed weight sets of this pair (the previous pair's MMAs have all completed)
-            const int cand = a.cand_begin + pl;
+            const int cand = pop_cand(a, pl);
             const float* e = (a.mode == 0 && a.sigma != 0.0f) ? a.eps + (long long)pl * m.P : nullptr;
             for (int k = tid; k < m.P; k += kTcRows) {
                 float wp, wm;

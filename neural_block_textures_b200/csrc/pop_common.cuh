@@ -22,6 +22,11 @@ __device__ __forceinline__ double cta_sum(double v, double* red) {
 // The perturbed weight of slot k for sign +/- : ES w0 +- sigma eps with each perturbed weight rounded once,
 // fma(+-sigma, eps, w0) (MlpTrainer::step, main.cpp:1856); FD: w0 except weight j at the float-realised
 // w0[j] + h / w0[j] - h (main.cpp:1906-1910).
+// Candidate index of launch slot i (perturbed_weight's `cand`: an ES pair, an FD weight, or -1 = unperturbed).
+__device__ __forceinline__ int pop_cand(const PopArgs& a, int i) {
+    return a.stats_first ? (i == 0 ? -1 : a.cand_begin + i - 1) : a.cand_begin + i;
+}
+
 __device__ __forceinline__ void perturbed_weight(const PopArgs& a, const float* e, int k, int cand, float& wp, float& wm) {
     const float w0 = a.w0[k];
     wp = w0; wm = w0;
