@@ -174,13 +174,30 @@ class NativeShardedES:
         dist.broadcast(uid, 0)
         self.comm = Comm(bytes(uid.cpu().numpy().tobytes()), self.world, self.rank)
         self.p2p = False
+        self.p2p_why = ""
         if p2p is not None and self.world > 1:
+            # collective decision: every rank uses the peer exchange, or none does (NCCL then)
             N, K, qat = p2p
-            mine = trainer.p2p_export(self.world, self.rank, N, K, qat)
+            try:
+                mine = trainer.p2p_export(self.world, self.rank, N, K, qat)
+            except RuntimeError as e:
+                mine, self.p2p_why = None, str(e)
             allh = [None] * self.world
             dist.all_gather_object(allh, mine)
-            trainer.p2p_import(b"".join(allh), self.world, self.rank)
-            self.p2p = True
+            ok = all(h is not None for h in allh)
+            if ok:
+                try:
+                    trainer.p2p_import(b"".join(allh), self.world, self.rank)
+                except RuntimeError as e:
+                    ok, self.p2p_why = False, str(e)
+            oks = [None] * self.world
+            dist.all_gather_object(oks, ok)
+            if all(oks):
+                self.p2p = True
+            else:
+                if ok:
+                    trainer.p2p_release()
+                self.p2p_why = self.p2p_why or "another rank could not set up the peer exchange"
 
     def plan(self, mlp_mode: int, N: int, M: int, K: int, qat: bool):
         return self.t.shard_iteration_plan(self.world, self.rank, mlp_mode, N, M, K, qat)

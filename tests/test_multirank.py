@@ -252,11 +252,14 @@ class FakeComm:
 
 
 class FakeP2PTrainer:
-    def __init__(self):
+    def __init__(self, fail_export=False):
         self.log = []
+        self.fail_export = fail_export
 
     def p2p_export(self, world, rank, N, K, qat):
         self.log.append(("export", world, rank, N, K, qat))
+        if self.fail_export:
+            raise RuntimeError("ntcb_p2p_export: cudaIpcGetMemHandle failed")
         return bytes([rank + 1]) * 64
 
     def p2p_import(self, handles, world, rank):
@@ -302,3 +305,33 @@ def test_native_driver_setup_two_ranks(tmp_path):
         log, state = (tmp_path / f"log{r}.txt").read_text().splitlines()
         assert log == repr([("export", 2, r, 64, 4, True), ("import", 2, r), ("release",)])
         assert state == repr((2, r, True, False))
+
+
+def _native_fallback_main(rank, world, port, out_dir):
+    from neural_block_textures_b200.shard import NativeShardedES
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tr = FakeP2PTrainer(fail_export=(rank == 1))
+        nat = NativeShardedES(tr, dist, device="cpu", p2p=(64, 4, True), comm_cls=FakeComm)
+        with open(os.path.join(out_dir, f"fb{rank}.txt"), "w") as f:
+            f.write(repr(tr.log) + "\n" + repr((nat.p2p, bool(nat.p2p_why))))
+        nat.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_native_driver_peer_exchange_all_or_none(tmp_path):
+    """When one rank cannot set up the peer exchange, no rank uses it (all stay on NCCL) and nobody waits."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_native_fallback_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=120)
+        assert pr.exitcode == 0
+    for r in range(2):
+        log, state = (tmp_path / f"fb{r}.txt").read_text().splitlines()
+        assert state == repr((False, True))
+        assert "import" not in log
