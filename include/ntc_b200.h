@@ -188,10 +188,13 @@ typedef struct ntcb_progress_stats {
     float lat_mean[NTCB_MAX_LEVELS], lat_sd[NTCB_MAX_LEVELS], lat_max[NTCB_MAX_LEVELS];
     /* --qat: level-0 training values off their channel's grid (main.cpp:4196-4200); 0 without --qat */
     long long qat_off_grid;
-    /* 1 when level 0 is DCT-coded (set_dct): its bits are left out of every figure above and its quantized copy is
-       the snapped plane; the caller adds its bit simulator's totals (dct_analyze, main.cpp:1080) as bitrate_stats
-       does at main.cpp:2294-2301 */
+    /* 1 when level 0 is DCT-coded and live (set_dct): its quantized copy is the snapped plane and its bits are its
+       bit simulator's (dct_analyze, main.cpp:1080, run on the device's symbols as the progress print runs it),
+       added to the figures above as bitrate_stats does at main.cpp:2294-2301 */
     int level0_dct;
+    /* the bit simulator's totals for that level (bits, all channels): raw, order-0, context, and the header part
+       each includes; 0 without a live DCT level */
+    double dct_bits_raw, dct_bits_h0, dct_bits_ctx, dct_bits_header;
 } ntcb_progress_stats;
 /* The progress print's statistics for the current model (main.cpp:4155-4205) without downloading it:
  * level_bits[l] = the post-hoc depth of each continuous level (bitrate_stats' lbits, main.cpp:2288; ignored for

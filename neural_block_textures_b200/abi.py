@@ -97,6 +97,7 @@ class ProgressStats(C.Structure):
         ("lat_mean", C.c_float * MAX_LEVELS), ("lat_sd", C.c_float * MAX_LEVELS), ("lat_max", C.c_float * MAX_LEVELS),
         ("qat_off_grid", C.c_longlong),
         ("level0_dct", C.c_int),
+        ("dct_bits_raw", C.c_double), ("dct_bits_h0", C.c_double), ("dct_bits_ctx", C.c_double), ("dct_bits_header", C.c_double),
     ]
 
 

@@ -1010,6 +1010,45 @@ void ntcb_kernel_time(ntcb_trainer* t, const char* kernel, double* total_ms, int
 long long ntcb_launch_count(const ntcb_trainer* t) { return t->impl.launches; }
 // The progress print's statistics (main.cpp:4155-4205) on the device; see ntcb_print_stats. The host part
 // below is bitrate_stats' arithmetic (main.cpp:2272-2352) on the device's exact histograms, term for term.
+// The bit simulator's totals from the token statistics of k_dct_tokens (dct_analyze, main.cpp:1080-1160): every
+// token is charged its symbol's code length -log2(count / total) under the order-0 model (raw, |q|, DC residual,
+// scale code) or the context model (run and |q| given the zigzag position of the previous nonzero), so each class
+// sums to count x code length over its histogram; one bit per sign; raw fixed lengths dc_raw_bits per block, 7 + 8
+// + 1 per nonzero, 7 per EOB, 4 per scale code; a 96-bit header per channel. The progress print has no context
+// statistics for the code plane and charges its order-0 figure in the context total too.
+static void dct_sim_totals(const int* hist, int C, double nb, int dc_step, double& raw, double& h0, double& ctx, double& header) {
+    auto cl0 = [](double cnt, double tot) { return cnt > 0 && tot > 0 ? -std::log2(cnt / tot) : 0.0; };
+    auto ent = [&](const int* h, int n, double tot) {
+        double e = 0;
+        for (int k = 0; k < n; k++) if (h[k]) e += (double)h[k] * cl0(h[k], tot);
+        return e;
+    };
+    int dc_raw_bits = 0;
+    { const int lvl = 512 / std::max(1, dc_step) + 1; while ((1 << dc_raw_bits) < lvl) dc_raw_bits++; }
+    raw = h0 = ctx = header = 0;
+    for (int c = 0; c < C; c++) {
+        const int* H = hist + (long long)c * ntcb::kDctHistInts;
+        const double nrun = H[ntcb::kDctCounts], neob = H[ntcb::kDctCounts + 1];
+        const double dc = ent(H + ntcb::kDctDcres, 4097, nb);
+        const double code = ent(H + ntcb::kDctCode, 16, nb);
+        const double run0 = ent(H + ntcb::kDctRun, 65, nrun + neob), mag0 = ent(H + ntcb::kDctMag, 257, nrun);
+        double runc = 0, magc = 0;
+        for (int prev = 0; prev < 64; prev++) {
+            const int* cr = H + ntcb::kDctCtxRun + prev * 65;
+            const int* cm = H + ntcb::kDctCtxMag + prev * 257;
+            double tr = 0, tm = 0;
+            for (int r = 0; r < 65; r++) tr += cr[r];
+            for (int m = 0; m < 257; m++) tm += cm[m];
+            runc += ent(cr, 65, tr);
+            magc += ent(cm, 257, tm);
+        }
+        raw += nb * dc_raw_bits + 16.0 * nrun + 7.0 * neob + 4.0 * nb + 96.0;
+        h0 += dc + run0 + mag0 + nrun + code + 96.0;
+        ctx += dc + runc + magc + nrun + code + 96.0;
+        header += 96.0;
+    }
+}
+
 static int print_stats_impl(Impl& I, const int* level_bits, int ew, int eh, float* zq_out, ntcb_progress_stats* out) {
     using namespace ntcb;
     require_ready(I); set_device(I);
@@ -1032,7 +1071,7 @@ static int print_stats_impl(Impl& I, const int* level_bits, int ew, int eh, floa
             q.hstride = std::max(q.hstride, 1 << std::min(16, std::max(0, q.bits[c])));
         }
         q.mm_at = ints; ints += 2 * C;
-        q.hist_at = ints; ints += q.dct ? 0 : 2LL * C * q.hstride;
+        q.hist_at = ints; ints += q.dct ? (long long)C * kDctHistInts : 2LL * C * q.hstride;
     }
     // scratch: [ints] int32, then sse 2 x kMaxOut / 3 u64, the off-grid count u64, moments nl x 3 nb f64
     const size_t o_sse = ((size_t)ints * 4 + 15) / 16 * 16;
@@ -1053,6 +1092,9 @@ static int print_stats_impl(Impl& I, const int* level_bits, int ew, int eh, floa
             const long long ntex = (long long)L.W * L.H, off = I.dm.lv[l].off;
             if (q.dct) {
                 NTCB_CHECK(cudaMemcpyAsync(zq + off, I.zdec + off, (size_t)ntex * L.C * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+                NTCB_CHECK(cudaMemsetAsync(ibuf + q.hist_at, 0, (size_t)L.C * kDctHistInts * sizeof(int), I.stream));
+                launch_dct_tokens(I.stream, I.dtab, I.dsym, I.dcode, ibuf + q.hist_at);
+                I.launches += 1;
             } else {
                 if (q.mode == 0) { launch_level_minmax(I.stream, I.z + off, ntex, L.C, ibuf + q.mm_at); I.launches += 2; }
                 LevelQuantArgs a{};
@@ -1114,7 +1156,19 @@ static int print_stats_impl(Impl& I, const int* level_bits, int ew, int eh, floa
         const Plan& q = plan[l];
         const auto& L = d.lv[l];
         const double ntex = (double)L.W * L.H;
-        if (q.dct) { s.level0_dct = 1; continue; }
+        if (q.dct) {
+            // a live DCT-coded level 0: its bit simulator's totals (dct_analyze as the progress print runs it, with the
+            // order-0 figure of the code plane in place of its context figure), as bitrate_stats adds them
+            // (main.cpp:2294-2301)
+            double raw = 0, h0 = 0, ctx = 0, hdr = 0;
+            dct_sim_totals(hi + q.hist_at, L.C, (double)L.W / 8 * (L.H / 8), I.dtab.dc_step, raw, h0, ctx, hdr);
+            raw_bits += raw - hdr; ent_bits += h0 - hdr; ctx_bits += ctx - hdr; est_bits += h0 - hdr;
+            s.bpp_ctx_level0 += (ctx - hdr) / npix;
+            header_bits += hdr;
+            s.level0_dct = 1;
+            s.dct_bits_raw = raw; s.dct_bits_h0 = h0; s.dct_bits_ctx = ctx; s.dct_bits_header = hdr;
+            continue;
+        }
         const bool fixed = q.mode == 1, qes = q.mode == 2;
         if (!fixed && !qes) raw_bits += (double)((long long)L.W * L.H * L.C) * (double)q.bits[0];
         for (int c = 0; c < L.C; c++) {

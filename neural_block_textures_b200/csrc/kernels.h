@@ -123,5 +123,16 @@ int lat_moment_blocks();
 void launch_lat_moments(cudaStream_t s, const float* z, long long n, double* part);
 void launch_qat_offgrid(cudaStream_t s, const float* z, long long n, int C, const int* bits, const float* grid,
                         unsigned long long* count);
+// Token statistics of a DCT-coded level 0 for the bit simulator (dct_analyze, main.cpp:1080-1160): per channel,
+// kDctHistInts ints at hist + c * kDctHistInts (zeroed by the caller): the run histogram (run 64 = EOB), the |q|
+// histogram (|q| > 256 folded into 256), the run and |q| histograms per context (the zigzag position of the
+// previous nonzero), the DC-residual histogram (DC minus the left block's, the upper block's in the first column,
+// 0 for the first block; offset 2048, clamped to 0..4096), the scale-code histogram, then the counts of nonzero
+// tokens, of EOBs and of magnitudes above 256.
+constexpr int kDctRun = 0, kDctMag = kDctRun + 65, kDctCtxRun = kDctMag + 257, kDctCtxMag = kDctCtxRun + 64 * 65,
+              kDctDcres = kDctCtxMag + 64 * 257, kDctCode = kDctDcres + 4097, kDctCounts = kDctCode + 16,
+              kDctHistInts = kDctCounts + 3;
+struct DctTables;
+void launch_dct_tokens(cudaStream_t s, const DctTables& T, const int16_t* sym, const uint8_t* code, int* hist);
 
 }  // namespace ntcb

@@ -8,6 +8,7 @@
 // (the strict-FP quantizers of quant.cuh), integer histograms, and integer squared-error sums. The double
 // moment sums are reduced per block in a fixed order and finished on the host in block order.
 #include "kernels.h"
+#include "kernels_snap.h"
 #include "quant.cuh"
 
 namespace ntcb {
@@ -242,6 +243,70 @@ void launch_qat_offgrid(cudaStream_t s, const float* z, long long n, int C, cons
     if (n <= 0) return;
     const unsigned blocks = (unsigned)std::min<long long>(blocks_for(n, 256), 148 * 4);
     k_qat_offgrid<<<blocks, 256, 0, s>>>(z, n, C, bits, grid, count);
+    NTCB_CHECK(cudaGetLastError());
+}
+
+// One thread per (block, channel): the block's DC residual and scale code, then its ACs in zigzag order as
+// (run, |q|) tokens with the zigzag position of the previous nonzero as context, and an EOB unless the last
+// nonzero sits at position 63 (the walk of dct_analyze's first pass, main.cpp:1100-1119). The small tables are
+// counted in shared memory and added to the channel's histograms once per CTA; the context tables, which are
+// sparse, take global atomics directly.
+__global__ void k_dct_tokens(DctTables T, const int16_t* __restrict__ sym, const uint8_t* __restrict__ code, int* __restrict__ hist) {
+    constexpr int kSmall = 65 + 257;               // run, mag: the global offsets of these equal the shared ones
+    constexpr int kShared = kSmall + 4097 + 16;    // + dcres, code (contiguous in both layouts)
+    __shared__ int sh[kShared];
+    __shared__ int cnt[3];
+    const int c = blockIdx.y;
+    for (int i = threadIdx.x; i < kShared; i += blockDim.x) sh[i] = 0;
+    if (threadIdx.x < 3) cnt[threadIdx.x] = 0;
+    __syncthreads();
+    int* H = hist + (long long)c * kDctHistInts;
+    const long long nb = (long long)T.BW * T.BH;
+    const long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    int nrun = 0, neob = 0, nover = 0;
+    if (b < nb) {
+        const int16_t* s = sym + (b * T.C + c) * 64;
+        const int bx = (int)(b % T.BW), by = (int)(b / T.BW);
+        const int pred = bx > 0 ? sym[((b - 1) * T.C + c) * 64] : (by > 0 ? sym[((b - T.BW) * T.C + c) * 64] : 0);
+        atomicAdd(&sh[kSmall + max(0, min(4096, (int)s[0] - pred + 2048))], 1);
+        atomicAdd(&sh[kSmall + 4097 + min((int)code[b * T.C + c], 15)], 1);
+        int run = 0, prev = 0, lnz = 0;
+        for (int p = 1; p < 64; p++) {
+            const int q = s[T.zigzag[p]];
+            if (q == 0) { run++; continue; }
+            const int aq = abs(q), mag = min(256, aq);
+            if (aq > 256) nover++;
+            atomicAdd(&sh[kDctRun + run], 1);
+            atomicAdd(&sh[kDctMag + mag], 1);
+            atomicAdd(&H[kDctCtxRun + prev * 65 + run], 1);
+            atomicAdd(&H[kDctCtxMag + prev * 257 + mag], 1);
+            nrun++; lnz = p; prev = p; run = 0;
+        }
+        if (lnz < 63) {
+            atomicAdd(&sh[kDctRun + 64], 1);
+            atomicAdd(&H[kDctCtxRun + prev * 65 + 64], 1);
+            neob++;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        nrun += __shfl_down_sync(0xffffffffu, nrun, o);
+        neob += __shfl_down_sync(0xffffffffu, neob, o);
+        nover += __shfl_down_sync(0xffffffffu, nover, o);
+    }
+    if ((threadIdx.x & 31) == 0) { atomicAdd(&cnt[0], nrun); atomicAdd(&cnt[1], neob); atomicAdd(&cnt[2], nover); }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kShared; i += blockDim.x) {
+        const int v = sh[i];
+        if (v) atomicAdd(&H[i < kSmall ? i : kDctDcres + (i - kSmall)], v);
+    }
+    if (threadIdx.x < 3 && cnt[threadIdx.x]) atomicAdd(&H[kDctCounts + threadIdx.x], cnt[threadIdx.x]);
+}
+
+void launch_dct_tokens(cudaStream_t s, const DctTables& T, const int16_t* sym, const uint8_t* code, int* hist) {
+    const long long nb = (long long)T.BW * T.BH;
+    if (nb <= 0 || T.C <= 0) return;
+    dim3 grid((unsigned)((nb + 255) / 256), (unsigned)T.C);
+    k_dct_tokens<<<grid, 256, 0, s>>>(T, sym, code, hist);
     NTCB_CHECK(cudaGetLastError());
 }
 

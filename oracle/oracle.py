@@ -190,7 +190,7 @@ def refcpu_lib() -> C.CDLL:
     for n in ["ref_sizes", "ref_set_model", "ref_get_model", "ref_init_like_cli", "ref_features", "ref_decode_full",
               "ref_decode_err", "ref_mlp_reset_adam", "ref_last_batch", "ref_mlp_grad", "ref_lat_step", "ref_set_lat_step_no",
               "ref_qat_search", "ref_iteration", "ref_qes_fit_level", "ref_qes_tables", "ref_qes_refresh", "ref_get_zdec",
-              "ref_dct_enable", "ref_dct_fit", "ref_dct_state", "ref_dct_shadow_pull"]:
+              "ref_dct_enable", "ref_dct_fit", "ref_dct_state", "ref_dct_shadow_pull", "ref_dct_analyze", "ref_dct_set_symbols"]:
         getattr(lib, n).argtypes = None
     lib.ref_init_like_cli.argtypes = [C.c_void_p, C.c_float]
     lib.ref_loss_subset.restype = C.c_double
@@ -352,6 +352,27 @@ class RefSession:
         code = np.zeros(n, np.uint8)
         self.lib.ref_dct_state(C.c_void_p(self.h), None, code.ctypes.data_as(C.POINTER(C.c_uint8)), None, None, None, None, None, None, None)
         return code
+
+    def dct_full_state(self):
+        """The session's DCT level after dct_probe_codes: (symbols int16 [block][channel][64], codes uint8, steps int32)."""
+        nbc = (self.spec.W // 8) * (self.spec.H // 8) * self.spec.levels[0].C
+        sym = np.zeros(nbc * 64, np.int16)
+        code = np.zeros(nbc, np.uint8)
+        step = np.zeros(self.spec.levels[0].C * 16 * 64, np.int32)
+        self.lib.ref_dct_state(C.c_void_p(self.h), sym.ctypes.data_as(C.POINTER(C.c_int16)), code.ctypes.data_as(C.POINTER(C.c_uint8)),
+                               step.ctypes.data_as(_ip), None, None, None, None, None, None)
+        return sym, code, step
+
+    def dct_set_symbols(self, sym, code):
+        sym = np.ascontiguousarray(sym, np.int16)
+        code = np.ascontiguousarray(code, np.uint8)
+        self.lib.ref_dct_set_symbols(C.c_void_p(self.h), sym.ctypes.data_as(C.POINTER(C.c_int16)), code.ctypes.data_as(C.POINTER(C.c_uint8)))
+
+    def dct_analyze(self):
+        """dct_analyze as the progress print runs it: (raw, h0, ctx, header) bits."""
+        out = np.zeros(4, np.float64)
+        self.lib.ref_dct_analyze(C.c_void_p(self.h), out.ctypes.data_as(_dp))
+        return tuple(float(v) for v in out)
 
     BITRATE_FIELDS = ("bpp_fp32", "bpp_q8", "bpp_q8_ent", "bpp_q8_ctx", "bpp_ctx_level0", "bpp_est", "bits_mlp",
                       "bits_raw_latent", "bits_header")

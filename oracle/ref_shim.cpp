@@ -343,6 +343,23 @@ void ref_dct_state(void* h, int16_t* sym, uint8_t* code, int* step, int32_t* bit
     if (last_nz_before) *last_nz_before = Q.last_nz_before;
     if (rate_hits) *rate_hits = Q.rate_hits;
 }
+// dct_analyze (main.cpp:1080) of the session's DCT level as the progress print runs it (g_ctx_stats off):
+// out = {raw_total, h0_total, ctx_total, header}.
+void ref_dct_analyze(void* h, double* out) {
+    auto* s = static_cast<RefSession*>(h);
+    const bool keep = g_ctx_stats;
+    g_ctx_stats = false;
+    const DctStats S = dct_analyze(s->D.dct);
+    g_ctx_stats = keep;
+    out[0] = S.raw_total; out[1] = S.h0_total; out[2] = S.ctx_total; out[3] = S.header;
+}
+// Replaces the session's DCT symbols and scale codes (sizes as ref_dct_state's).
+void ref_dct_set_symbols(void* h, const int16_t* sym, const uint8_t* code) {
+    auto* s = static_cast<RefSession*>(h);
+    DctLevel& Q = s->D.dct;
+    std::copy(sym, sym + Q.sym.size(), Q.sym.begin());
+    std::copy(code, code + Q.code.size(), Q.code.begin());
+}
 // The --dct-shadow-pull step on the host (main.cpp:4139-4146).
 void ref_dct_shadow_pull(void* h, float f) {
     auto* s = static_cast<RefSession*>(h);

@@ -124,3 +124,40 @@ def test_print_stats_rejects_bad_depth(cuda_device):
     with pytest.raises(ValueError):
         tr.print_stats([0])
     tr.close()
+
+
+@pytest.mark.parametrize("C", [1, 2])
+def test_print_stats_dct_bit_simulator(C, cuda_device):
+    """A live DCT-coded level 0: the device's token statistics and entropy sums against the reference's own bit
+    simulator (dct_analyze, main.cpp:1080, g_ctx_stats off as in the progress print) on the same symbols and codes:
+    raw bits and header exact, order-0 and context bits within 1e-9 (the same code lengths summed per symbol
+    instead of per token); the progress figures against the reference's bitrate_stats on that state."""
+    if not refcpu_available():
+        pytest.skip("reference CPU library not built")
+    from neural_block_textures_b200.model import LevelSpec, ModelSpec
+    spec = ModelSpec(64, 64, [LevelSpec(64, 64, C, True), LevelSpec(16, 16, 2)], dct_q=(50,) * C, max_pairs=16,
+                     max_batch=256, seed=23 + C)
+    tgt = target_for(spec)
+    z, p = spec.init_params()
+    ref = RefSession(spec, tgt)
+    ref.set_model(z, p)
+    ref.dct_probe_codes(spec.dct_q)          # the reference fits the scale codes, goes live and snaps
+    sym, code, step = ref.dct_full_state()
+    assert np.count_nonzero(sym) > 0
+    nbc = code.size
+    d = abi.DctDesc()
+    d.live, d.C, d.BW, d.BH, d.N, d.dc_step = 1, C, spec.W // 8, spec.H // 8, 8, 4
+    with Trainer() as tr:
+        ok, why = tr.init(spec.model_desc(), z, p, tgt)
+        assert ok, why
+        tr.set_dct(d, code, sym, step)
+        st, _ = tr.print_stats([8] * len(spec.levels))
+        dsym, dcode = tr.download_dct(nbc)
+    assert st.level0_dct == 1
+    ref.dct_set_symbols(dsym, dcode)
+    raw, h0, ctx, hdr = ref.dct_analyze()
+    assert st.dct_bits_raw == raw and st.dct_bits_header == hdr == 96.0 * C
+    assert abs(st.dct_bits_h0 - h0) <= 1e-9 * h0 and abs(st.dct_bits_ctx - ctx) <= 1e-9 * ctx
+    want, _ = ref.bitrate_stats(8)
+    for k in ("bpp_q8", "bpp_q8_ent", "bpp_q8_ctx", "bpp_ctx_level0", "bpp_est", "bits_header"):
+        assert abs(getattr(st, k) - want[k]) <= 1e-9 * max(abs(want[k]), 1e-300), (k, getattr(st, k), want[k])
