@@ -121,6 +121,45 @@ def test_native_iteration_one_rank_matches_plain_steps(cuda_device):
     assert np.array_equal(pp, p1) and np.array_equal(zz, z1)
 
 
+def test_native_iteration_one_rank_other_exchanges(cuda_device):
+    """The other exchange forms on a one-rank communicator, against the plain steps: the fitness-only MLP exchange
+    (64 pairs, below the segment-block threshold) and the pixel-row latent exchange (two ES-trained levels), plus
+    an FD iteration; both peer-exchange-free paths must reproduce the plain steps bit for bit."""
+    from neural_block_textures_b200 import Trainer
+    from neural_block_textures_b200.model import LevelSpec, ModelSpec
+    from neural_block_textures_b200.trainer import Comm
+    spec = ModelSpec(64, 64, [LevelSpec(32, 32, 4), LevelSpec(16, 16, 2)], max_pairs=64, max_batch=M, seed=22)
+    tgt = _target(spec)
+    n = 64
+
+    def run(native):
+        z, p = spec.init_params()
+        with Trainer() as tr:
+            ok, why = tr.init(spec.model_desc(), z, p, tgt)
+            assert ok, why
+            if native:
+                ok, mx, lx, why = tr.shard_iteration_plan(1, 0, 1, n, M, K, False)
+                assert ok and (mx, lx) == (2, 2), (mx, lx, why)
+                for it in range(1, ITERS + 1):
+                    tr.shard_iteration(comm, it, 1, 0.02, 0.005, n, M, K, 0.05, 0.02, False)
+                tr.shard_iteration(comm, ITERS + 1, 2, 1e-3, 0.005, n, M, K, 0.05, 0.02, False)
+            else:
+                for it in range(1, ITERS + 1):
+                    tr.mlp_step(it, 0.02, 0.005, n, M)
+                    tr.lat_step(it, 0.05, 0.02, K)
+                tr.mlp_step_fd(ITERS + 1, 1e-3, 0.005, M)
+                tr.lat_step(ITERS + 1, 0.05, 0.02, K)
+            return tr.download_model()
+
+    comm = Comm(Comm.unique_id(), 1, 0)
+    try:
+        z1, p1 = run(False)
+        zn, pn = run(True)
+    finally:
+        comm.close()
+    assert np.array_equal(pn, p1) and np.array_equal(zn, z1)
+
+
 def test_native_iteration_plan_refusals(cuda_device):
     """The plan names the exchange per phase and refuses ranks that cannot split the work evenly."""
     from neural_block_textures_b200 import Trainer
