@@ -69,7 +69,6 @@ void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, fl
                          float lr, float c1, float c2);
 void launch_fd_grad_adam(cudaStream_t s, const double* dl, const double* hh, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2);
-void launch_adam(cudaStream_t s, float* theta, const float* g, float* m, float* v, long long n, float lr, float c1, float c2);
 void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* z, float* img);
 // DCT sensitivity probe (codes [BW * BH][C], gains optional) of the MLP w on the decode buffer z.
 void launch_dct_probe(cudaStream_t s, const DevModel& m, const float* w, const float* z, int BW, int BH, int C, uint8_t* code, float* gain);

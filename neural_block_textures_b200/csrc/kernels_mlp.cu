@@ -391,20 +391,6 @@ void launch_fd_grad_adam(cudaStream_t s, const double* dl, const double* hh, int
     NTCB_CHECK(cudaGetLastError());
 }
 
-__global__ void k_adam(float* __restrict__ theta, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
-                       long long n, float lr, float c1, float c2) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    float th = theta[i], mm = m[i], vv = v[i];
-    adam_update(th, g[i], mm, vv, lr, c1, c2);
-    theta[i] = th; m[i] = mm; v[i] = vv;
-}
-void launch_adam(cudaStream_t s, float* theta, const float* g, float* m, float* v, long long n, float lr, float c1, float c2) {
-    if (n <= 0) return;
-    k_adam<<<blocks_for(n, 256), 256, 0, s>>>(theta, g, m, v, n, lr, c1, c2);
-    NTCB_CHECK(cudaGetLastError());
-}
-
 // ------------------------------------------------------------------ full-image decode
 // Decoder::decode_full (main.cpp:1712-1718): every pixel's features and MLP outputs, interleaved.
 template <class S, int TPB, int R>
