@@ -53,3 +53,42 @@ def test_final_psnr_matches_reference(name, tmp_path, cuda_device):
     if (REF / "ntc_ref").exists():
         p_ref = _run(REF / "ntc_ref", [*common, "--cuda", "--out", str(tmp_path / "ref")])
         assert abs(p_new - p_ref) <= PSNR_TOL, f"reference cuda backend {p_ref} dB, b200 backend {p_new} dB"
+
+
+CONTAINER_FLAGS = ("--latent 128 128 1 --latent2 32 32 2 --filter nearest,bilinear --qat 2 --mlp-pairs 64 --write-ntcb "
+                   "--seed 2 --rng hash --print-every 1000000 --cuda")
+
+
+@pytest.mark.parametrize("iters", [0, 3])
+def test_written_files_match_reference_backend(iters, tmp_path, cuda_device):
+    """The reference trainer (main.cpp) writing its --write-ntcb container (and, after training, model.bin) with this
+    backend and with the reference's own CUDA backend, same seed and --rng hash, this backend on its exact kernels
+    (NTCB_POP_KERNEL=ffma): the containers (8-bit latent levels, fp16 weights) are identical byte for byte; model.bin
+    (the fp32 latent) has the same header and agrees to 1e-5 of the values' range (the latent ES pass and its
+    footprint sums are pinned to tolerances, not to the reference's bit pattern)."""
+    import os
+    for b in ("ntc_new", "ntc_ref"):
+        if not (REF / b).exists():
+            pytest.skip(f"oracle/_ref/{b} not built (needs the reference tree)")
+    synth.write_png(tmp_path / "in.png", synth.synth_rgb8(128, 128, 7))
+    args = [str(tmp_path / "in.png"), *CONTAINER_FLAGS.split(), "--iters", str(iters)]
+    env = dict(os.environ, NTCB_POP_KERNEL="ffma")
+    for b in ("ntc_new", "ntc_ref"):
+        r = subprocess.run([str(REF / b), *args, "--out", str(tmp_path / b)], capture_output=True, text=True, timeout=600, env=env)
+        assert r.returncode == 0, (r.stdout + r.stderr)[-3000:]
+    a = (tmp_path / "ntc_new" / "model.ntcb").read_bytes()
+    b = (tmp_path / "ntc_ref" / "model.ntcb").read_bytes()
+    assert a == b, f"model.ntcb: {len(a)} vs {len(b)} bytes, {sum(x != y for x, y in zip(a, b))} differ"
+    mb = tmp_path / "ntc_ref" / "model.bin"
+    assert (tmp_path / "ntc_new" / "model.bin").exists() == mb.exists()
+    if mb.exists():
+        import numpy as np
+        a = (tmp_path / "ntc_new" / "model.bin").read_bytes()
+        b = mb.read_bytes()
+        assert len(a) == len(b)
+        nfl = (128 * 128 * 1 + 32 * 32 * 2) + 819          # latent floats + MLP weights at the end of the file
+        hdr = len(b) - 4 * nfl
+        assert a[:hdr] == b[:hdr]
+        fa = np.frombuffer(a[hdr:], np.float32).astype(np.float64)
+        fb = np.frombuffer(b[hdr:], np.float32).astype(np.float64)
+        assert np.abs(fa - fb).max() <= 1e-5 * np.abs(fb).max()
