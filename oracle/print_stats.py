@@ -2,7 +2,8 @@
 
 A numpy restatement of the reference trainer's progress-print statistics (main.cpp:4155-4205), the checker of
 ntcb_print_stats: bitrate_stats in its progress-print form (main.cpp:2272-2352, g_ctx_stats off), mse_of
-(main.cpp:1764-1788), latent_stats (main.cpp:2212-2217) and the --qat off-grid count (main.cpp:4196-4200).
+(main.cpp:1764-1788), latent_stats (main.cpp:2212-2217), the --qat off-grid count (main.cpp:4196-4200) and the
+totals of the DCT bit simulator (dct_analyze, main.cpp:1080-1175) that bitrate_stats charges a live DCT level 0.
 The quantizers follow the reference's strict-FP forms (main.cpp:446-482): every float32 operation is one
 IEEE operation here (numpy float32 arithmetic does not contract), and lround is computed in float64, where
 |x| + 0.5 is exact for a float32 x. Pinned against the reference's own functions through
@@ -153,3 +154,51 @@ def qat_off_grid(spec, z: np.ndarray, grid: np.ndarray) -> int:
     for c, b in enumerate(spec.qat_bits):
         n += int(np.sum(grid[b, qat_index(z0[:, c], b)] != z0[:, c]))
     return n
+
+
+def dct_bits(sym: np.ndarray, code: np.ndarray, C: int, BW: int, BH: int, dc_step: int, zigzag: np.ndarray):
+    """dct_analyze's (raw, h0, ctx, header) bit totals as the progress print runs it (main.cpp:1080-1175, g_ctx_stats
+    off: the code plane's order-0 figure stands in for its context figure). sym: int16 [block][channel][64] in
+    natural order, code: uint8 [block][channel], zigzag[p] = the natural index of zigzag position p. Per channel:
+    the DC residual against the left block (the upper one in the first column, 0 first), the ACs as (run, |q|)
+    tokens in zigzag order with the zigzag position of the previous nonzero as context, an EOB unless the last
+    nonzero is at 63; each token charged -log2(count / total) of its symbol (summed here as count x code length)."""
+    nb = BW * BH
+    sym = np.asarray(sym, np.int64).reshape(nb, C, 64)
+    cl0 = lambda c, t: -math.log2(c / t) if c and t else 0.0
+    ent = lambda h, t: sum(float(v) * cl0(float(v), float(t)) for v in h if v)
+    dc_raw_bits = 0
+    while (1 << dc_raw_bits) < 512 // dc_step + 1:
+        dc_raw_bits += 1
+    raw = h0 = ctx = header = 0.0
+    for c in range(C):
+        run = np.zeros(65, np.int64); mag = np.zeros(257, np.int64)
+        cr = np.zeros((64, 65), np.int64); cm = np.zeros((64, 257), np.int64)
+        dcr = np.zeros(4097, np.int64); chist = np.zeros(16, np.int64)
+        nrun = neob = 0
+        for b in range(nb):
+            s = sym[b, c]
+            bx, by = b % BW, b // BW
+            pred = sym[b - 1, c, 0] if bx > 0 else (sym[b - BW, c, 0] if by > 0 else 0)
+            dcr[max(0, min(4096, int(s[0]) - int(pred) + 2048))] += 1
+            chist[min(int(code[b * C + c]), 15)] += 1
+            r = prev = lnz = 0
+            for p in range(1, 64):
+                q = int(s[zigzag[p]])
+                if q == 0:
+                    r += 1
+                    continue
+                m = min(256, abs(q))
+                run[r] += 1; mag[m] += 1; cr[prev, r] += 1; cm[prev, m] += 1
+                nrun += 1; lnz = p; prev = p; r = 0
+            if lnz < 63:
+                run[64] += 1; cr[prev, 64] += 1; neob += 1
+        dc, cd = ent(dcr, nb), ent(chist, nb)
+        run0, mag0 = ent(run, nrun + neob), ent(mag, nrun)
+        runc = sum(ent(cr[k], cr[k].sum()) for k in range(64))
+        magc = sum(ent(cm[k], cm[k].sum()) for k in range(64))
+        raw += nb * dc_raw_bits + 16 * nrun + 7 * neob + 4 * nb + 96
+        h0 += dc + run0 + mag0 + nrun + cd + 96
+        ctx += dc + runc + magc + nrun + cd + 96
+        header += 96
+    return raw, h0, ctx, header

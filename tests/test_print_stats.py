@@ -148,3 +148,24 @@ def test_quantizer_functions_vs_reference():
             lib.ref_qat_levels_index(C.c_float(x), b, C.byref(k))
             want.append(k.value)
         assert np.array_equal(ps.qat_index(vv, b), want), b
+
+
+@pytest.mark.parametrize("C", [1, 2])
+def test_dct_bit_simulator_oracle_vs_reference(C):
+    """The oracle's restatement of the DCT bit simulator against the reference's own dct_analyze (through the
+    reference CPU library) on a live DCT level fitted by the reference: raw and header bits exact, the entropy
+    totals to 1e-12 (code lengths summed per symbol instead of per token)."""
+    from neural_block_textures_b200 import dct
+    spec = ModelSpec(64, 64, [LevelSpec(64, 64, C, True), LevelSpec(16, 16, 2)], dct_q=(50,) * C, max_pairs=16,
+                     max_batch=256, seed=23 + C)
+    tgt = target_for(spec)
+    z, p = spec.init_params()
+    ref = RefSession(spec, tgt)
+    ref.set_model(z, p)
+    ref.dct_probe_codes(spec.dct_q)
+    sym, code, _ = ref.dct_full_state()
+    assert np.count_nonzero(sym) > 0
+    raw, h0, ctx, hdr = ps.dct_bits(sym, code, C, spec.W // 8, spec.H // 8, 4, dct.zigzag_table())
+    rraw, rh0, rctx, rhdr = ref.dct_analyze()
+    assert raw == rraw and hdr == rhdr
+    assert abs(h0 - rh0) <= 1e-12 * rh0 and abs(ctx - rctx) <= 1e-12 * rctx
