@@ -7,11 +7,13 @@ level 0 = 512x512x1 2-bit --qat selector plane, level 1 = 128x128x2 bilinear, 24
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
 
---impl ours (default): the CUDA backend. N > 1 (torchrun, one process per GPU): the ES population is sharded
-over the ranks (each evaluates its pairs, regenerating their noise from the counter); one NCCL all-gather of
-the per-pair fitness (2 doubles per pair) feeds the identical gradient + Adam on every rank; the latent step is
-sharded by image rows (all-gather of the per-pixel loss differences) and the selector search by level-0 texel
-rows (all-gather of level 0), with identical gathers / Adam / snap on every rank (neural_block_textures_b200/shard.py).
+--impl ours (default): the CUDA backend. N > 1 (torchrun, one process per GPU): one ntcb_shard_iteration call per
+iteration (neural_block_textures_b200.shard.NativeShardedES): the ES population is sharded over the ranks (each
+evaluates its pairs, regenerating their noise from the counter, and sums its own ES-gradient segments), the latent
+step by texel rows and the selector search by level-0 rows, and each of the three exchanges per iteration is the
+library's peer-memory kernel over CUDA IPC mappings (--exchange nccl: NCCL all-gathers on the library's own
+communicator; --shard-driver python: the per-phase entry points around torch.distributed all-gathers). Every rank
+ends each iteration bit-identical to one GPU.
 --impl reference: the reference's own CPU trainer (main.cpp compiled from source, OpenMP on every host
 thread) timed on a bounded sample of the same iteration (rank 0 only).
 """
