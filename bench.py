@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--fd-steps", type=int, default=100, help="FD-phase iterations timed after the ES ones (0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-cuda", action="store_true", help="skip timing the reference's own CUDA backend (oracle/_ref/ntc_ref)")
+    ap.add_argument("--no-cfg5", action="store_true", help="skip the config-5 (population 32768) leg")
     ap.add_argument("--shard-driver", default="native", choices=["native", "python"],
                     help="N > 1: one library call per iteration with in-place NCCL all-gathers on the library's own communicator "
                          "(native), or the per-phase entry points around torch.distributed all-gathers (python)")
@@ -277,21 +278,25 @@ def ntcb_decode_leg(reps=20):
     return line
 
 
-def tf32_peak_tflops(n=8192, reps=20):
-    """cuBLAS TF32 GEMM throughput on this GPU (the denominator for the tensor-core population kernel)."""
+def tf32_peak_tflops(n=8192, reps=20, rounds=5):
+    """cuBLAS TF32 GEMM throughput on this GPU: the best of `rounds` timings of `reps` back-to-back GEMMs (the tensor
+    pipe the population kernel runs on; a secondary denominator beside the measured bf16 peak)."""
     import torch
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True
     a = torch.randn(n, n, device="cuda"); b = torch.randn(n, n, device="cuda"); c = torch.empty(n, n, device="cuda")
     for _ in range(3):
         torch.matmul(a, b, out=c)
-    e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        torch.matmul(a, b, out=c)
-    e1.record(); e1.synchronize()
+    best = 0.0
+    for _ in range(rounds):
+        e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            torch.matmul(a, b, out=c)
+        e1.record(); e1.synchronize()
+        best = max(best, 2.0 * n ** 3 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12)
     torch.backends.cuda.matmul.allow_tf32 = prev
-    return 2.0 * n ** 3 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+    return best
 
 
 def tc_issued_flops_per_decode(spec) -> int:
@@ -304,26 +309,30 @@ def tc_issued_flops_per_decode(spec) -> int:
 
 
 def pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks):
+    """The population kernel against the measured peaks. Primary: the driver-measured dense bf16 tensor peak of
+    MEASURED_PEAKS.json (burst: the kernel is timed alone per launch). Secondary: the TF32 tensor pipe the kernel runs
+    on (cuBLAS measured here) and the FP32 FFMA pipe (measured by the library)."""
     base = {"kernel": "k_pop_eval_tc (tcgen05 3xTF32)" if kernel == "tensor" else "k_pop_eval_x2 (packed FP32)",
             "achieved": achieved, "unit": "TFLOP/s", "traffic": traffic, "flops_per_launch": eval_flops,
             "avg_launch_ms": eval_avg_s * 1e3, "fp32_ffma_peak": ffma,
             "frac_of_fp32_ffma_peak": (achieved / ffma) if achieved else None}
+    if "bf16_tflops" in peaks:
+        base.update({"bound": "tensor", "peak": peaks["bf16_tflops"], "frac": (achieved / peaks["bf16_tflops"]) if achieved else None,
+                     "peak_source": "of measured: MEASURED_PEAKS.json bf16_tflops (dense bf16 cuBLAS burst on this pool's B200s)"})
+    else:
+        base.update({"bound": "tensor", "peak": 1590.0, "frac": (achieved / 1590.0) if achieved else None,
+                     "peak_source": "of fallback: 1.59 PFLOP/s dense bf16 (MEASURED_PEAKS.json absent)"})
     if kernel == "tensor" and achieved and tf32:
         issued = achieved * tc_issued_flops_per_decode(cfg.spec) / cfg.flops_per_decode()
-        base.update({"bound": "tensor", "peak": tf32, "frac": achieved / tf32,
-                     "peak_source": "cuBLAS TF32 GEMM (8192^3) measured in bench.py on this GPU",
+        base.update({"tf32_peak": tf32, "frac_of_tf32_peak": achieved / tf32,
+                     "tf32_peak_source": "cuBLAS TF32 GEMM (8192^3), best of 5 x 20 launches in bench.py on this GPU",
                      "issued_tensor_tflops": issued, "issued_frac_of_tf32_peak": issued / tf32,
                      "note": "achieved counts algorithmic FLOPs (2 sum n_in n_out per decode); the kernel issues "
                              f"{tc_issued_flops_per_decode(cfg.spec)} tensor FLOPs per decode (3xTF32, padded K/N)"})
-    else:
-        base.update({"bound": "fp32", "peak": ffma, "frac": (achieved / ffma) if achieved else None,
-                     "peak_source": "FP32 FFMA throughput measured on this GPU by ntcb_fp32_peak_tflops"})
-    if achieved and "bf16_tflops" in peaks:
-        base["frac_of_measured_bf16_tensor"] = achieved / peaks["bf16_tflops"]
     return base
 
 
-def ref_cuda_leg(cfg, n1=20, span_s=6.0):
+def ref_cuda_leg(cfg, n1=20, span_s=24.0):
     """The reference's own CUDA backend (cuda/ntc_cuda.cu built unmodified for sm_100a, linked into the reference
     CLI as oracle/_ref/ntc_ref) on the same configuration and GPU. Runs of n1 and n2 ES iterations with no
     intermediate prints: the CLI reports the elapsed time (0.1 s resolution) at the last iteration before its final
@@ -379,6 +388,152 @@ def ref_cuda_leg(cfg, n1=20, span_s=6.0):
             "method": f"wall clock of the reference CLI, ({n2} - {n1}) ES iterations (0.1 s print resolution), same synthetic input"}
 
 
+class Arm:
+    """One configuration set up on this rank: the trainer on its own stream and, for N > 1, the sharded driver."""
+
+    def __init__(self, cfg, args, world, rank, dist):
+        import torch
+        from neural_block_textures_b200 import Trainer
+        from neural_block_textures_b200.shard import ShardedES, NativeShardedES, pair_range
+        self.cfg, self.dist = cfg, dist
+        spec = cfg.spec
+        self.z0, self.p0 = spec.init_params()
+        self.tr = Trainer()
+        ok, why = self.tr.init(spec.model_desc(), self.z0, self.p0, cfg.target())
+        if not ok:
+            raise SystemExit(f"init failed: {why}")
+        self.stream = torch.cuda.Stream()
+        self.tr.set_stream(self.stream.cuda_stream)
+        self.tr.set_pop_kernel(args.pop_kernel == "tensor")
+        self.N, self.M, K = cfg.pairs, cfg.batch, cfg.lat_pairs
+        p0, p1 = pair_range(self.N, world, rank)
+        self.per = p1 - p0
+        self.has_lat = len(spec.levels) > 1 or not spec.qat_bits
+        self.qat = bool(spec.qat_bits)
+        self.K = K
+        self.Kl = K if self.has_lat else 0
+        self.sharded = self.native = None
+        L0 = spec.levels[0]
+        if world > 1 and args.shard_driver == "native":
+            self.native = NativeShardedES(self.tr, dist, device="cuda",
+                                          p2p=(self.N, self.Kl, self.qat) if args.exchange == "p2p" else None)
+            for mode in (1, 2):
+                ok, _, _, why = self.native.plan(mode, self.N, self.M, self.Kl, self.qat)
+                if not ok:
+                    raise SystemExit(f"native sharded iteration does not apply: {why}")
+        elif world > 1:
+            self.sharded = ShardedES(self.tr, dist, self.N, device="cuda", stream=self.stream, K=self.Kl, image=(spec.W, spec.H),
+                                     level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None, P=spec.P)
+
+    def exchange(self) -> str:
+        if self.native is None and self.sharded is None:
+            return "none"
+        if self.sharded is not None:
+            return "torch.distributed NCCL all-gathers"
+        return "peer-memory exchange kernel (CUDA IPC, NVLink)" if self.native.p2p else "NCCL in-place all-gathers"
+
+    def step(self, it):
+        c, tr = self.cfg, self.tr
+        if self.native is not None:
+            self.native.iteration(it, 1, c.mlp_sigma, c.mlp_lr, self.N, self.M, self.Kl, c.lat_sigma, c.lat_lr, self.qat)
+        elif self.sharded is None:
+            tr.mlp_step(it, c.mlp_sigma, c.mlp_lr, self.N, self.M)
+            if self.has_lat:
+                tr.lat_step(it, c.lat_sigma, c.lat_lr, self.K)
+            if self.qat:
+                tr.qat_search()
+        else:
+            self.sharded.step(it, c.mlp_sigma, c.mlp_lr, self.M)
+            if self.has_lat:
+                self.sharded.lat_step(it, c.lat_sigma, c.lat_lr, self.K)
+            if self.qat:
+                self.sharded.qat_search()
+
+    def fd_step(self, it):
+        c, tr = self.cfg, self.tr
+        if self.native is not None:
+            self.native.iteration(it, 2, c.fd_h, c.mlp_lr, self.N, self.M, self.Kl, c.lat_sigma, c.lat_lr, self.qat)
+        elif self.sharded is None:
+            tr.mlp_step_fd(it, c.fd_h, c.mlp_lr, self.M)
+            if self.has_lat:
+                tr.lat_step(it, c.lat_sigma, c.lat_lr, self.K)
+            if self.qat:
+                tr.qat_search()
+        else:
+            self.sharded.fd_step(it, c.fd_h, c.mlp_lr, self.M)
+            if self.has_lat:
+                self.sharded.lat_step(it, c.lat_sigma, c.lat_lr, self.K)
+            if self.qat:
+                self.sharded.qat_search()
+
+    def close(self):
+        if self.native is not None:
+            self.native.close()
+            self.native = None
+        self.tr.close()
+
+
+def start_together(stream, dist):
+    """Drain this rank's work, then line the ranks up: after this, every rank's next launch starts within host
+    jitter of the others', so no rank's first timed step absorbs a peer's late start."""
+    import torch
+    stream.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def max_over_ranks(vals, dist):
+    """Element-wise max over ranks of a list of floats (device-side all-reduce, identical steps on every rank)."""
+    if not dist:
+        return list(vals)
+    import torch
+    t = torch.tensor(list(vals), dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.cpu()]
+
+
+def timed_steps(arm, step_fn, it, steps, flush, dist):
+    """`steps` iterations, each bracketed by CUDA events on the trainer's stream, the L2 flushed before each outside
+    the events. Returns (per-step ms of this rank, next iteration number)."""
+    import torch
+    evs = []
+    for _ in range(steps):
+        with torch.cuda.stream(arm.stream):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(arm.stream)
+        step_fn(it); it += 1
+        with torch.cuda.stream(arm.stream):
+            e1.record(arm.stream)
+        evs.append((e0, e1))
+    arm.stream.synchronize()
+    return [a.elapsed_time(b) for a, b in evs], it
+
+
+def cfg5_leg(args, world, rank, dist, flush):
+    """The north star's scaling configuration (config 5: 2048^2, population 32768) on the same N GPUs, same timing
+    rules as the headline (warm-up, ranks lined up, L2 flushed between steps, CUDA events, max over ranks)."""
+    from neural_block_textures_b200 import model
+    cfg = model.config(5)
+    arm = Arm(cfg, args, world, rank, dist)
+    it = 1
+    for _ in range(args.warmup):
+        arm.step(it); it += 1
+    start_together(arm.stream, dist)
+    per, it = timed_steps(arm, arm.step, it, args.steps, flush, dist)
+    tot, med = max_over_ranks([sum(per), statistics.median(per)], dist)
+    dec = sum(cfg.decodes_per_iter().values())
+    out = {"workload": cfg.name, "cli": cfg.cli, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": tot / args.steps, "ms_per_step_median": med, "value": dec * args.steps / (tot * 1e-3),
+           "unit": "decodes/s", "decodes_per_step": cfg.decodes_per_iter(), "exchange": arm.exchange(),
+           "scaling": "strong", "l2": "flushed between steps (256 MiB memset outside the timed events)",
+           "note": "efficiency at N = value(N) / (N value(1)) over the cfg5 objects of the per-N lines"}
+    arm.close()
+    return out
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
@@ -392,113 +547,43 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    from neural_block_textures_b200 import Trainer, load_library, model
+    from neural_block_textures_b200 import load_library, model
 
     cfg = model.config(args.config)
     spec = cfg.spec
-    target = cfg.target()
-    z0, p0 = spec.init_params()
-    tr = Trainer()
-    ok, why = tr.init(spec.model_desc(), z0, p0, target)
-    if not ok:
-        raise SystemExit(f"init failed: {why}")
-    stream = torch.cuda.Stream()
-    tr.set_stream(stream.cuda_stream)
-    tr.set_pop_kernel(args.pop_kernel == "tensor")
-    N, M, K = cfg.pairs, cfg.batch, cfg.lat_pairs
-    from neural_block_textures_b200.shard import ShardedES, pair_range
-    per = pair_range(N, world, rank)[1] - pair_range(N, world, rank)[0]
-    L0 = spec.levels[0]
-    has_lat = len(spec.levels) > 1 or not spec.qat_bits
-    sharded = native = None
-    qat = bool(spec.qat_bits)
-    Kl = K if has_lat else 0
-    if world > 1 and args.shard_driver == "native":
-        from neural_block_textures_b200.shard import NativeShardedES
-        native = NativeShardedES(tr, dist, device="cuda", p2p=(N, Kl, qat) if args.exchange == "p2p" else None)
-        for mode in (1, 2):
-            ok, _, _, why = native.plan(mode, N, M, Kl, qat)
-            if not ok:
-                raise SystemExit(f"native sharded iteration does not apply: {why}")
-    elif world > 1:
-        sharded = ShardedES(tr, dist, N, device="cuda", stream=stream, K=Kl, image=(spec.W, spec.H),
-                            level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None, P=spec.P)
+    arm = Arm(cfg, args, world, rank, dist)
+    tr, stream = arm.tr, arm.stream
+    N, M = arm.N, arm.M
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     dec = cfg.decodes_per_iter()
     decodes = sum(dec.values())
-
-    def step(it):
-        if native is not None:
-            native.iteration(it, 1, cfg.mlp_sigma, cfg.mlp_lr, N, M, Kl, cfg.lat_sigma, cfg.lat_lr, qat)
-        elif sharded is None:
-            tr.mlp_step(it, cfg.mlp_sigma, cfg.mlp_lr, N, M)
-            if has_lat:
-                tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
-            if spec.qat_bits:
-                tr.qat_search()
-        else:
-            sharded.step(it, cfg.mlp_sigma, cfg.mlp_lr, M)
-            if has_lat:
-                sharded.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
-            if spec.qat_bits:
-                sharded.qat_search()
-
-    def fd_step(it):
-        if native is not None:
-            native.iteration(it, 2, cfg.fd_h, cfg.mlp_lr, N, M, Kl, cfg.lat_sigma, cfg.lat_lr, qat)
-        elif sharded is None:
-            tr.mlp_step_fd(it, cfg.fd_h, cfg.mlp_lr, M)
-            if has_lat:
-                tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
-            if spec.qat_bits:
-                tr.qat_search()
-        else:
-            sharded.fd_step(it, cfg.fd_h, cfg.mlp_lr, M)
-            if has_lat:
-                sharded.lat_step(it, cfg.lat_sigma, cfg.lat_lr, K)
-            if spec.qat_bits:
-                sharded.qat_search()
+    step, fd_step = arm.step, arm.fd_step
 
     it = 1
     for _ in range(args.warmup):
         step(it); it += 1
-    stream.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
+    start_together(stream, dist)
     # Inside the timed region only the population kernel carries CUDA events (the roofline's launch time): events
     # around every launch cost host calls that, on several GPUs, can outlast the device work of a step.
     tr.kernel_timing(True)
     tr.kernel_timing_only("mlp_eval")
     launches0 = tr.launch_count()
-    evs = []
     with ClockSampler(local) as clk:
         time.sleep(0.6)            # nvidia-smi's first sample lands before the timed steps start
-        for _ in range(args.steps):
-            with torch.cuda.stream(stream):
-                flush.zero_()          # L2 flush between steps, outside the timed events
-                e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            step(it); it += 1
-            with torch.cuda.stream(stream):
-                e1.record(stream)
-            evs.append((e0, e1))
-        stream.synchronize()
+        start_together(stream, dist)
+        per_step, it = timed_steps(arm, step, it, args.steps, flush, dist)
     torch.cuda.synchronize()
     launches = tr.launch_count() - launches0
-    ms = sum(a.elapsed_time(b) for a, b in evs)
     eval_ms, eval_n = tr.kernel_time("mlp_eval")
     tr.kernel_timing(False)
-    if dist:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, ms_med, ms_first = max_over_ranks([sum(per_step), statistics.median(per_step), per_step[0]], dist)
 
     # ---- per-phase breakdown: a separate pass with every kernel class timed (device time of this library's
-    # kernels and, under the native sharded driver, of the NCCL all-gathers; the rest of a step is idle gaps)
+    # kernels and, under the native sharded driver, of the exchanges; the rest of a step is idle gaps)
     nb = min(args.steps, 100)
     tr.kernel_timing_only(None)
     tr.kernel_timing(True)
+    start_together(stream, dist)
     for _ in range(nb):
         with torch.cuda.stream(stream):
             flush.zero_()
@@ -518,27 +603,11 @@ def main():
     if args.fd_steps > 0:
         for _ in range(3):
             fd_step(it); it += 1
-        stream.synchronize()
-        if dist:
-            dist.barrier()
-        fevs = []
-        for _ in range(args.fd_steps):
-            with torch.cuda.stream(stream):
-                flush.zero_()
-                e0 = torch.cuda.Event(enable_timing=True); e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            fd_step(it); it += 1
-            with torch.cuda.stream(stream):
-                e1.record(stream)
-            fevs.append((e0, e1))
-        stream.synchronize()
-        fms = sum(a.elapsed_time(b) for a, b in fevs)
-        if dist:
-            t = torch.tensor([fms], dtype=torch.float64, device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            fms = float(t.item())
+        start_together(stream, dist)
+        fper, it = timed_steps(arm, fd_step, it, args.fd_steps, flush, dist)
+        fms, fmed = max_over_ranks([sum(fper), statistics.median(fper)], dist)
         fdec = cfg.decodes_per_iter(fd=True)
-        fd_line = {"steps": args.fd_steps, "ms_per_step": fms / args.fd_steps, "decodes_per_step": fdec,
+        fd_line = {"steps": args.fd_steps, "ms_per_step": fms / args.fd_steps, "ms_per_step_median": fmed, "decodes_per_step": fdec,
                    "value": sum(fdec.values()) * args.fd_steps / (fms * 1e-3), "unit": "decodes/s",
                    "kernel": ("k_pop_eval_tc (tcgen05 3xTF32)" if tr.pop_kernel() == "tensor" else "k_pop_eval_x2 (packed FP32, exact)")
                              + ": the stats pair and the 2P FD candidates in one launch"}
@@ -546,35 +615,36 @@ def main():
     # ---- end to end through the public API with host buffers (pinned), copies inside the timed region
     zh = torch.empty(spec.nz, dtype=torch.float32, pin_memory=True).numpy()
     ph = torch.empty(spec.P, dtype=torch.float32, pin_memory=True).numpy()
-    zh[:] = z0; ph[:] = p0
+    zh[:] = arm.z0; ph[:] = arm.p0
     e2e_steps = args.e2e_steps
     for _ in range(2):
         tr.upload_model(zh, ph); step(it); it += 1
         zz, pp = tr.download_model(); tr.mlp_stats()
-    if dist:
-        dist.barrier()
+    start_together(stream, dist)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         tr.upload_model(zh, ph)
         step(it); it += 1
         zz, pp = tr.download_model()
         tr.mlp_stats()
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks([time.perf_counter() - t0], dist)[0]
     e2e_value = decodes * e2e_steps / e2e_s
     h2d = 4 * (spec.nz + spec.P)
     d2h = 4 * (spec.nz + spec.P) + 16 * N
+    kernel = tr.pop_kernel()
+    pprint = progress_print_leg(tr, cfg, not args.no_cpu_baseline) if (rank == 0 and world == 1) else None
+    exchange = arm.exchange()
+    arm.close()
+
+    # ---- the north star's scaling configuration on the same GPUs (every rank takes part)
+    cfg5 = cfg5_leg(args, world, rank, dist, flush) if not args.no_cfg5 else None
 
     if rank == 0:
         lib = load_library()
         ffma = float(lib.ntcb_fp32_peak_tflops())
-        kernel = tr.pop_kernel()
         tf32 = tf32_peak_tflops() if kernel == "tensor" else None
         fpd = cfg.flops_per_decode()
-        eval_flops = 2 * per * M * fpd if world > 1 else 2 * N * M * fpd
+        eval_flops = 2 * arm.per * M * fpd if world > 1 else 2 * N * M * fpd
         eval_avg_s = (eval_ms / max(eval_n, 1)) * 1e-3
         achieved = eval_flops / eval_avg_s / 1e12 if eval_n else None
         peaks = {}
@@ -588,11 +658,10 @@ def main():
         line = {
             "metric": "candidate-pixel decodes/s (ES training iteration)", "value": value, "unit": "decodes/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "ms_per_step_median": ms_med, "ms_first_step": ms_first,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg.name, "cli": cfg.cli, "decodes_per_step": dec, "parallelism": f"population x{world}",
-                       "exchange": ("none" if world == 1 else "torch.distributed NCCL all-gathers" if sharded is not None else
-                                    "peer-memory exchange kernel (CUDA IPC, NVLink)" if native.p2p else "NCCL in-place all-gathers"),
-                       "pop_kernel": kernel,
+                       "exchange": exchange, "pop_kernel": kernel,
                        "l2": "flushed between steps (256 MiB memset outside the timed events)"},
             "roofline": pop_roofline(kernel, cfg, achieved, ffma, tf32, traffic, eval_flops, eval_avg_s, peaks),
             "phase_ms_per_step": {**breakdown, "kernels_total": sum(v for k, v in breakdown.items() if k != "exchange"),
@@ -601,20 +670,17 @@ def main():
                     "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
             "gpu_launches": launches,
             "fd_phase": fd_line,
+            "cfg5": cfg5,
             "clocks": clk.summary(),
         }
-        if world == 1:
-            line["progress_print"] = progress_print_leg(tr, cfg, not args.no_cpu_baseline)
+        if pprint is not None:
+            line["progress_print"] = pprint
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_leg(cfg)
             line["ntcb_decode"] = ntcb_decode_leg()
         if world == 1 and not args.no_ref_cuda:
-            tr.close()
             line["ref_cuda_backend"] = ref_cuda_leg(cfg)
         print(json.dumps(line))
-    if native is not None:
-        native.close()
-    tr.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

@@ -151,9 +151,10 @@ void ntcb_noise_fill(uint64_t seed, uint32_t stream, uint32_t step, uint32_t pai
  * NTCB_STATIC_SCRATCH_BYTES per GPU, held until exit. Inputs are host arrays: w (the flat MLP), feat (M rows of
  * d->nin features, the minibatch pixels' MLP inputs), tgt (M rows of d->nout targets); fit receives 2 * npairs
  * doubles (L+, L- per pair). Returns 1, or 0 with a reason in why when the sizes need more than the static
- * maximum or the model is outside the envelope. The first call on a device looks up the array's device address
- * (make it before any stream capture). Calls in one process share the array: concurrent calls race and must be
- * serialised by the caller. Synchronous on the legacy default stream. */
+ * maximum, the model is outside the envelope, a CUDA error was already pending, or a CUDA call inside it failed
+ * (it never exits the process). The first call on a device looks up the array's device address (make it before
+ * any stream capture; not valid across a cudaDeviceReset). Calls in one process share the array: concurrent calls
+ * race and must be serialised by the caller. Synchronous on the legacy default stream. */
 #define NTCB_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
 int ntcb_es_fitness_noalloc(const ntcb_model_desc* d, int it, float sigma, int pair_begin, int npairs,
                             const float* w, const float* feat, const float* tgt, int M, double* fit,
@@ -332,8 +333,9 @@ int ntcb_shard_iteration_plan(const ntcb_trainer* t, int world, int rank, int ml
 void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, float mlp_sigma, float mlp_lr, int N, int M, int K,
                           float lat_sigma, float lat_lr, int qat);
 /* Peer-memory exchanges for ntcb_shard_iteration (addition): instead of NCCL, each exchange is one kernel that writes
- * this rank's block into every peer's staging buffer over NVLink, signals each peer with a system-scope flag, waits
- * (bounded, a few seconds) for every peer's signal and copies the staged blocks into place. Set-up: every rank calls
+ * this rank's block into every peer's staging buffer over NVLink as 16-byte lines that carry the exchange's epoch
+ * beside the data (no separate flag or fence), waits (bounded, a few seconds) until every peer's lines carry the
+ * epoch and copies the staged words into place. Set-up: every rank calls
  * ntcb_p2p_export for the (world, N, K, qat) it will iterate with, which allocates its exchange buffer and writes the
  * buffer's CUDA IPC handle (NTCB_P2P_HANDLE_BYTES bytes); the caller gathers the handles of all ranks in rank order
  * (any host channel) and every rank calls ntcb_p2p_import. Both return 0 with a reason on failure (then the
@@ -345,6 +347,18 @@ int ntcb_p2p_import(ntcb_trainer* t, const unsigned char* handles, int world, in
 /* Unmaps the peers' exchange buffers after this rank's stream has drained (the iteration falls back to NCCL). Call it
  * on every rank, then a barrier, before any rank destroys its trainer: a buffer is freed only when no peer maps it. */
 void ntcb_p2p_release(ntcb_trainer* t);
+/* Bounded-wait control of the peer exchanges (addition; the reference has no multi-GPU path and exits on any runtime
+ * failure, cuda/ntc_cuda.cu:55-56). ntcb_p2p_set_poll_limit: how many times an exchange polls one staged line of a
+ * peer before it gives up (0 restores the default, 2^22 polls: a few seconds); a wait that runs out sets the
+ * trainer's device error word to 2 and the next synchronising call prints and exits. ntcb_p2p_barrier: every rank
+ * pushes a token to every peer and waits for all peers' tokens through the same staging, with `polls` as the limit (0:
+ * the trainer's limit); it synchronises the trainer's stream and returns the device error word instead of exiting
+ * (0 = every peer arrived, 2 = a peer did not arrive in time, 1 = an earlier tensor-core wait had timed out), then
+ * clears it. Every rank must call it at the same point of its sequence of exchanges. After a non-zero return the
+ * ranks' exchange epochs disagree: release the peer exchange (ntcb_p2p_release) and set it up again before the next
+ * sharded iteration. */
+void ntcb_p2p_set_poll_limit(ntcb_trainer* t, unsigned polls);
+int ntcb_p2p_barrier(ntcb_trainer* t, unsigned polls);
 
 #ifdef __cplusplus
 }

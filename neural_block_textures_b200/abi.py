@@ -184,6 +184,8 @@ SIGNATURES = {
     "ntcb_p2p_export": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_ubyte), C.c_char_p, C.c_size_t]),
     "ntcb_p2p_import": (C.c_int, [_vp, C.POINTER(C.c_ubyte), C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
     "ntcb_p2p_release": (None, [_vp]),
+    "ntcb_p2p_set_poll_limit": (None, [_vp, C.c_uint]),
+    "ntcb_p2p_barrier": (C.c_int, [_vp, C.c_uint]),
 }
 
 COMM_ID_BYTES = 128   # NTCB_COMM_ID_BYTES

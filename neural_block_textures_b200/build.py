@@ -17,7 +17,7 @@ BUILD_DIR = PKG / "_build"
 LIB = OUT_DIR / "libntc_b200.so"
 SOURCES = ["kernels_mlp.cu", "kernels_tc.cu", "kernels_latent.cu", "kernels_snap.cu", "kernels_stats.cu", "engine.cu",
            "ntcb_format.cpp", "ntcb_decoder.cu",
-           "static_scratch.cu", "nccl_link.cpp", "p2p_exchange.cu"]
+           "static_scratch.cu", "nccl_link.cpp", "p2p_exchange.cu", "device_cache.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # No fast-math: the noise (logf / cosf / sqrtf), the sigmoid (expf) and every division must be CUDA's
 # IEEE / accurate versions for parity with the reference backend.

@@ -22,8 +22,21 @@ constexpr int kMaxCh = 16;
 constexpr int kMaxIn = 64;      // widest MLP input / hidden layer the backend accepts (as the reference's v1 envelope)
 constexpr int kMaxWidth = 64;
 
+// A failing CUDA call prints and exits the process, as the reference backend does (cuda/ntc_cuda.cu:55-56), unless the
+// calling host thread has installed a soft-error slot (SoftErrorScope): then the first failure is recorded there and
+// the call returns, so an entry point that reports errors to its caller can check the slot and return.
+extern thread_local cudaError_t* g_soft_error;
+struct SoftErrorScope {
+    cudaError_t err = cudaSuccess;
+    cudaError_t* prev;
+    SoftErrorScope() : prev(g_soft_error) { g_soft_error = &err; }
+    ~SoftErrorScope() { g_soft_error = prev; }
+    SoftErrorScope(const SoftErrorScope&) = delete;
+    SoftErrorScope& operator=(const SoftErrorScope&) = delete;
+};
 #define NTCB_CHECK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { \
-    fprintf(stderr, "ntc_b200: CUDA error %s at %s:%d: %s\n", #x, __FILE__, __LINE__, cudaGetErrorString(e_)); exit(1); } } while (0)
+    if (::ntcb::g_soft_error) { if (*::ntcb::g_soft_error == cudaSuccess) *::ntcb::g_soft_error = e_; } else { \
+    fprintf(stderr, "ntc_b200: CUDA error %s at %s:%d: %s\n", #x, __FILE__, __LINE__, cudaGetErrorString(e_)); exit(1); } } } while (0)
 
 struct DevLevel {
     int W, H, C, nearest;

@@ -87,6 +87,7 @@ struct Trainer::Impl {
     char* p2p_buf = nullptr;   // this rank's exchange buffer (flags, counters, staging)
     bool p2p_ready = false;
     uint32_t p2p_epoch = 0;
+    uint32_t p2p_poll_limit = ntcb::kP2PPollLimit;   // polls of one staged line before an exchange wait fails
     float* qat_grid = nullptr; int* qat_bits = nullptr;
     // progress-print statistics: the last set_qes description (host copy) and a device scratch buffer
     ntc_cuda::QesDesc qes_host{};
@@ -1511,6 +1512,28 @@ int ntcb_p2p_import(ntcb_trainer* t, const unsigned char* handles, int world, in
     return 1;
 }
 
+void ntcb_p2p_set_poll_limit(ntcb_trainer* t, unsigned polls) {
+    t->impl.p2p_poll_limit = polls ? polls : ntcb::kP2PPollLimit;
+}
+
+int ntcb_p2p_barrier(ntcb_trainer* t, unsigned polls) {
+    Impl& I = t->impl;
+    require_ready(I); set_device(I);
+    if (!I.p2p_ready) die("p2p_barrier: no peer exchange set up (ntcb_p2p_export / ntcb_p2p_import)");
+    // one 4-byte token per rank, all-gathered through the staging into this rank's header slots
+    char* slots = I.p2p_buf;
+    static_assert(ntcb::kP2PHeader >= 4 * ntcb::kP2PMaxRanks, "barrier token slots");
+    const uint32_t token = I.p2p_epoch + 1;
+    NTCB_CHECK(cudaMemcpyAsync(slots + 4 * (size_t)I.p2p.rank, &token, 4, cudaMemcpyHostToDevice, I.stream));
+    I.p2p_epoch++;
+    ntcb::launch_p2p_allgather(I.stream, I.p2p, slots, 4, I.p2p_epoch, polls ? polls : I.p2p_poll_limit, I.tc_err);
+    NTCB_CHECK(cudaStreamSynchronize(I.stream));
+    int e = 0;
+    NTCB_CHECK(cudaMemcpy(&e, I.tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) NTCB_CHECK(cudaMemset(I.tc_err, 0, sizeof(int)));
+    return e;
+}
+
 void ntcb_p2p_release(ntcb_trainer* t) {
     Impl& I = t->impl;
     if (!I.p2p_ready) return;
@@ -1536,7 +1559,7 @@ void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, f
             if (bytes % 4 || ntcb::p2p_stage_bytes(bytes) > I.p2p.cap)
                 die("shard_iteration: an exchange block does not fit the peer buffers set up for it");
             I.p2p_epoch++;
-            timed(I, "exchange", 1, [&] { ntcb::launch_p2p_allgather(I.stream, I.p2p, buf, bytes, I.p2p_epoch, I.tc_err); });
+            timed(I, "exchange", 1, [&] { ntcb::launch_p2p_allgather(I.stream, I.p2p, buf, bytes, I.p2p_epoch, I.p2p_poll_limit, I.tc_err); });
         } else {
             timed(I, "exchange", 0, [&] { ntcb::nccl::all_gather_inplace(c->nc, buf, bytes, r, I.stream); });
         }

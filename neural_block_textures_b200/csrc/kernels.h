@@ -17,6 +17,11 @@ namespace ntcb {
 int shape_id(const DevModel& m);
 double measure_ffma_tflops(int sms);   // FP32 FMA peak of the current device, TFLOP/s
 
+// Per-device launch set-up (device_cache.cu): the current device's SM count, and a kernel's dynamic shared-memory
+// opt-in, each made once per device ordinal (thread-safe).
+int device_sm_count();
+void ensure_dynamic_smem(const void* kernel, int bytes);
+
 // ---- MLP population (kernels_mlp.cu) ----
 struct PopArgs {
     int mode;                  // 0 = ES pairs (w0 +- sigma eps), 1 = FD (w0 with weight j at +- h)

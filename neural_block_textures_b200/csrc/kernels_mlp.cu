@@ -252,11 +252,8 @@ void launch_pop_eval(cudaStream_t s, int shape, const DevModel& m, const PopArgs
             const int chunks = pop_chunks(a.M, a.chunk);
             dim3 grid((unsigned)a.ncand, (unsigned)chunks);
             const size_t smem = 2 * (size_t)m.P * sizeof(float);
-            static bool attr_set = false;   // two weight sets of up to 12288 floats: above the 48 KB default
-            if (!attr_set) {
-                NTCB_CHECK(cudaFuncSetAttribute(k_pop_eval_generic<kPopTPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 12288 * 4));
-                attr_set = true;
-            }
+            // two weight sets of up to 12288 floats: above the 48 KB default
+            ensure_dynamic_smem((const void*)k_pop_eval_generic<kPopTPB>, 2 * 12288 * 4);
             k_pop_eval_generic<kPopTPB><<<grid, kPopTPB, smem, s>>>(m, a, chunks);
         }
     }

@@ -25,8 +25,9 @@
 // top 19 bits of x and x_lo = x - x_hi (exact), accumulated in FP32 by the tensor core. The dropped a_lo b_lo
 // term and the TF32 truncation of the lo parts leave a relative error near 2^-21 per product: FP32-level, but
 // not the bit pattern of the reference's sequential FMA chain. The output sigmoid uses the fast exponential.
-// Fitness agrees with the exact kernels to ~1e-6 relative (the pinned tolerance is 1e-5); the packed-FP32
-// kernel stays available for bit-exact runs and is always used for FD.
+// Fitness agrees with the exact kernels to ~1e-6 relative (the pinned tolerance is 1e-5). FD candidates (mode 1:
+// the stats pair and weight j at +-h) run on this kernel too unless the exact mode is selected; the packed-FP32
+// kernel stays available for bit-exact runs (ntcb_set_pop_kernel).
 //
 // Every mbarrier wait is bounded: on time-out the CTA records an error flag, stops issuing, gives the
 // outstanding MMAs one more bounded wait and still frees its TMEM.
@@ -490,14 +491,9 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
     using T = TcShape<S>;
     const int chunks = pop_chunks(a.M, a.chunk);
     const size_t smem = (size_t)T::STREAMS * 2 * T::SIGN * sizeof(float);
-    static int nsm = 0;
     constexpr bool kL3TC = T::L3TC;
-    if (nsm == 0) {
-        int dev = 0;
-        NTCB_CHECK(cudaGetDevice(&dev));
-        NTCB_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-        NTCB_CHECK(cudaFuncSetAttribute(k_pop_eval_tc<S, kL3TC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    }
+    const int nsm = device_sm_count();
+    ensure_dynamic_smem((const void*)k_pop_eval_tc<S, kL3TC>, (int)smem);
     const long long items = (long long)a.ncand * chunks;
     const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
     k_pop_eval_tc<S, kL3TC><<<grid, T::TPB, smem, s>>>(m, a, chunks);
@@ -665,13 +661,8 @@ void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const floa
                    long long p_end, long long pstride, int* err) {
     using T = TcShape<S>;
     const size_t smem = (size_t)T::SIGN * sizeof(float);
-    static int nsm = 0;
-    if (nsm == 0) {
-        int dev = 0;
-        NTCB_CHECK(cudaGetDevice(&dev));
-        NTCB_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-        NTCB_CHECK(cudaFuncSetAttribute(k_lat_eval_tc<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    }
+    const int nsm = device_sm_count();
+    ensure_dynamic_smem((const void*)k_lat_eval_tc<S>, (int)smem);
     const long long items = (long long)K * ((p_end - p_begin + kTcRows - 1) / kTcRows);
     const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
     k_lat_eval_tc<S><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);

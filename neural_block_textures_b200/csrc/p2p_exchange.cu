@@ -10,7 +10,6 @@ namespace {
 
 constexpr int kP2PThreads = 512;
 constexpr uint32_t kP2PSpinPolls = 256;        // polls of a line before backing off with __nanosleep
-constexpr uint32_t kP2PPollLimit = 1u << 22;   // polls of one line (>= 128 ns each after the spin): a few seconds
 
 __device__ __forceinline__ char* stage_of(char* base, const P2PArgs& a, int par, int q) {
     return base + kP2PHeader + ((size_t)par * a.world + q) * a.cap;
@@ -25,7 +24,8 @@ __device__ __forceinline__ void ld_line(const void* p, uint64_t& lo, uint64_t& h
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "l"(p) : "memory");
 }
 
-__global__ void __launch_bounds__(kP2PThreads) k_p2p_allgather(P2PArgs a, char* dst, size_t bytes, uint32_t epoch, int* err) {
+__global__ void __launch_bounds__(kP2PThreads) k_p2p_allgather(P2PArgs a, char* dst, size_t bytes, uint32_t epoch, uint32_t poll_limit,
+                                                                int* err) {
     const int r = a.rank, G = a.world, par = (int)(epoch & 1u);
     const size_t nwords = bytes / 4, nlines = (nwords + 1) / 2;
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kP2PThreads) k_p2p_allgather(P2PArgs a, char* 
             for (;;) {
                 ld_line(s + 16 * i, lo, hi);
                 if ((uint32_t)(lo >> 32) == epoch && (uint32_t)(hi >> 32) == epoch) break;
-                if (++polls > kP2PPollLimit) { atomicExch(err, 2); return; }
+                if (++polls > poll_limit) { atomicExch(err, 2); return; }
                 if (polls > kP2PSpinPolls) __nanosleep(128);
             }
             out[2 * i] = (uint32_t)lo;
@@ -61,16 +61,11 @@ __global__ void __launch_bounds__(kP2PThreads) k_p2p_allgather(P2PArgs a, char* 
 
 size_t p2p_stage_bytes(size_t bytes) { return ((bytes / 4 + 1) / 2) * 16; }
 
-void launch_p2p_allgather(cudaStream_t s, const P2PArgs& a, void* dst, size_t bytes, uint32_t epoch, int* err) {
-    static int nsm = 0;
-    if (nsm == 0) {
-        int dev = 0;
-        NTCB_CHECK(cudaGetDevice(&dev));
-        NTCB_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-    }
+void launch_p2p_allgather(cudaStream_t s, const P2PArgs& a, void* dst, size_t bytes, uint32_t epoch, uint32_t poll_limit, int* err) {
+    const int nsm = device_sm_count();
     const size_t lines = (bytes / 4 + 1) / 2;
     const int grid = (int)std::max<size_t>(1, std::min<size_t>((size_t)nsm, (lines + kP2PThreads - 1) / kP2PThreads));
-    k_p2p_allgather<<<grid, kP2PThreads, 0, s>>>(a, static_cast<char*>(dst), bytes, epoch, err);
+    k_p2p_allgather<<<grid, kP2PThreads, 0, s>>>(a, static_cast<char*>(dst), bytes, epoch, std::max(1u, poll_limit), err);
     NTCB_CHECK(cudaGetLastError());
 }
 

@@ -1,7 +1,7 @@
 // Peer-memory all-gather for the sharded iteration (one process and one GPU per rank, NVLink / NVSwitch peers).
 //
 // Every rank owns one exchange buffer, mapped into every other rank's address space with CUDA IPC:
-//   [kP2PHeader bytes, unused] [staging: 2 parities x world x cap bytes, block q of a parity = rank q's lines]
+//   [kP2PHeader bytes: the rank's token slots of ntcb_p2p_barrier] [staging: 2 parities x world x cap bytes, block q of a parity = rank q's lines]
 // A block travels as 16-byte lines of two 64-bit elements {epoch << 32 | one 4-byte word}: the data carries its own
 // arrival flag (the low-latency line format NCCL's LL protocol uses), so one kernel per exchange stores the rank's
 // own block as lines into every peer's staging (parity = epoch & 1) and then polls its own staging, line by line
@@ -20,7 +20,7 @@
 namespace ntcb {
 
 constexpr int kP2PMaxRanks = 8;
-constexpr size_t kP2PHeader = 256;   // unused bytes before the staging (keeps it 256-byte aligned)
+constexpr size_t kP2PHeader = 256;   // bytes before the staging (barrier tokens; keeps the staging 256-byte aligned)
 
 struct P2PArgs {
     int world = 1, rank = 0;
@@ -30,9 +30,12 @@ struct P2PArgs {
 
 // Staging bytes of a block of `bytes` (a multiple of 4): 16 per two words.
 size_t p2p_stage_bytes(size_t bytes);
+// Polls of one staged line before a wait is declared failed (>= 128 ns each after the first 256): a few seconds.
+constexpr uint32_t kP2PPollLimit = 1u << 22;
 // In-place all-gather of `bytes` per rank over the exchange buffers: rank r's block is at dst + r * bytes on entry,
-// every rank's block is there on exit. p2p_stage_bytes(bytes) <= cap, bytes a multiple of 4. A wait that runs out
-// sets *err = 2 and the kernel returns (the host reports it at the next synchronising call).
-void launch_p2p_allgather(cudaStream_t s, const P2PArgs& a, void* dst, size_t bytes, uint32_t epoch, int* err);
+// every rank's block is there on exit. p2p_stage_bytes(bytes) <= cap, bytes a multiple of 4. A line that has not
+// arrived after poll_limit polls sets *err = 2 and its thread returns (the host reads the word at its next
+// synchronising call).
+void launch_p2p_allgather(cudaStream_t s, const P2PArgs& a, void* dst, size_t bytes, uint32_t epoch, uint32_t poll_limit, int* err);
 
 }  // namespace ntcb

@@ -11,10 +11,17 @@
 // held until the process exits. Host code cannot use its name as a device address (in host code it names a
 // host-side stand-in), so the first call on each device, with that device current, asks the runtime for the
 // device address (cudaGetSymbolAddress) and keeps it; later calls on that device reuse it. That first call
-// may load the module, so make it before any stream capture begins. Within one process every call on a device
-// shares the array, which keeps the last call's contents: calls that overlap in time (for example from
-// several host threads) race on it and must be serialised by the caller; each process has its own copy.
-// No region needs clearing between calls: every value a kernel reads is written earlier in the same call.
+// may load the module, so make it before any stream capture begins. The kept address belongs to the device's
+// current context: after a cudaDeviceReset the module may load at another address, so do not call this entry
+// again in a process that has reset the device. Within one process every call on a device shares the array,
+// which keeps the last call's contents: calls that overlap in time (for example from several host threads)
+// race on it and must be serialised by the caller; each process has its own copy. No region needs clearing
+// between calls: every value a kernel reads is written earlier in the same call.
+//
+// Errors come back to the caller, never as a process exit: a bad argument or a request above the maximum is
+// refused before the GPU is touched, and a CUDA failure inside the call (a copy, a launch) makes it return 0 with
+// the runtime's message. A CUDA error the caller left pending before the call is reported the same way (and left
+// pending), since the call could not tell its own launch errors from it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -101,6 +108,16 @@ extern "C" int ntcb_es_fitness_noalloc(const ntcb_model_desc* d, int it, float s
         set_reason(why, why_cap, msg);
         return 0;
     }
+    // ---- a CUDA error pending from the caller's earlier work: report it, leave it pending
+    {
+        const cudaError_t pending = cudaPeekAtLastError();
+        if (pending != cudaSuccess) {
+            char msg[200];
+            snprintf(msg, sizeof(msg), "a CUDA error was pending before the call: %s", cudaGetErrorString(pending));
+            set_reason(why, why_cap, msg);
+            return 0;
+        }
+    }
     // ---- once per device: the device address of the static array
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) { set_reason(why, why_cap, "no usable CUDA device"); return 0; }
@@ -111,6 +128,7 @@ extern "C" int ntcb_es_fitness_noalloc(const ntcb_model_desc* d, int it, float s
             void* p = nullptr;
             const cudaError_t e = cudaGetSymbolAddress(&p, g_fitness_scratch);
             if (e != cudaSuccess || !p) {
+                cudaGetLastError();
                 char msg[200];
                 snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the static scratch failed: %s", cudaGetErrorString(e));
                 set_reason(why, why_cap, msg);
@@ -128,21 +146,37 @@ extern "C" int ntcb_es_fitness_noalloc(const ntcb_model_desc* d, int it, float s
     float* eps = reinterpret_cast<float*>(base + o_eps);
     double* part = reinterpret_cast<double*>(base + o_part);
     double* sfit = reinterpret_cast<double*>(base + o_fit);
-    // ---- inputs in, kernels, output out (legacy default stream; the copies are synchronous)
+    // ---- inputs in, kernels, output out (legacy default stream; the copies are synchronous). Inside the scope every
+    // CUDA failure, here or in the launchers, is recorded instead of ending the process; the first one is returned.
+    SoftErrorScope soft;
+    auto failed = [&](const char* where) {
+        if (soft.err == cudaSuccess) return false;
+        cudaGetLastError();   // clear a launch error this call made (a sticky error stays with the context)
+        char msg[240];
+        snprintf(msg, sizeof(msg), "CUDA error during %s: %s", where, cudaGetErrorString(soft.err));
+        set_reason(why, why_cap, msg);
+        return true;
+    };
     NTCB_CHECK(cudaMemcpy(sw, w, (size_t)P * 4, cudaMemcpyHostToDevice));
     NTCB_CHECK(cudaMemcpy(frows, feat, (size_t)M * d->nin * 4, cudaMemcpyHostToDevice));
     NTCB_CHECK(cudaMemcpy(trows, tgt, (size_t)M * d->nout * 4, cudaMemcpyHostToDevice));
+    if (failed("the input copies")) return 0;
     k_rows_to_cols<<<(unsigned)(((long long)M * d->nin + 255) / 256), 256>>>(frows, M, d->nin, mstride, feat_t);
     NTCB_CHECK(cudaGetLastError());
     k_rows_to_cols<<<(unsigned)(((long long)M * d->nout + 255) / 256), 256>>>(trows, M, d->nout, mstride, tgt_t);
     NTCB_CHECK(cudaGetLastError());
+    if (failed("the row transposes")) return 0;
     if (sigma != 0.0f) launch_mlp_noise(nullptr, d->seed, it, pair_begin, npairs, (int)P, eps);
+    if (failed("the noise launch")) return 0;
     PopArgs a{};
     a.mode = 0; a.it = it; a.sigma = sigma; a.fd_h = 0.0f; a.cand_begin = pair_begin; a.ncand = npairs;
     a.M = M; a.mstride = mstride; a.chunk = chunk;
     a.w0 = sw; a.eps = eps; a.feat_t = feat_t; a.tgt_t = tgt_t; a.part = part;
     launch_pop_eval(nullptr, shape, m, a);
+    if (failed("the population launch")) return 0;
     launch_pop_finish(nullptr, part, npairs, chunks, 3.0 * (double)d->wsum * M, sfit);
+    if (failed("the fitness launch")) return 0;
     NTCB_CHECK(cudaMemcpy(fit, sfit, (size_t)npairs * 2 * 8, cudaMemcpyDeviceToHost));
+    if (failed("the kernels or the result copy")) return 0;
     return 1;
 }

@@ -50,6 +50,14 @@ def qat_index(v: float, bits: int) -> int:
     return max(0, min(levels, k))
 
 
+def qat_index_array(v: np.ndarray, bits: int) -> np.ndarray:
+    """qat_index of every element of v (the same float32 steps, lround as floor(|x| + 0.5) with the sign)."""
+    levels = (1 << bits) - 1
+    x = ((v.astype(np.float32) + np.float32(1.0)) * np.float32(0.5) * np.float32(levels)).astype(np.float64)
+    k = np.floor(np.abs(x) + 0.5) * np.where(x >= 0, 1.0, -1.0)
+    return np.clip(k, 0, levels).astype(np.int64)
+
+
 @dataclass
 class ModelSpec:
     W: int
@@ -166,8 +174,7 @@ class ModelSpec:
             L0 = self.levels[0]
             z0 = z[: L0.size].reshape(-1, L0.C)
             for c, b in enumerate(self.qat_bits):
-                for t in range(z0.shape[0]):
-                    z0[t, c] = grid[b, qat_index(float(z0[t, c]), b)]
+                z0[:, c] = grid[b, qat_index_array(z0[:, c], b)]
         if self.dct_q:
             L0 = self.levels[0]
             z[: L0.size] = np.clip(z[: L0.size], -1.0, 1.0)

@@ -34,13 +34,12 @@ def _value_noise(rng: np.random.Generator, W: int, H: int, cells: int) -> np.nda
     fy = y - y0
     sx = fx * fx * (3 - 2 * fx)
     sy = fy * fy * (3 - 2 * fy)
-    a = g[y0][:, x0]
-    b = g[y0][:, x0 + 1]
-    c = g[y0 + 1][:, x0]
-    d = g[y0 + 1][:, x0 + 1]
+    # Interpolate along x on the (cells + 1) grid rows first, then pick and blend rows: every output element goes
+    # through the same operations as a * (1 - sx) + b * sx per corner row, so the field is unchanged.
     sx = sx[None, :, None]
+    gx = g[:, x0] * (1 - sx) + g[:, x0 + 1] * sx          # (cells + 1, W, 3)
     sy = sy[:, None, None]
-    return (a * (1 - sx) + b * sx) * (1 - sy) + (c * (1 - sx) + d * sx) * sy
+    return gx[y0] * (1 - sy) + gx[y0 + 1] * sy
 
 
 def base_field(W: int, H: int, seed: int) -> np.ndarray:

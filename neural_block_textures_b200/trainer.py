@@ -297,6 +297,15 @@ class Trainer:
             raise RuntimeError("ntcb_p2p_import: " + why.value.decode())
 
 
+    def p2p_set_poll_limit(self, polls: int) -> None:
+        """Polls of one staged peer line before an exchange wait fails (0: the default; ntcb_p2p_set_poll_limit)."""
+        self.lib.ntcb_p2p_set_poll_limit(self.h, polls)
+
+    def p2p_barrier(self, polls: int = 0) -> int:
+        """Peer barrier through the exchange buffers (ntcb_p2p_barrier): 0 when every peer arrived, 2 when a wait ran
+        out (the error word is returned and cleared instead of exiting)."""
+        return int(self.lib.ntcb_p2p_barrier(self.h, polls))
+
     def p2p_release(self) -> None:
         """Unmaps the peers' exchange buffers (ntcb_p2p_release); every rank, then a barrier, before destroying."""
         self.lib.ntcb_p2p_release(self.h)

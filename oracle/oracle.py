@@ -342,11 +342,15 @@ class RefSession:
     def psnr_of_decode(self, img):
         return self.lib.ref_psnr_of_decode(C.c_void_p(self.h), f32p(img))
 
-    def dct_probe_codes(self, q, dc_step: int = 4):
-        """The reference's own host probe: turn on the DCT-coded level 0 (ref_dct_enable), fit the scale codes
-        on the current model and decode buffer (Decoder::dct_fit_all), return the codes [block][channel]."""
+    def dct_probe_codes(self, q, dc_step: int = 4, deadzone: int = 0, lam: float = 0.0, rate_es: bool = False,
+                        rate_trunc: bool = False, lambda_lo: float = 0.0):
+        """The reference's own host probe: turn on the DCT-coded level 0 (ref_dct_enable, with the given dead-zone and
+        --dct-lambda settings), fit the scale codes on the current model and decode buffer (Decoder::dct_fit_all),
+        return the codes [block][channel]."""
         qa = np.ascontiguousarray(q, np.int32)
-        self.lib.ref_dct_enable(C.c_void_p(self.h), qa.ctypes.data_as(_ip), dc_step, 0, C.c_float(0.0), 0, 0, C.c_float(0.0))
+        self._dct = (dc_step, deadzone, lam, rate_es, rate_trunc)
+        self.lib.ref_dct_enable(C.c_void_p(self.h), qa.ctypes.data_as(_ip), dc_step, deadzone, C.c_float(lam), int(rate_es),
+                                int(rate_trunc), C.c_float(lambda_lo))
         self.lib.ref_dct_fit(C.c_void_p(self.h), 1)
         n = (self.spec.W // 8) * (self.spec.H // 8) * self.spec.levels[0].C
         code = np.zeros(n, np.uint8)
@@ -362,6 +366,19 @@ class RefSession:
         self.lib.ref_dct_state(C.c_void_p(self.h), sym.ctypes.data_as(C.POINTER(C.c_int16)), code.ctypes.data_as(C.POINTER(C.c_uint8)),
                                step.ctypes.data_as(_ip), None, None, None, None, None, None)
         return sym, code, step
+
+    def dct_desc_fields(self) -> dict:
+        """The device description of the session's live DCT level as main.cpp's dct_desc_of builds it
+        (main.cpp:2947-2956): geometry, rate flags, rate_scale, the host's lam_t16 bit patterns, lo_w16, dead-zone."""
+        dc_step, deadzone, lam, rate_es, rate_trunc = self._dct
+        lam_t16 = np.zeros(16, np.float32)
+        lo = C.c_int()
+        self.lib.ref_dct_state(C.c_void_p(self.h), None, None, None, None, lam_t16.ctypes.data_as(_fp), C.byref(lo), None, None, None)
+        W, H = self.spec.W, self.spec.H
+        rate_scale = np.float32(float(np.float32(lam)) / (16.0 * 65025.0 * W * H)) if rate_es else np.float32(0.0)
+        return {"live": 1, "C": self.spec.levels[0].C, "BW": W // 8, "BH": H // 8, "N": 8, "dc_step": dc_step,
+                "rate_es": int(rate_es), "rate_trunc": int(rate_trunc), "rate_scale": float(rate_scale), "lam_t16": lam_t16,
+                "lo_w16": lo.value, "deadzone": int(deadzone)}
 
     def dct_set_symbols(self, sym, code):
         sym = np.ascontiguousarray(sym, np.int16)

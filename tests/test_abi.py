@@ -2,6 +2,7 @@
 declares and every ntc_cuda::Trainer member the reference trainer calls, and the description structs
 have the reference header's layout (main.cpp fills them by field name)."""
 import ctypes as C
+import os
 import re
 import shutil
 import subprocess
@@ -12,7 +13,8 @@ import pytest
 from neural_block_textures_b200 import abi
 
 ROOT = Path(__file__).resolve().parent.parent
-REF_HEADER = Path("/root/reference/cuda/ntc_cuda.h")
+# The reference tree (read-only, present where the oracle is built; NTC_REFERENCE names it, as __graft_entry__ reads it).
+REF_HEADER = Path(os.environ.get("NTC_REFERENCE", "/root/reference")) / "cuda" / "ntc_cuda.h"
 LIB = abi.LIB_PATH
 
 

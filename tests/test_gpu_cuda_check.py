@@ -39,14 +39,22 @@ LINES = {
     # the benchmark's shapes (fixed-shape kernels): config 2 and config 3
     "cfg2_shape": "{img} --latent 512 512 1 --latent2 128 128 2 --filter nearest,bilinear --qat 2 --mlp-pairs 64",
     "cfg3_shape": "{m1} {m2} {m3} {m4} --latent 512 512 2 --latent2 128 128 4 --filter nearest,bilinear --qat 2 --mlp-pairs 64",
+    # config 4 at its own size: 1024^2, DCT-coded level 0 at q 50 with the default widths, the default --dct-lambda recipe
+    # (rate term in the latent gradient and truncation at snap), the default dead-zone and shadow pull; --dct-start 0 makes the
+    # level live before the harness runs (at the config's default 0.5 the DCT checks would report "skipped")
+    "cfg4_shape": "{img1024} --latent 1024 1024 1 --latent2 256 256 2 --filter nearest,bilinear --dct-q 50 --dct-start 0 --mlp-pairs 64",
+    # config 5 at its own size: 2048^2, level 0 1024x1024x2 2-bit selectors (2x2-pixel cells), level 1 256x256x4
+    "cfg5_shape": "{img2048} --latent 1024 1024 2 --latent2 256 256 4 --filter nearest,bilinear --qat 2 --mlp-pairs 64",
 }
 
 
 @pytest.fixture(scope="module")
 def images(tmp_path_factory):
     d = tmp_path_factory.mktemp("imgs")
-    paths = {"img": d / "synth512_s21.png"}
+    paths = {"img": d / "synth512_s21.png", "img1024": d / "synth1024_s4.png", "img2048": d / "synth2048_s5.png"}
     synth.write_png(paths["img"], synth.synth_rgb8(512, 512, 21))
+    synth.write_png(paths["img1024"], synth.synth_rgb8(1024, 1024, 4))
+    synth.write_png(paths["img2048"], synth.synth_rgb8(2048, 2048, 5))
     for t, im in enumerate(synth.synth_material(512, 512, 31, 4)):
         paths[f"m{t + 1}"] = d / f"mat512_s31_t{t}.png"
         synth.write_png(paths[f"m{t + 1}"], im)

@@ -39,6 +39,27 @@ def _run(exe: Path, args: list[str], timeout=1200) -> float:
     return _psnr(r.stdout)
 
 
+# Config 2 at its full size (512^2, population 8192, M = 4096) for 1000 iterations with the FD polish from 500: this
+# backend (default tensor-core kernels) against the reference's CUDA backend (no CPU run: ~2 s per iteration there).
+FULL_RUNS = {
+    "cfg2_full_1000": ("cfg2.png", 512, 2, "--latent 512 512 1 --latent2 128 128 2 --filter nearest,bilinear --qat 2 --mlp-pairs 4096 "
+                                        "--iters 1000 --mlp-fd 0.5 --seed 2"),
+}
+
+
+@pytest.mark.parametrize("name", list(FULL_RUNS))
+def test_final_psnr_full_size_matches_reference_backend(name, tmp_path, cuda_device):
+    for b in ("ntc_new", "ntc_ref"):
+        if not (REF / b).exists():
+            pytest.skip(f"oracle/_ref/{b} not built (needs the reference tree)")
+    png, size, seed, flags = FULL_RUNS[name]
+    synth.write_png(tmp_path / png, synth.synth_rgb8(size, size, seed))
+    common = [str(tmp_path / png), *flags.split(), "--rng", "hash", "--print-every", "1000000", "--cuda"]
+    p_new = _run(REF / "ntc_new", [*common, "--out", str(tmp_path / "new")])
+    p_ref = _run(REF / "ntc_ref", [*common, "--out", str(tmp_path / "ref")])
+    assert abs(p_new - p_ref) <= PSNR_TOL, f"reference cuda backend {p_ref} dB, b200 backend {p_new} dB"
+
+
 @pytest.mark.parametrize("name", list(RUNS))
 def test_final_psnr_matches_reference(name, tmp_path, cuda_device):
     for b in ("ntc_cpu", "ntc_new"):
