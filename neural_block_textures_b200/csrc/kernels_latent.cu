@@ -3,8 +3,11 @@
 #include "adam.cuh"
 #include "kernels.h"
 #include "mlp_tile.cuh"
+#include "fixed_layout.cuh"
 #include "latent_features.cuh"
 #include "noise.cuh"
+
+#include <type_traits>
 #include "quant.cuh"
 
 namespace ntcb {
@@ -40,7 +43,7 @@ void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevM
 // dpix[k][p] = (e+ - e-) * inv_px with the float per-pixel error of decode_err (main.cpp:1722-1735, 2015).
 // The reference launches one kernel per pair and regenerates the noise of every tap
 // (cuda/ntc_cuda.cu:358-409, 1124-1144).
-template <class S, int TPB>
+template <class S, int TPB, class LY>
 __global__ void __launch_bounds__(TPB) k_lat_eval_fixed(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                         const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
                                                         int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
@@ -56,10 +59,17 @@ __global__ void __launch_bounds__(TPB) k_lat_eval_fixed(DevModel m, const float*
 #pragma unroll
     for (int q = 0; q < R2; q++) {
         const int k = min(k0 + q, K - 1);
-        float fp[kMaxIn], fm[kMaxIn];
-        perturbed_features_pm(m, z, eps + (long long)k * nz, active, sg, px, py, fp, fm);
+        if constexpr (std::is_void_v<LY>) {
+            float fp[kMaxIn], fm[kMaxIn];
+            perturbed_features_pm(m, z, eps + (long long)k * nz, active, sg, px, py, fp, fm);
 #pragma unroll
-        for (int i = 0; i < S::NIN; i++) x[q][i] = make_float2(fp[i], fm[i]);
+            for (int i = 0; i < S::NIN; i++) x[q][i] = make_float2(fp[i], fm[i]);
+        } else {
+            float fp[S::NIN], fm[S::NIN];
+            layout_features_pm<LY>(m, z, eps + (long long)k * nz, active, sg, px, py, fp, fm);
+#pragma unroll
+            for (int i = 0; i < S::NIN; i++) x[q][i] = make_float2(fp[i], fm[i]);
+        }
     }
     float2 o[R2][S::NOUT];
     fixed_forward_x2<S, R2>(ws, x, o, m.leak, m.clamp_out);
@@ -103,16 +113,32 @@ __global__ void k_lat_eval_generic(DevModel m, const float* __restrict__ wg, con
     dpix[(long long)k * pstride + (p - p_begin)] = (ep - em) * inv_px;
 }
 
+template <class S>
+void launch_lat_fixed(cudaStream_t s, const DevModel& m, const float* w, const float* zdec, const float* eps, long long nz,
+                      const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix, long long p_begin,
+                      long long p_end, long long pstride) {
+    using LY = typename LayoutForNin<S::NIN>::type;
+    dim3 grid(blocks_for(p_end - p_begin, kLatTPB), (unsigned)((K + kLatPairs - 1) / kLatPairs));
+    const size_t smem = 2 * S::SIZE * sizeof(float);
+    if constexpr (!std::is_void_v<LY>) {
+        if (LY::matches(m)) {
+            k_lat_eval_fixed<S, kLatTPB, LY><<<grid, kLatTPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix,
+                                                                         p_begin, p_end, pstride);
+            return;
+        }
+    }
+    k_lat_eval_fixed<S, kLatTPB, void><<<grid, kLatTPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix,
+                                                                   p_begin, p_end, pstride);
+}
+
 void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                      long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
                      long long p_begin, long long p_end, long long pstride) {
     const long long n = p_end - p_begin;
     if (n <= 0) return;
     switch (shape) {
-#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: { using S = FixedShape<NIN, H1, H2, NOUT>; \
-        dim3 grid(blocks_for(n, kLatTPB), (unsigned)((K + kLatPairs - 1) / kLatPairs)); \
-        k_lat_eval_fixed<S, kLatTPB><<<grid, kLatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, eps, nz, tgt, K, active_mask, sg, inv_px, dpix, \
-                                                                                     p_begin, p_end, pstride); break; }
+#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: launch_lat_fixed<FixedShape<NIN, H1, H2, NOUT>>(s, m, w, zdec, eps, nz, tgt, K, \
+        active_mask, sg, inv_px, dpix, p_begin, p_end, pstride); break;
         NTCB_FIXED_SHAPES(NTCB_CASE)
 #undef NTCB_CASE
         default: {
@@ -209,8 +235,8 @@ void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* 
 // channel. The reference's choice (best = loss[current]; for every other value k in order: if loss[k] <
 // best take it) equals: the smallest k != current attaining the minimum of the other losses, if that
 // minimum is below loss[current]; the lanes combine their (loss, k) with that rule by shuffles.
-template <class S, int TPB, int G, int R2>
-__global__ void __launch_bounds__(TPB, 4) k_qat_fixed(DevModel m, const float* __restrict__ wg, float* __restrict__ z,
+template <class S, int TPB, int G, int R2, class LY>
+__global__ void __launch_bounds__(TPB, 3) k_qat_fixed(DevModel m, const float* __restrict__ wg, float* __restrict__ z,
                                                    const float* __restrict__ tgt, const int* __restrict__ xr,
                                                    const int* __restrict__ yr, const float* __restrict__ grid,
                                                    const int* __restrict__ bits_c, long long t_begin, long long t_end) {
@@ -243,8 +269,15 @@ __global__ void __launch_bounds__(TPB, 4) k_qat_fixed(DevModel m, const float* _
                 for (int px = x0; px < x1; px++) {
                     // keeps the weight loads of the forward inside the loop (hoisted, they exhaust the registers)
                     asm volatile("" ::: "memory");
-                    float f[kMaxIn];
-                    pixel_features(m, z, px, py, f);
+                    float f[S::NIN];
+                    if constexpr (std::is_void_v<LY>) {
+                        float fr[kMaxIn];
+                        pixel_features(m, z, px, py, fr);
+#pragma unroll
+                        for (int i = 0; i < S::NIN; i++) f[i] = fr[i];
+                    } else {
+                        layout_features<LY>(m, z, px, py, f);   // registers: the layout is known at compile time
+                    }
                     float2 x[R2][S::NIN];
 #pragma unroll
                     for (int h = 0; h < R2; h++) {
@@ -332,9 +365,18 @@ __global__ void k_qat_generic(DevModel m, const float* __restrict__ wg, float* _
 template <class S, int G, int R2>
 void launch_qat_fixed(cudaStream_t s, const DevModel& m, const float* w, float* zdec, const float* tgt, const int* xr0,
                       const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end) {
+    using LY = typename LayoutForNin<S::NIN>::type;
     const long long lanes = (t_end - t_begin) * G;
-    k_qat_fixed<S, kQatTPB, G, R2><<<blocks_for(lanes, kQatTPB), kQatTPB, 2 * S::SIZE * sizeof(float), s>>>(m, w, zdec, tgt, xr0, yr0,
-                                                                                                           grid, bits, t_begin, t_end);
+    const size_t smem = 2 * S::SIZE * sizeof(float);
+    if constexpr (!std::is_void_v<LY>) {
+        if (LY::matches(m)) {
+            k_qat_fixed<S, kQatTPB, G, R2, LY><<<blocks_for(lanes, kQatTPB), kQatTPB, smem, s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits,
+                                                                                                t_begin, t_end);
+            return;
+        }
+    }
+    k_qat_fixed<S, kQatTPB, G, R2, void><<<blocks_for(lanes, kQatTPB), kQatTPB, smem, s>>>(m, w, zdec, tgt, xr0, yr0, grid, bits,
+                                                                                          t_begin, t_end);
 }
 
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,

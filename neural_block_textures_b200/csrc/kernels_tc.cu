@@ -36,8 +36,10 @@
 #include "pop_common.cuh"
 #include "tc.cuh"
 #include "latent_features.cuh"
+#include "fixed_layout.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace ntcb {
 
@@ -80,9 +82,10 @@ struct TcShape {
     // The output layer runs on the tensor core for wide outputs (12: measured 1.33 vs 1.52 ms at config 3)
     // and on the FP32 pipe for 3 outputs (0.86 vs 1.03 ms at config 2), where 16-wide MMAs are mostly padding.
     static constexpr bool L3TC = S::NOUT > 4;
-    // TMEM columns of one stream: D (layers 1 and 2), D3 (tensor output layer only), X hi / lo, H hi / lo
-    static constexpr int cD = 0, cD3 = 32, cXh = L3TC ? 48 : 32, cXl = cXh + K1, cHh = cXl + K1, cHl = cHh + K2;
-    static constexpr int COLS = cHl + K2;
+    // TMEM columns of one stream: D (layers 1 and 2), D3 (tensor output layer only), X and H as A operands, each
+    // split into hi / lo and interleaved by 8-column K steps ([hi 8 | lo 8] per step: one 16-column store per step)
+    static constexpr int cD = 0, cD3 = 32, cX = L3TC ? 48 : 32, cH = cX + 2 * K1;
+    static constexpr int COLS = cH + 2 * K2;
     // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread;
     // 4 streams is the floor the kernels were tuned at). Measured: 2 streams cost +33 % over 4.
     static constexpr int STREAMS = kTmemCols / COLS >= 5 ? 5 : 4;
@@ -136,22 +139,30 @@ __device__ __forceinline__ float2 leaky_pair(float2 x, float leak) {
     return make_float2(fmaxf(x.x, t.x), fmaxf(x.y, t.y));
 }
 
-// Split N (multiple of 8) values into hi / lo and store them to TMEM columns [ch, ch + N) / [cl, cl + N).
+// Split N (multiple of 8) values into hi / lo and store them as an interleaved A operand from TMEM column c:
+// K step q / 8 occupies columns [c + 2q, c + 2q + 16) = [hi of v[q .. q + 8) | lo of v[q .. q + 8)].
 template <int N>
-__device__ __forceinline__ void store_split(uint32_t trow, int ch, int cl, const float* v) {
+__device__ __forceinline__ void store_split(uint32_t trow, int c, const float* v) {
 #pragma unroll
     for (int q = 0; q < N; q += 8) {
-        float hi[8], lo[8];
+        float hl[16];
 #pragma unroll
         for (int j = 0; j < 8; j += 2) {
             const float2 x = make_float2(v[q + j], v[q + j + 1]);
             const float2 h = make_float2(tc::tf32_hi(x.x), tc::tf32_hi(x.y));
             const float2 l = __ffma2_rn(h, make_float2(-1.0f, -1.0f), x);   // x - hi, exact
-            hi[j] = h.x; hi[j + 1] = h.y; lo[j] = l.x; lo[j + 1] = l.y;
+            hl[j] = h.x; hl[j + 1] = h.y; hl[8 + j] = l.x; hl[8 + j + 1] = l.y;
         }
-        tc::st_x8(trow + ch + q, hi);
-        tc::st_x8(trow + cl + q, lo);
+        tc::st_x8p(trow + c + 2 * q, hl);          // two 8-column stores: one 16-column store spills registers
+        tc::st_x8p(trow + c + 2 * q + 8, hl + 8);
     }
+}
+// N (multiple of 8) accumulator columns from TMEM column c into v, in as few loads as the widths allow.
+template <int N>
+__device__ __forceinline__ void load_acc(uint32_t trow, int c, float* v) {
+#pragma unroll
+    for (int q = 0; q + 16 <= N; q += 16) tc::ld_x16p(trow + c + q, v + q);
+    if constexpr (N % 16 != 0) tc::ld_x8p(trow + c + (N / 16) * 16, v + (N / 16) * 16);
 }
 
 // Output layer + weighted squared error of one row on the FP32 pipe, from the layer-2 accumulator row h
@@ -191,17 +202,19 @@ __device__ __forceinline__ float out_layer_error(const DevModel& m, const float*
     return e;
 }
 
-// Warp 0 (converged): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K step), then commit.
+// Warp 0 (converged): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K step), then commit. a: the
+// interleaved A operand in TMEM (K step s: hi at a + 16 s, lo at a + 16 s + 8); b_hi4 / b_lo4: the B operands' shared
+// addresses shifted right by 4 (hoisted; each descriptor is then one add).
 template <int K, int N>
-__device__ __forceinline__ void issue3(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo, uint64_t* bar) {
+__device__ __forceinline__ void issue3(uint32_t d, uint32_t a, uint32_t b_hi4, uint32_t b_lo4, uint64_t* bar) {
     constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
     constexpr uint32_t sbo = (uint32_t)K * 32u;
     tc::fence_after_sync();
 #pragma unroll
     for (int s = 0; s < K / 8; s++) {
-        if (elect_one()) tc::mma_tf32_ts(d, a_lo + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, s > 0 ? 1u : 0u);
-        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_lo + 256 * s, 128, sbo), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s + 8, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, s > 0 ? 1u : 0u);
+        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
     }
     if (elect_one()) tc::commit(bar);
     __syncwarp();
@@ -210,31 +223,40 @@ __device__ __forceinline__ void issue3(uint32_t d, uint32_t a_hi, uint32_t a_lo,
 // Layer 2 of a shape with B1TC: the 3xTF32 product over K, then D += 1 * b1_lo + 1 * b1_hi from the constant A
 // block `one` (its lo part is zero), then commit.
 template <int K, int N>
-__device__ __forceinline__ void issue3_bias(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo, uint32_t one,
-                                            uint32_t bb_hi, uint32_t bb_lo, uint64_t* bar) {
+__device__ __forceinline__ void issue3_bias(uint32_t d, uint32_t a, uint32_t b_hi4, uint32_t b_lo4, uint32_t one, uint32_t bb_hi4,
+                                            uint32_t bb_lo4, uint64_t* bar) {
     constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
     constexpr uint32_t sbo = (uint32_t)K * 32u;
     tc::fence_after_sync();
 #pragma unroll
     for (int s = 0; s < K / 8; s++) {
-        if (elect_one()) tc::mma_tf32_ts(d, a_lo + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, s > 0 ? 1u : 0u);
-        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_lo + 256 * s, 128, sbo), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, a_hi + 8 * s, tc::sdesc(b_hi + 256 * s, 128, sbo), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s + 8, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, s > 0 ? 1u : 0u);
+        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
     }
-    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc(bb_lo, 128, 256), id, 1u);
-    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc(bb_hi, 128, 256), id, 1u);
+    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_lo4, 128, 256), id, 1u);
+    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_hi4, 128, 256), id, 1u);
     if (elect_one()) tc::commit(bar);
     __syncwarp();
 }
 
-// Layer 2 of unit (A = H hi / lo of the stream, B = the sign's W1 and b1 blocks).
+// Byte offset / 16 of a float offset into a weight set (every B operand block starts on a 16-byte boundary).
+template <int FLOATS>
+constexpr uint32_t s4() { static_assert(FLOATS % 4 == 0, "B operand blocks are 16-byte aligned"); return (uint32_t)FLOATS / 4; }
+
+// Layer 1 of unit (A = X of the stream, B = the sign's W0 | b0 block); sb4 = the sign's weight set address >> 4.
 template <class T>
-__device__ __forceinline__ void issue_layer2(uint32_t tbase, uint32_t tb, uint32_t sb, uint64_t* bar) {
+__device__ __forceinline__ void issue_layer1(uint32_t tb, uint32_t sb4, uint64_t* bar) {
+    issue3<T::K1, T::N1>(tb + T::cD, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), bar);
+}
+// Layer 2 of unit (A = H of the stream, B = the sign's W1 and b1 blocks).
+template <class T>
+__device__ __forceinline__ void issue_layer2(uint32_t tbase, uint32_t tb, uint32_t sb4, uint64_t* bar) {
     if constexpr (T::B1TC)
-        issue3_bias<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, tbase + T::cOne,
-                                  sb + T::oBbh * 4, sb + T::oBbl * 4, bar);
+        issue3_bias<T::K2, T::N2>(tb + T::cD, tb + T::cH, sb4 + s4<T::oB2h>(), sb4 + s4<T::oB2l>(), tbase + T::cOne,
+                                  sb4 + s4<T::oBbh>(), sb4 + s4<T::oBbl>(), bar);
     else
-        issue3<T::K2, T::N2>(tb + T::cD, tb + T::cHh, tb + T::cHl, sb + T::oB2h * 4, sb + T::oB2l * 4, bar);
+        issue3<T::K2, T::N2>(tb + T::cD, tb + T::cH, sb4 + s4<T::oB2h>(), sb4 + s4<T::oB2l>(), bar);
 }
 
 // The constant A block of the layer-2 bias step: TMEM column cOne = 1, cOne + 1 .. + 7 = 0 on all 128 lanes,
@@ -310,7 +332,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
 
     const uint32_t tb = tbase + (uint32_t)(T::COLS * g);
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
-    const uint32_t sb0 = tc::smem_addr(sw), sb1 = sb0 + (uint32_t)(T::SIGN * 4);
+    const uint32_t sb0 = tc::smem_addr(sw) >> 4, sb1 = sb0 + s4<T::SIGN>();   // the signs' weight sets, address >> 4
     const float leak = m.leak;
     uint32_t waited = 0, waited3 = 0;   // completed phases this thread has observed on bar / bar3
     bool ok = true;
@@ -337,7 +359,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         float x[T::K1];
 #pragma unroll
         for (int i = 0; i < T::K1; i++) x[i] = i < S::NIN ? xr[i] : (i == S::NIN ? 1.0f : 0.0f);
-        store_split<T::K1>(trow, T::cXh, T::cXl, x);
+        store_split<T::K1>(trow, T::cX, x);
     };
     const long long items = (long long)a.ncand * chunks;
     const long long nstreams = (long long)gridDim.x * T::STREAMS, gs = (long long)blockIdx.x * T::STREAMS + g;
@@ -370,7 +392,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb0 + T::oB1h * 4, sb0 + T::oB1l * 4, bar);
+        if (warp == issuer) issue_layer1<T>(tb, sb0, bar);
 
 #pragma unroll 1
         for (int base = row0; base < row1; base += kTcRows) {
@@ -390,15 +412,14 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 float h[S::H1 > S::H2 ? S::H1 : S::H2];
                 // layer 1 result -> H
                 wait_mma();
-#pragma unroll
-                for (int q = 0; q < S::H1; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+                load_acc<S::H1>(trow, T::cD, h);
                 tc::wait_ld();
 #pragma unroll
                 for (int j = 0; j < S::H1; j += 2) {
                     const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak);
                     h[j] = v.x; h[j + 1] = v.y;
                 }
-                store_split<T::K2>(trow, T::cHh, T::cHl, h);
+                store_split<T::K2>(trow, T::cH, h);
                 tc::wait_st();
                 tc::fence_before_sync();
                 ok = stream_sync_and(bar_id, ok);
@@ -406,8 +427,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 if (warp == issuer) issue_layer2<T>(tbase, tb, sb, bar);
                 // layer 2 result -> registers
                 wait_mma();
-#pragma unroll
-                for (int q = 0; q < S::H2; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+                load_acc<S::H2>(trow, T::cD, h);
                 tc::wait_ld();
                 // next unit's layer 1: the other sign of this tile, or the next tile's + sign
                 const bool next = sg == 0 || more;
@@ -421,18 +441,15 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                         const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
                         h[j] = h0.x; h[j + 1] = h0.y; h[j + 2] = h1.x; h[j + 3] = h1.y;
                     }
-                    store_split<T::K3>(trow, T::cHh, T::cHl, h);
+                    store_split<T::K3>(trow, T::cH, h);
                     if (sg == 1 && more) { store_x(); load_x(base + 2 * kTcRows); }
                     tc::wait_st();
                     tc::fence_before_sync();
                     ok = stream_sync_and(bar_id, ok);
                     if (!ok) break;
                     if (warp == issuer) {
-                        issue3<T::K3, T::N3>(tb + T::cD3, tb + T::cHh, tb + T::cHl, sb + T::oB3h * 4, sb + T::oB3l * 4, bar3);
-                        if (next) {
-                            const uint32_t nb = sg ? sb0 : sb1;
-                            issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
-                        }
+                        issue3<T::K3, T::N3>(tb + T::cD3, tb + T::cH, sb + s4<T::oB3h>(), sb + s4<T::oB3l>(), bar3);
+                        if (next) issue_layer1<T>(tb, sg ? sb0 : sb1, bar);
                     }
                     wait_mma3();
                     float o[T::NOUTP];
@@ -455,10 +472,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     tc::fence_before_sync();
                     ok = stream_sync_and(bar_id, ok);
                     if (!ok) break;
-                    if (next && warp == issuer) {
-                        const uint32_t nb = sg ? sb0 : sb1;
-                        issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, nb + T::oB1h * 4, nb + T::oB1l * 4, bar);
-                    }
+                    if (next && warp == issuer) issue_layer1<T>(tb, sg ? sb0 : sb1, bar);
                     // output layer and error of this unit, overlapping the tensor core's next layer 1
                     const double e = valid ? (double)out_layer_error<S>(m, ws, h, t, leak) : 0.0;
                     if (sg == 0) acc_p += e; else acc_m += e;
@@ -509,7 +523,7 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
 // 128-pixel tile), its two units are the + and - decodes of the tile (X = the +/- perturbed features, which
 // share their taps and are gathered together, one item ahead, while the layer-2 MMAs of the current item
 // run). The output layer runs on the FP32 pipe.
-template <class S>
+template <class S, class LY>
 __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                          const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
                                                          int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
@@ -540,7 +554,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
 
     const uint32_t tb = tbase + (uint32_t)(T::COLS * g);
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
-    const uint32_t sb = tc::smem_addr(sw);
+    const uint32_t sb = tc::smem_addr(sw) >> 4;   // the weight set's address >> 4
     const float leak = m.leak;
     uint32_t waited = 0;
     bool ok = true;
@@ -563,10 +577,14 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         const int k = (int)(item / ntiles);
         const long long p = p_begin + (item - (long long)k * ntiles) * kTcRows + tid;
         const long long pc = p < p_end ? p : p_end - 1;
-        float a[kMaxIn], b[kMaxIn];
-        perturbed_features_pm(m, z, eps + (long long)k * nz, active, sg, (int)(pc % m.W), (int)(pc / m.W), a, b);
+        if constexpr (std::is_void_v<LY>) {
+            float a[kMaxIn], b[kMaxIn];
+            perturbed_features_pm(m, z, eps + (long long)k * nz, active, sg, (int)(pc % m.W), (int)(pc / m.W), a, b);
 #pragma unroll
-        for (int i = 0; i < S::NIN; i++) { xp[i] = a[i]; xm[i] = b[i]; }
+            for (int i = 0; i < S::NIN; i++) { xp[i] = a[i]; xm[i] = b[i]; }
+        } else {
+            layout_features_pm<LY>(m, z, eps + (long long)k * nz, active, sg, (int)(pc % m.W), (int)(pc / m.W), xp, xm);
+        }
 #pragma unroll
         for (int c = 0; c < S::NOUT; c++) tt[c] = __ldg(tgt + pc * S::NOUT + c);
     };
@@ -574,21 +592,20 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         float v[T::K1];
 #pragma unroll
         for (int i = 0; i < T::K1; i++) v[i] = i < S::NIN ? x[i] : (i == S::NIN ? 1.0f : 0.0f);
-        store_split<T::K1>(trow, T::cXh, T::cXl, v);
+        store_split<T::K1>(trow, T::cX, v);
     };
     // layer-1 result -> H in TMEM, then layer 2 issued
     auto layer1_to_layer2 = [&]() {
         float h[S::H1];
         wait_mma();
-#pragma unroll
-        for (int q = 0; q < S::H1; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+        load_acc<S::H1>(trow, T::cD, h);
         tc::wait_ld();
 #pragma unroll
         for (int j = 0; j < S::H1; j += 2) {
             const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak);
             h[j] = v.x; h[j + 1] = v.y;
         }
-        store_split<T::K2>(trow, T::cHh, T::cHl, h);
+        store_split<T::K2>(trow, T::cH, h);
         tc::wait_st();
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
@@ -601,7 +618,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        if (warp == issuer) issue_layer1<T>(tb, sb, bar);
     }
 #pragma unroll 1
     for (long long item = i0; item < i1 && ok; item++) {
@@ -613,28 +630,26 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         if (!ok) break;
         if (more) gather(item + 1, np, nm, nt);    // overlaps the layer-2 MMAs
         wait_mma();
-#pragma unroll
-        for (int q = 0; q < S::H2; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+        load_acc<S::H2>(trow, T::cD, h);
         tc::wait_ld();
         store_x(fm);
         tc::wait_st();
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
-        if (warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        if (warp == issuer) issue_layer1<T>(tb, sb, bar);
         const float ep = out_layer_error<S>(m, sw, h, t, leak);
         // - unit
         layer1_to_layer2();
         if (!ok) break;
         wait_mma();
-#pragma unroll
-        for (int q = 0; q < S::H2; q += 8) tc::ld_x8p(trow + T::cD + q, h + q);
+        load_acc<S::H2>(trow, T::cD, h);
         tc::wait_ld();
         if (more) { store_x(np); tc::wait_st(); }
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
-        if (more && warp == issuer) issue3<T::K1, T::N1>(tb + T::cD, tb + T::cXh, tb + T::cXl, sb + T::oB1h * 4, sb + T::oB1l * 4, bar);
+        if (more && warp == issuer) issue_layer1<T>(tb, sb, bar);
         const float em = out_layer_error<S>(m, sw, h, t, leak);
         {
             const int k = (int)(item / ntiles);
@@ -661,11 +676,19 @@ void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const floa
                    long long p_end, long long pstride, int* err) {
     using T = TcShape<S>;
     const size_t smem = (size_t)T::SIGN * sizeof(float);
+    using LY = typename LayoutForNin<S::NIN>::type;
     const int nsm = device_sm_count();
-    ensure_dynamic_smem((const void*)k_lat_eval_tc<S>, (int)smem);
     const long long items = (long long)K * ((p_end - p_begin + kTcRows - 1) / kTcRows);
     const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
-    k_lat_eval_tc<S><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
+    if constexpr (!std::is_void_v<LY>) {
+        if (LY::matches(m)) {
+            ensure_dynamic_smem((const void*)k_lat_eval_tc<S, LY>, (int)smem);
+            k_lat_eval_tc<S, LY><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
+            return;
+        }
+    }
+    ensure_dynamic_smem((const void*)k_lat_eval_tc<S, void>, (int)smem);
+    k_lat_eval_tc<S, void><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
 }
 
 }  // namespace

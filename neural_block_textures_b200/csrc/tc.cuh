@@ -50,6 +50,17 @@ __device__ __forceinline__ void ld_x8p(uint32_t taddr, float* v) {
                  : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
                  : "r"(taddr) : "memory");
 }
+__device__ __forceinline__ void st_x16p(uint32_t taddr, const float* v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+                 ::"r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+                   "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]) : "memory");
+}
+__device__ __forceinline__ void ld_x16p(uint32_t taddr, float* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]),
+                   "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]), "=f"(v[14]), "=f"(v[15])
+                 : "r"(taddr) : "memory");
+}
 __device__ __forceinline__ void ld_x4p(uint32_t taddr, float* v) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
                  : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "r"(taddr) : "memory");
@@ -64,6 +75,12 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// The same descriptor from the byte address already shifted right by 4 (shared memory < 256 KB, so it fits the
+// 14-bit field and no masking is needed): one add per MMA when the shift is hoisted out of the issue loop.
+__device__ __forceinline__ uint64_t sdesc_s4(uint32_t saddr_s4, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)(saddr_s4 + ((lbo >> 4) << 16)) | ((uint64_t)(((sbo >> 4) & 0x3FFFu) | (1u << 14)) << 32);
 }
 
 // ---- MMA (single thread issues)

@@ -380,6 +380,10 @@ class RefSession:
                 "rate_es": int(rate_es), "rate_trunc": int(rate_trunc), "rate_scale": float(rate_scale), "lam_t16": lam_t16,
                 "lo_w16": lo.value, "deadzone": int(deadzone)}
 
+    def dct_shadow_pull(self, f: float) -> None:
+        """The --dct-shadow-pull step on the host (main.cpp:4139-4146): z += f (zq - z) on level 0, then the re-snap."""
+        self.lib.ref_dct_shadow_pull(C.c_void_p(self.h), C.c_float(f))
+
     def dct_set_symbols(self, sym, code):
         sym = np.ascontiguousarray(sym, np.int16)
         code = np.ascontiguousarray(code, np.uint8)
