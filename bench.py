@@ -16,6 +16,13 @@ communicator; --shard-driver python: the per-phase entry points around torch.dis
 ends each iteration bit-identical to one GPU.
 --impl reference: the reference's own CPU trainer (main.cpp compiled from source, OpenMP on every host
 thread) timed on a bounded sample of the same iteration (rank 0 only).
+
+Timing: W warm-up iterations, then the ranks are lined up (stream drained, barrier, device synchronised) and K
+iterations are timed one by one with CUDA events on the trainer's stream, the L2 flushed before each outside the
+events; ms_per_step is the per-rank sum / K, max over ranks (ms_per_step_median beside it). The same rules time
+the FD phase, the NCCL-exchange variant (N > 1: the north star's all-gather over NCCL instead of the peer-memory
+kernel) and the `cfg5` leg: the north star's scaling configuration (config 5, 2048^2, population 32768) on the same
+N GPUs, so that the per-N lines carry its strong-scaling inputs next to the config-2 headline.
 """
 from __future__ import annotations
 
@@ -634,6 +641,23 @@ def main():
     kernel = tr.pop_kernel()
     pprint = progress_print_leg(tr, cfg, not args.no_cpu_baseline) if (rank == 0 and world == 1) else None
     exchange = arm.exchange()
+    # ---- the same ES iterations with NCCL all-gathers in place of the peer-memory exchange (N > 1, native driver): the
+    # north star's fitness exchange by NCCL, timed by the same rules for comparison (the peer exchange is released on
+    # every rank first; the library then issues the in-place NCCL all-gathers on its own communicator)
+    nccl_line = None
+    if arm.native is not None and arm.native.p2p:
+        tr.p2p_release()
+        dist.barrier()
+        arm.native.p2p = False
+        for _ in range(3):
+            step(it); it += 1
+        start_together(stream, dist)
+        nper, it = timed_steps(arm, step, it, args.steps, flush, dist)
+        nms, nmed = max_over_ranks([sum(nper), statistics.median(nper)], dist)
+        nccl_line = {"exchange": "NCCL in-place all-gathers (library communicator)", "steps": args.steps,
+                     "ms_per_step": nms / args.steps, "ms_per_step_median": nmed,
+                     "value": decodes * args.steps / (nms * 1e-3), "unit": "decodes/s"}
+
     arm.close()
 
     # ---- the north star's scaling configuration on the same GPUs (every rank takes part)
@@ -670,6 +694,7 @@ def main():
                     "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
             "gpu_launches": launches,
             "fd_phase": fd_line,
+            "nccl_exchange": nccl_line,
             "cfg5": cfg5,
             "clocks": clk.summary(),
         }

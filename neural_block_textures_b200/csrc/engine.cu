@@ -59,6 +59,7 @@ struct Trainer::Impl {
     float* lat_eps = nullptr; long long lat_eps_cap = 0;   // [K][nz]
     float* dpix = nullptr; long long dpix_cap = 0;         // [K][npix]
     std::vector<int*> lvl_xr, lvl_yr;                      // per level footprint ranges (device)
+    int qat_cw = 0, qat_ch = 0;                            // level-0 cell size in pixels when every footprint is a whole cell
     int* ranges = nullptr;
     // DCT
     bool dct = false, dct_live = false, rate_es = false, rate_trunc = false;
@@ -377,6 +378,14 @@ bool init_impl(Impl& I, const ntc_cuda::ModelDesc& d, const float* z, const floa
             const bool nr = d.lv[l].nearest;
             if (!axis_ranges(d.W, d.lv[l].W, nr, xb, xe) || !axis_ranges(d.H, d.lv[l].H, nr, yb, ye)) {
                 why = "a texel footprint is not contiguous (unsupported level geometry)"; free_all(I); return false;
+            }
+            if (l == 0 && nr && d.W % d.lv[0].W == 0 && d.H % d.lv[0].H == 0) {
+                // uniform cells: texel t covers pixels [t r, (t + 1) r) on both axes (the tensor-core selector search)
+                const int rx = d.W / d.lv[0].W, ry = d.H / d.lv[0].H;
+                bool uniform = true;
+                for (int t = 0; t < d.lv[0].W; t++) uniform = uniform && xb[t] == t * rx && xe[t] == (t + 1) * rx;
+                for (int t = 0; t < d.lv[0].H; t++) uniform = uniform && yb[t] == t * ry && ye[t] == (t + 1) * ry;
+                if (uniform) { I.qat_cw = rx; I.qat_ch = ry; }
             }
             offs.push_back(all.size());
             all.insert(all.end(), xb.begin(), xb.end()); all.insert(all.end(), xe.begin(), xe.end());
@@ -722,10 +731,14 @@ void lat_step_impl(Impl& I, int it, float sigma, float lr, int K) {
 void qat_rows_part(Impl& I, long long t_begin, long long t_end) {
     if (I.d.qat <= 0) die("qat_search without --qat in the model description");
     timed(I, "qat", 1, [&] {
-        int max_bits = 0;
-        for (int c = 0; c < I.d.lv[0].C; c++) max_bits = std::max(max_bits, I.d.qat_bits[c]);
-        ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits, t_begin, t_end,
-                         max_bits);
+        int max_bits = 0, min_bits = 64;
+        for (int c = 0; c < I.d.lv[0].C; c++) { max_bits = std::max(max_bits, I.d.qat_bits[c]); min_bits = std::min(min_bits, I.d.qat_bits[c]); }
+        const bool tc = I.tensor_pop && I.qat_cw > 0 && min_bits == max_bits &&
+                        ntcb::launch_qat_tc(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.qat_grid, max_bits, I.qat_cw, I.qat_ch, t_begin,
+                                            t_end, I.tc_err);
+        if (!tc)
+            ntcb::launch_qat(I.stream, I.shape, I.dm, I.w, I.zdec, I.tgt, I.lvl_xr[0], I.lvl_yr[0], I.qat_grid, I.qat_bits, t_begin, t_end,
+                             max_bits);
     });
 }
 void qat_copy_back(Impl& I) {

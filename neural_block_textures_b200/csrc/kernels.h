@@ -99,6 +99,11 @@ struct LatAdam {              // Adam on the texels a gather produces (latent, m
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
                        int rows_per_block, int ty0, int ty1, int row_base, const LatAdam& adam);
+// Tensor-core selector search (one bit depth for every level-0 channel, uniform cw x ch pixel cells, the fixed shapes
+// with their compile-time level layout, (2^bits) cw ch <= 32 rows per texel); false when it does not apply (nothing
+// launched). err: device flag set when an MMA completion wait timed out.
+bool launch_qat_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt, const float* grid,
+                   int bits, int cw, int ch, long long t_begin, long long t_end, int* err);
 void launch_qat(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt,
                 const int* xr0, const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end,
                 int max_bits);

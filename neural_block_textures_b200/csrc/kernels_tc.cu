@@ -37,6 +37,7 @@
 #include "tc.cuh"
 #include "latent_features.cuh"
 #include "fixed_layout.cuh"
+#include "quant.cuh"
 
 #include <algorithm>
 #include <type_traits>
@@ -57,66 +58,182 @@ __host__ __device__ constexpr int kmajor(int n, int k, int K) { return (n >> 3) 
 
 template <class S>
 struct TcShape {
-    static constexpr int K1 = round_up(S::NIN + 1, 8);
+    // Layer-1 bias: a column of X (X = [features | 1 | 0 pad]) when the features leave padding in their 8-wide K step,
+    // otherwise (8 features) a K step of its own against the constant block (below), which keeps X at 8 columns.
+    static constexpr bool XB = S::NIN % 8 != 0;
+    static constexpr int K1 = round_up(S::NIN + (XB ? 1 : 0), 8);
     static constexpr int N1 = round_up(S::H1, 16);
     static constexpr int K2 = S::H1;
-    static constexpr int N2 = round_up(S::H2, 16);
     static constexpr int K3 = S::H2;
     static constexpr int N3 = round_up(S::NOUT, 16);
     static constexpr int NOUTP = round_up(S::NOUT, 4);
-    static_assert(S::H1 % 8 == 0 && S::H2 % 8 == 0, "hidden widths must be multiples of 8");
-    static_assert(N1 <= 32 && N2 <= 32 && N3 <= 16, "accumulators wider than their reserved TMEM columns");
-    // shared memory, floats, per sign
-    static constexpr int oB1h = 0, oB1l = oB1h + N1 * K1;
-    static constexpr int oB2h = oB1l + N1 * K1, oB2l = oB2h + N2 * K2;
-    static constexpr int ob1 = oB2l + N2 * K2;                 // b1 [H2]
-    static constexpr int oW2 = round_up(ob1 + S::H2, 4);      // W2 [NOUT][H2], the reference's row-major order
-    static constexpr int ob2 = oW2 + S::NOUT * S::H2;         // b2 [NOUTP]
-    static_assert(S::H2 % 4 == 0, "output-layer rows are read as float4");
-    static constexpr int oB3h = round_up(ob2 + NOUTP, 4), oB3l = oB3h + N3 * K3;   // W2 as an MMA B operand
-    // b1 as an extra K step of layer 2: B block [N2][8] K-major with b1 in k = 0 (hi / lo), against a constant
-    // A block (column 0 = 1, columns 1-7 = 0) that every stream of the CTA shares
-    static constexpr int oBbh = oB3l + N3 * K3, oBbl = oBbh + N2 * 8;
-    static constexpr int SIGN = round_up(oBbl + N2 * 8, 32);
-    // TMEM columns: D (layers 1 and 2), D3 (output layer), X hi / lo, H hi / lo
     // The output layer runs on the tensor core for wide outputs (12: measured 1.33 vs 1.52 ms at config 3)
     // and on the FP32 pipe for 3 outputs (0.86 vs 1.03 ms at config 2), where 16-wide MMAs are mostly padding.
     static constexpr bool L3TC = S::NOUT > 4;
+    // FP32 output layer: layer 2 also produces W2 h2 (the output layer's linear part) in NLIN extra accumulator columns.
+    static constexpr int NLIN = L3TC ? 0 : S::NOUT;
+    static constexpr int N2 = round_up(S::H2 + NLIN, 16);
+    static constexpr int D2COLS = round_up(S::H2 + NLIN, 4);   // accumulator columns the layer-2 epilogue loads
+    static constexpr int P = S::H1 * S::NIN + S::H1 + S::H2 * S::H1 + S::H2 + S::NOUT * S::H2 + S::NOUT;
+    static_assert(S::H1 % 8 == 0 && S::H2 % 8 == 0, "hidden widths must be multiples of 8");
+    static_assert(N1 <= 32 && N2 <= 32 && N3 <= 16, "accumulators wider than their reserved TMEM columns");
+    // shared memory, floats, per weight set (sign)
+    static constexpr int oB1h = 0, oB1l = oB1h + N1 * K1;           // layer 1: [W0 | b0] (W0 alone without XB)
+    static constexpr int oB2h = oB1l + N1 * K1, oB2l = oB2h + N2 * K2;   // layer 2, H step: c1 W1 (+ W2 c1 W1 rows)
+    static constexpr int oB2xh = oB2l + N2 * K2, oB2xl = oB2xh + N2 * K1;   // layer 2, X step: leak W1 [W0 | b0] (+ W2 rows)
+    static constexpr int ob1 = oB2xl + N2 * K1;                     // b1 [H2]
+    static constexpr int oW2 = round_up(ob1 + S::H2, 4);            // FP32 output layer: c1 W2 [NOUT][H2], row-major
+    static constexpr int ob2 = oW2 + S::NOUT * S::H2;               // b2 [NOUTP]
+    static_assert(S::H2 % 4 == 0, "output-layer rows are read as float4");
+    static constexpr int oB3h = round_up(ob2 + NOUTP, 4), oB3l = oB3h + N3 * K3;   // W2 as an MMA B operand
+    // b1 as an extra K step of layer 2: B block [N2][8] K-major with b1 (and W2 b1) in k = 0 (hi / lo), against a
+    // constant A block (column 0 = 1, columns 1-7 = 0) that every stream of the CTA shares
+    static constexpr int oBbh = oB3l + N3 * K3, oBbl = oBbh + N2 * 8;
+    static constexpr int oB0h = oBbl + N2 * 8, oB0l = oB0h + N1 * 8;   // layer-1 bias step without XB: b0 in k = 0
+    static constexpr int oRaw = oB0l + N1 * 8;                      // the set's flat weights (staging input)
+    static constexpr int SIGN = round_up(oRaw + P, 32);
     // TMEM columns of one stream: D (layers 1 and 2), D3 (tensor output layer only), X and H as A operands, each
-    // split into hi / lo and interleaved by 8-column K steps ([hi 8 | lo 8] per step: one 16-column store per step)
+    // split into hi / lo and interleaved by 8-column K steps ([hi 8 | lo 8] per step)
     static constexpr int cD = 0, cD3 = 32, cX = L3TC ? 48 : 32, cH = cX + 2 * K1;
     static constexpr int COLS = cH + 2 * K2;
-    // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread;
-    // 4 streams is the floor the kernels were tuned at). Measured: 2 streams cost +33 % over 4.
-    static constexpr int STREAMS = kTmemCols / COLS >= 5 ? 5 : 4;
+    // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread, enough
+    // for up to 6 features; 4 streams is the floor the kernels were tuned at). Measured: 2 streams cost +33 % over 4.
+    static constexpr int STREAMS = (kTmemCols / COLS >= 5 && S::NIN <= 6) ? 5 : 4;
     static constexpr int TPB = kTcRows * STREAMS;
     static_assert(STREAMS * COLS <= kTmemCols, "TMEM columns");
-    // Layer-2 bias on the tensor core when the streams leave 8 TMEM columns for the constant block (every 3-output
-    // shape); otherwise (12 outputs: all 512 columns in use) it is added in the epilogue.
-    static constexpr bool B1TC = !L3TC && STREAMS * COLS + 8 <= kTmemCols;
+    // Layer-2 bias (and, without XB, the layer-1 bias) on the tensor core when the streams leave 8 TMEM columns for the
+    // constant block; otherwise b1 is added in the epilogue.
+    static constexpr bool B1TC = STREAMS * COLS + 8 <= kTmemCols;
+    static_assert(L3TC || B1TC, "the FP32 output layer's linear part needs the layer-2 bias on the tensor core");
+    static_assert(XB || B1TC, "the layer-1 bias step needs the constant block");
     static constexpr int cOne = STREAMS * COLS;   // the constant block's first column (from the CTA's TMEM base)
-
-    // Writes flat reference weight k (value w) to every place a kernel variant reads it from: MMA B operands
-    // as hi / lo, biases and the row-major output layer as plain floats.
-    __device__ static void store(float* sw, int k, float w) {
-        const float hi = tc::tf32_hi(w), lo = w - hi;
-        if (k < S::H1 * S::NIN) { const int j = k / S::NIN, i = k - j * S::NIN; sw[oB1h + kmajor(j, i, K1)] = hi; sw[oB1l + kmajor(j, i, K1)] = lo; return; }
-        k -= S::H1 * S::NIN;
-        if (k < S::H1) { sw[oB1h + kmajor(k, S::NIN, K1)] = hi; sw[oB1l + kmajor(k, S::NIN, K1)] = lo; return; }
-        k -= S::H1;
-        if (k < S::H2 * S::H1) { const int j = k / S::H1, i = k - j * S::H1; sw[oB2h + kmajor(j, i, K2)] = hi; sw[oB2l + kmajor(j, i, K2)] = lo; return; }
-        k -= S::H2 * S::H1;
-        if (k < S::H2) { sw[ob1 + k] = w; sw[oBbh + kmajor(k, 0, 8)] = hi; sw[oBbl + kmajor(k, 0, 8)] = lo; return; }
-        k -= S::H2;
-        if (k < S::NOUT * S::H2) {
-            const int o = k / S::H2, j = k - o * S::H2;
-            sw[oW2 + k] = w; sw[oB3h + kmajor(o, j, K3)] = hi; sw[oB3l + kmajor(o, j, K3)] = lo;
-            return;
-        }
-        k -= S::NOUT * S::H2;
-        sw[ob2 + k] = w;
-    }
 };
+
+// ---- weight staging: leaky ReLU folded into the operands
+// For any slope l, leaky(x) = l x + c1 (x + |x|) with c1 = (1 - l) / 2, and x + |x| = 2 relu(x) exactly, which is
+// one add with an absolute-value operand on the FP32 pipe (no multiply, no ALU max). So
+//   h2 = W1 leaky(h1) + b1 = (c1 W1) (h1 + |h1|) + (l W1 W0) x + (l W1 b0 + b1)        (h1 = W0 x + b0)
+// layer 2 takes A = split(h1 + |h1|) against B = c1 W1 (the H step) plus A = X against B = l W1 [W0 | b0] (one more
+// 8-wide K step on the features already in TMEM), and for the FP32 output layer
+//   out = b2 + W2 leaky(h2) = b2 + l (W2 h2) + (c1 W2) (h2 + |h2|)
+// where W2 h2 comes out of layer 2 itself: B rows H2 .. H2 + NOUT hold W2 times the rows above them (W2 c1 W1,
+// W2 l W1 [W0 | b0], W2 b1), filling the accumulator's padding columns.
+template <class S>
+__device__ __forceinline__ void put_split(float* sw, int oh, int ol, int idx, float w) {
+    const float hi = tc::tf32_hi(w);
+    sw[oh + idx] = hi;
+    sw[ol + idx] = w - hi;
+}
+
+// Row j < H2 of the layer-2 bias step: b1 (+ l W1 b0 when b0 is not a column of X).
+template <class S>
+__device__ __forceinline__ float bias2_row(const float* W1, const float* b0, const float* b1, float leak, int j) {
+    if constexpr (TcShape<S>::XB) {
+        return b1[j];
+    } else {
+        float v = 0.0f;
+        for (int q = 0; q < S::H1; q++) v = fmaf(W1[j * S::H1 + q], b0[q], v);
+        return fmaf(leak, v, b1[j]);
+    }
+}
+
+// Phase A of staging one weight set from its flat weights at sw + oRaw (the reference layout, main.cpp:549-599):
+// every derived value that needs only the flat weights. Threads tid, tid + nthr, ... of the set's staging group.
+template <class S>
+__device__ __forceinline__ void stage_set_a(float* sw, float leak, int tid, int nthr) {
+    using T = TcShape<S>;
+    const float* W0 = sw + T::oRaw;
+    const float* b0 = W0 + S::H1 * S::NIN;
+    const float* W1 = b0 + S::H1;
+    const float* b1 = W1 + S::H2 * S::H1;
+    const float* W2 = b1 + S::H2;
+    const float* b2 = W2 + S::NOUT * S::H2;
+    const float c1 = 0.5f * (1.0f - leak);
+    constexpr int XC = S::NIN + (T::XB ? 1 : 0);   // X columns with weights: the features (and the bias column)
+    constexpr int nB1 = S::H1 * XC, nB0 = T::XB ? 0 : S::H1, nB2 = (S::H2 + T::NLIN) * S::H1, nB2x = S::H2 * XC;
+    constexpr int nBb = T::B1TC ? S::H2 + T::NLIN : 0, nW2 = S::NOUT * S::H2, nb = S::H2 + S::NOUT;
+    constexpr int total = nB1 + nB0 + nB2 + nB2x + nBb + nW2 + nb;
+    for (int e = tid; e < total; e += nthr) {
+        int k = e;
+        if (k < nB1) {                        // layer 1: [W0 | b0], or W0
+            const int j = k / XC, i = k - j * XC;
+            put_split<S>(sw, T::oB1h, T::oB1l, kmajor(j, i, T::K1), i < S::NIN ? W0[j * S::NIN + i] : b0[j]);
+            continue;
+        }
+        k -= nB1;
+        if (k < nB0) {                        // layer-1 bias step: b0
+            put_split<S>(sw, T::oB0h, T::oB0l, kmajor(k, 0, 8), b0[k]);
+            continue;
+        }
+        k -= nB0;
+        if (k < nB2) {                        // layer 2, H step: c1 W1, then the output rows W2 (c1 W1)
+            const int j = k / S::H1, i = k - j * S::H1;
+            float v;
+            if (j < S::H2) {
+                v = c1 * W1[j * S::H1 + i];
+            } else {
+                const int c = j - S::H2;
+                v = 0.0f;
+                for (int q = 0; q < S::H2; q++) v = fmaf(W2[c * S::H2 + q], c1 * W1[q * S::H1 + i], v);
+            }
+            put_split<S>(sw, T::oB2h, T::oB2l, kmajor(j, i, T::K2), v);
+            continue;
+        }
+        k -= nB2;
+        if (k < nB2x) {                       // layer 2, X step: l W1 [W0 | b0], or l W1 W0
+            const int j = k / XC, i = k - j * XC;
+            float v = 0.0f;
+            for (int q = 0; q < S::H1; q++) v = fmaf(W1[j * S::H1 + q], i < S::NIN ? W0[q * S::NIN + i] : b0[q], v);
+            put_split<S>(sw, T::oB2xh, T::oB2xl, kmajor(j, i, T::K1), leak * v);
+            continue;
+        }
+        k -= nB2x;
+        if (k < nBb) {                        // layer-2 bias step: its rows, then W2 times them
+            float v;
+            if (k < S::H2) {
+                v = bias2_row<S>(W1, b0, b1, leak, k);
+            } else {
+                const int c = k - S::H2;
+                v = 0.0f;
+                for (int q = 0; q < S::H2; q++) v = fmaf(W2[c * S::H2 + q], bias2_row<S>(W1, b0, b1, leak, q), v);
+            }
+            put_split<S>(sw, T::oBbh, T::oBbl, kmajor(k, 0, 8), v);
+            continue;
+        }
+        k -= nBb;
+        if (k < nW2) {                        // output layer: c1 W2 (FP32 pipe), or W2 as an MMA operand and as floats
+            if constexpr (T::L3TC) {
+                const int o = k / S::H2, j = k - o * S::H2;
+                put_split<S>(sw, T::oB3h, T::oB3l, kmajor(o, j, T::K3), W2[k]);
+                sw[T::oW2 + k] = W2[k];
+            } else {
+                sw[T::oW2 + k] = c1 * W2[k];
+            }
+            continue;
+        }
+        k -= nW2;
+        if (k < S::H2) sw[T::ob1 + k] = b1[k];
+        else sw[T::ob2 + k - S::H2] = b2[k - S::H2];
+    }
+}
+
+// Phase B: the output rows of the X step, W2 (l W1 [W0 | b0]), from phase A's values (hi + lo = the exact float).
+template <class S>
+__device__ __forceinline__ void stage_set_b(float* sw, int tid, int nthr) {
+    using T = TcShape<S>;
+    const float* W2 = sw + T::oRaw + S::H1 * S::NIN + S::H1 + S::H2 * S::H1 + S::H2;
+    constexpr int XC = S::NIN + (T::XB ? 1 : 0);
+    constexpr int n = T::NLIN * XC;
+    for (int e = tid; e < n; e += nthr) {
+        const int c = e / XC, i = e - c * XC;
+        float v = 0.0f;
+        for (int q = 0; q < S::H2; q++) {
+            const int at = kmajor(q, i, T::K1);
+            v = fmaf(W2[c * S::H2 + q], sw[T::oB2xh + at] + sw[T::oB2xl + at], v);
+        }
+        put_split<S>(sw, T::oB2xh, T::oB2xl, kmajor(S::H2 + c, i, T::K1), v);
+    }
+}
 
 __device__ __forceinline__ bool elect_one() {
     uint32_t p = 0;
@@ -128,9 +245,6 @@ __device__ __forceinline__ float rcp_approx(float x) {
     float r;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
-}
-__device__ __forceinline__ float out_act_fast(float s, int clamp_out) {
-    return clamp_out ? fminf(fmaxf(s, 0.0f), 1.0f) : rcp_approx(1.0f + __expf(-s));
 }
 // Leaky ReLU of a pair; for 0 <= leak <= 1 (the only slopes the compiled shapes admit) max(x, leak x)
 // equals the reference's select for every float.
@@ -157,18 +271,24 @@ __device__ __forceinline__ void store_split(uint32_t trow, int c, const float* v
         tc::st_x8p(trow + c + 2 * q + 8, hl + 8);
     }
 }
-// N (multiple of 8) accumulator columns from TMEM column c into v, in as few loads as the widths allow.
+// N (multiple of 4) accumulator columns from TMEM column c into v, in as few loads as the widths allow.
 template <int N>
 __device__ __forceinline__ void load_acc(uint32_t trow, int c, float* v) {
+    static_assert(N % 4 == 0, "accumulator columns in fours");
 #pragma unroll
     for (int q = 0; q + 16 <= N; q += 16) tc::ld_x16p(trow + c + q, v + q);
-    if constexpr (N % 16 != 0) tc::ld_x8p(trow + c + (N / 16) * 16, v + (N / 16) * 16);
+    constexpr int r = N / 16 * 16;
+    if constexpr (N % 16 >= 8) tc::ld_x8p(trow + c + r, v + r);
+    if constexpr (N % 8 == 4) tc::ld_x4p(trow + c + N - 4, v + N - 4);
 }
 
-// Output layer + weighted squared error of one row on the FP32 pipe, from the layer-2 accumulator row h
-// (b1 not yet added): hidden units in pairs (packed bias, activation and products), two partial sums per
-// output, float error sum over the channels.
-template <class S>
+// Output layer + weighted squared error of one row on the FP32 pipe, from the layer-2 accumulator row h: h[0 .. H2)
+// = h2 (b1 included), h[H2 + c] = (W2 h2)_c. out_c = b2_c + l (W2 h2)_c + sum_j (c1 W2)_cj (h2_j + |h2_j|) (the folded
+// leaky ReLU: one add per hidden unit), hidden units in pairs, two partial sums per output, float error sum.
+// Shapes whose population kernel runs the output layer on the tensor core (L3TC) have no W2 h2 columns: there the
+// FP32 form (the latent pass) applies the leaky ReLU to h2 as written (adding b1 when the tensor core has not), with
+// the plain W2.
+template <class S, bool CLAMP>
 __device__ __forceinline__ float out_layer_error(const DevModel& m, const float* ws, const float* h, const float* t,
                                                  float leak) {
     using T = TcShape<S>;
@@ -177,29 +297,44 @@ __device__ __forceinline__ float out_layer_error(const DevModel& m, const float*
     for (int c = 0; c < S::NOUT; c++) acc[c] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int j = 0; j < S::H2; j += 4) {
-        float2 h0, h1;
-        if constexpr (T::B1TC) {   // b1 already in the accumulator
-            h0 = leaky_pair(make_float2(h[j], h[j + 1]), leak);
-            h1 = leaky_pair(make_float2(h[j + 2], h[j + 3]), leak);
+        float2 r0, r1;
+        if constexpr (T::L3TC) {
+            r0 = make_float2(h[j], h[j + 1]);
+            r1 = make_float2(h[j + 2], h[j + 3]);
+            if constexpr (!T::B1TC) {
+                const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
+                r0 = __fadd2_rn(r0, make_float2(b.x, b.y));
+                r1 = __fadd2_rn(r1, make_float2(b.z, b.w));
+            }
+            r0 = leaky_pair(r0, leak);
+            r1 = leaky_pair(r1, leak);
         } else {
-            const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
-            h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak);
-            h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
+            r0 = make_float2(h[j] + fabsf(h[j]), h[j + 1] + fabsf(h[j + 1]));
+            r1 = make_float2(h[j + 2] + fabsf(h[j + 2]), h[j + 3] + fabsf(h[j + 3]));
         }
 #pragma unroll
         for (int c = 0; c < S::NOUT; c++) {
             const float4 w = *reinterpret_cast<const float4*>(ws + T::oW2 + c * S::H2 + j);
-            acc[c] = __ffma2_rn(make_float2(w.x, w.y), h0, acc[c]);
-            acc[c] = __ffma2_rn(make_float2(w.z, w.w), h1, acc[c]);
+            acc[c] = __ffma2_rn(make_float2(w.x, w.y), r0, acc[c]);
+            acc[c] = __ffma2_rn(make_float2(w.z, w.w), r1, acc[c]);
         }
     }
     float e = 0.0f;
 #pragma unroll
     for (int c = 0; c < S::NOUT; c++) {
-        const float d = out_act_fast(ws[T::ob2 + c] + (acc[c].x + acc[c].y), m.clamp_out) - t[c];
+        float sum = ws[T::ob2 + c] + (acc[c].x + acc[c].y);
+        if constexpr (!T::L3TC) sum = fmaf(leak, h[S::H2 + c], sum);
+        const float o = CLAMP ? fminf(fmaxf(sum, 0.0f), 1.0f) : rcp_approx(1.0f + __expf(-sum));
+        const float d = o - t[c];
         e = fmaf(m.cw[c], d * d, e);
     }
     return e;
+}
+// The layer-1 epilogue's operand for layer 2: h1 + |h1| (= 2 relu(h1)), in place.
+template <int N>
+__device__ __forceinline__ void relu2(float* h) {
+#pragma unroll
+    for (int j = 0; j < N; j++) h[j] = h[j] + fabsf(h[j]);
 }
 
 // Warp 0 (converged): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K step), then commit. a: the
@@ -220,13 +355,14 @@ __device__ __forceinline__ void issue3(uint32_t d, uint32_t a, uint32_t b_hi4, u
     __syncwarp();
 }
 
-// Layer 2 of a shape with B1TC: the 3xTF32 product over K, then D += 1 * b1_lo + 1 * b1_hi from the constant A
-// block `one` (its lo part is zero), then commit.
-template <int K, int N>
-__device__ __forceinline__ void issue3_bias(uint32_t d, uint32_t a, uint32_t b_hi4, uint32_t b_lo4, uint32_t one, uint32_t bb_hi4,
-                                            uint32_t bb_lo4, uint64_t* bar) {
+// Layer 2: the 3xTF32 product of the H step over K (A = split(h1 + |h1|)), then the X step over KX (A = the features,
+// B = l W1 [W0 | b0]), then with B1TC D += 1 * b1_lo + 1 * b1_hi from the constant A block `one` (its lo part is
+// zero), then commit.
+template <int K, int KX, int N, bool BIAS>
+__device__ __forceinline__ void issue_l2(uint32_t d, uint32_t a, uint32_t b_hi4, uint32_t b_lo4, uint32_t ax, uint32_t bx_hi4,
+                                         uint32_t bx_lo4, uint32_t one, uint32_t bb_hi4, uint32_t bb_lo4, uint64_t* bar) {
     constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
-    constexpr uint32_t sbo = (uint32_t)K * 32u;
+    constexpr uint32_t sbo = (uint32_t)K * 32u, sbox = (uint32_t)KX * 32u;
     tc::fence_after_sync();
 #pragma unroll
     for (int s = 0; s < K / 8; s++) {
@@ -234,8 +370,16 @@ __device__ __forceinline__ void issue3_bias(uint32_t d, uint32_t a, uint32_t b_h
         if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
         if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
     }
-    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_lo4, 128, 256), id, 1u);
-    if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_hi4, 128, 256), id, 1u);
+#pragma unroll
+    for (int s = 0; s < KX / 8; s++) {
+        if (elect_one()) tc::mma_tf32_ts(d, ax + 16 * s + 8, tc::sdesc_s4(bx_hi4 + 16 * s, 128, sbox), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, ax + 16 * s, tc::sdesc_s4(bx_lo4 + 16 * s, 128, sbox), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, ax + 16 * s, tc::sdesc_s4(bx_hi4 + 16 * s, 128, sbox), id, 1u);
+    }
+    if constexpr (BIAS) {
+        if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_lo4, 128, 256), id, 1u);
+        if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_hi4, 128, 256), id, 1u);
+    }
     if (elect_one()) tc::commit(bar);
     __syncwarp();
 }
@@ -246,17 +390,19 @@ constexpr uint32_t s4() { static_assert(FLOATS % 4 == 0, "B operand blocks are 1
 
 // Layer 1 of unit (A = X of the stream, B = the sign's W0 | b0 block); sb4 = the sign's weight set address >> 4.
 template <class T>
-__device__ __forceinline__ void issue_layer1(uint32_t tb, uint32_t sb4, uint64_t* bar) {
-    issue3<T::K1, T::N1>(tb + T::cD, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), bar);
+__device__ __forceinline__ void issue_layer1(uint32_t tbase, uint32_t tb, uint32_t sb4, uint64_t* bar) {
+    if constexpr (T::XB)
+        issue3<T::K1, T::N1>(tb + T::cD, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), bar);
+    else   // the features over K1, then b0 against the constant block
+        issue_l2<T::K1, 0, T::N1, true>(tb + T::cD, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), 0, 0, 0, tbase + T::cOne,
+                                        sb4 + s4<T::oB0h>(), sb4 + s4<T::oB0l>(), bar);
 }
-// Layer 2 of unit (A = H of the stream, B = the sign's W1 and b1 blocks).
+// Layer 2 of unit (A = H and X of the stream, B = the sign's H-step, X-step and bias blocks).
 template <class T>
 __device__ __forceinline__ void issue_layer2(uint32_t tbase, uint32_t tb, uint32_t sb4, uint64_t* bar) {
-    if constexpr (T::B1TC)
-        issue3_bias<T::K2, T::N2>(tb + T::cD, tb + T::cH, sb4 + s4<T::oB2h>(), sb4 + s4<T::oB2l>(), tbase + T::cOne,
-                                  sb4 + s4<T::oBbh>(), sb4 + s4<T::oBbl>(), bar);
-    else
-        issue3<T::K2, T::N2>(tb + T::cD, tb + T::cH, sb4 + s4<T::oB2h>(), sb4 + s4<T::oB2l>(), bar);
+    issue_l2<T::K2, T::K1, T::N2, T::B1TC>(tb + T::cD, tb + T::cH, sb4 + s4<T::oB2h>(), sb4 + s4<T::oB2l>(), tb + T::cX,
+                                            sb4 + s4<T::oB2xh>(), sb4 + s4<T::oB2xl>(), tbase + T::cOne, sb4 + s4<T::oBbh>(),
+                                            sb4 + s4<T::oBbl>(), bar);
 }
 
 // The constant A block of the layer-2 bias step: TMEM column cOne = 1, cOne + 1 .. + 7 = 0 on all 128 lanes,
@@ -297,7 +443,7 @@ __device__ __forceinline__ double stream_sum(double v, double* red4, int id) {
 // weight sets, and works through a contiguous range of the (pair, chunk) items, so consecutive items
 // mostly share a pair and its weights are staged once. The streams interleave on the SM: one stream's
 // element-wise work overlaps the others' MMAs.
-template <class S, bool L3TC>
+template <class S, bool L3TC, bool CLAMP>
 __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, PopArgs a, int chunks) {
     using T = TcShape<S>;
     constexpr int NS = T::STREAMS;
@@ -372,12 +518,18 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
             // stage both perturbed weight sets of this pair (the previous pair's MMAs have all completed)
             const int cand = pop_cand(a, pl);
             const float* e = (a.mode == 0 && a.sigma != 0.0f) ? a.eps + (long long)pl * m.P : nullptr;
-            for (int k = tid; k < m.P; k += kTcRows) {
+            for (int k = tid; k < T::P; k += kTcRows) {
                 float wp, wm;
                 perturbed_weight(a, e, k, cand, wp, wm);
-                T::store(sw, k, wp);
-                T::store(sw + T::SIGN, k, wm);
+                sw[T::oRaw + k] = wp;
+                sw[T::SIGN + T::oRaw + k] = wm;
             }
+            stream_sync(bar_id);
+            stage_set_a<S>(sw, leak, tid, kTcRows);
+            stage_set_a<S>(sw + T::SIGN, leak, tid, kTcRows);
+            stream_sync(bar_id);
+            stage_set_b<S>(sw, tid, kTcRows);
+            stage_set_b<S>(sw + T::SIGN, tid, kTcRows);
             tc::fence_proxy_async_smem();
             cur = pl;
         }
@@ -392,7 +544,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == issuer) issue_layer1<T>(tb, sb0, bar);
+        if (warp == issuer) issue_layer1<T>(tbase, tb, sb0, bar);
 
 #pragma unroll 1
         for (int base = row0; base < row1; base += kTcRows) {
@@ -409,25 +561,21 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
             for (int sg = 0; sg < 2; sg++) {
                 const uint32_t sb = sg ? sb1 : sb0;
                 const float* ws = sw + sg * T::SIGN;
-                float h[S::H1 > S::H2 ? S::H1 : S::H2];
-                // layer 1 result -> H
+                float h[S::H1 > T::D2COLS ? S::H1 : T::D2COLS];
+                // layer 1 result -> H (h1 + |h1|, the folded leaky ReLU)
                 wait_mma();
                 load_acc<S::H1>(trow, T::cD, h);
                 tc::wait_ld();
-#pragma unroll
-                for (int j = 0; j < S::H1; j += 2) {
-                    const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak);
-                    h[j] = v.x; h[j + 1] = v.y;
-                }
+                relu2<S::H1>(h);
                 store_split<T::K2>(trow, T::cH, h);
                 tc::wait_st();
                 tc::fence_before_sync();
                 ok = stream_sync_and(bar_id, ok);
                 if (!ok) break;
                 if (warp == issuer) issue_layer2<T>(tbase, tb, sb, bar);
-                // layer 2 result -> registers
+                // layer 2 result -> registers (with the FP32 output layer: h2 and W2 h2)
                 wait_mma();
-                load_acc<S::H2>(trow, T::cD, h);
+                load_acc<L3TC ? S::H2 : T::D2COLS>(trow, T::cD, h);
                 tc::wait_ld();
                 // next unit's layer 1: the other sign of this tile, or the next tile's + sign
                 const bool next = sg == 0 || more;
@@ -436,9 +584,14 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     // (into D) go out together as two commits
 #pragma unroll
                     for (int j = 0; j < S::H2; j += 4) {
-                        const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
-                        const float2 h0 = leaky_pair(__fadd2_rn(make_float2(h[j], h[j + 1]), make_float2(b.x, b.y)), leak);
-                        const float2 h1 = leaky_pair(__fadd2_rn(make_float2(h[j + 2], h[j + 3]), make_float2(b.z, b.w)), leak);
+                        float2 h0 = make_float2(h[j], h[j + 1]), h1 = make_float2(h[j + 2], h[j + 3]);
+                        if constexpr (!T::B1TC) {
+                            const float4 b = *reinterpret_cast<const float4*>(ws + T::ob1 + j);
+                            h0 = __fadd2_rn(h0, make_float2(b.x, b.y));
+                            h1 = __fadd2_rn(h1, make_float2(b.z, b.w));
+                        }
+                        h0 = leaky_pair(h0, leak);
+                        h1 = leaky_pair(h1, leak);
                         h[j] = h0.x; h[j + 1] = h0.y; h[j + 2] = h1.x; h[j + 3] = h1.y;
                     }
                     store_split<T::K3>(trow, T::cH, h);
@@ -449,7 +602,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     if (!ok) break;
                     if (warp == issuer) {
                         issue3<T::K3, T::N3>(tb + T::cD3, tb + T::cH, sb + s4<T::oB3h>(), sb + s4<T::oB3l>(), bar3);
-                        if (next) issue_layer1<T>(tb, sg ? sb0 : sb1, bar);
+                        if (next) issue_layer1<T>(tbase, tb, sg ? sb0 : sb1, bar);
                     }
                     wait_mma3();
                     float o[T::NOUTP];
@@ -459,7 +612,8 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     float e = 0.0f;
 #pragma unroll
                     for (int c = 0; c < S::NOUT; c++) {
-                        const float d = out_act_fast(o[c] + ws[T::ob2 + c], m.clamp_out) - t[c];
+                        const float sum = o[c] + ws[T::ob2 + c];
+                        const float d = (CLAMP ? fminf(fmaxf(sum, 0.0f), 1.0f) : rcp_approx(1.0f + __expf(-sum))) - t[c];
                         e = fmaf(m.cw[c], d * d, e);
                     }
                     if (valid) { if (sg == 0) acc_p += (double)e; else acc_m += (double)e; }
@@ -472,9 +626,10 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     tc::fence_before_sync();
                     ok = stream_sync_and(bar_id, ok);
                     if (!ok) break;
-                    if (next && warp == issuer) issue_layer1<T>(tb, sg ? sb0 : sb1, bar);
+                    if (next && warp == issuer) issue_layer1<T>(tbase, tb, sg ? sb0 : sb1, bar);
                     // output layer and error of this unit, overlapping the tensor core's next layer 1
-                    const double e = valid ? (double)out_layer_error<S>(m, ws, h, t, leak) : 0.0;
+                    double e = 0.0;
+                    if constexpr (!L3TC) e = valid ? (double)out_layer_error<S, CLAMP>(m, ws, h, t, leak) : 0.0;
                     if (sg == 0) acc_p += e; else acc_m += e;
                 }
             }
@@ -507,10 +662,15 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
     const size_t smem = (size_t)T::STREAMS * 2 * T::SIGN * sizeof(float);
     constexpr bool kL3TC = T::L3TC;
     const int nsm = device_sm_count();
-    ensure_dynamic_smem((const void*)k_pop_eval_tc<S, kL3TC>, (int)smem);
     const long long items = (long long)a.ncand * chunks;
     const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
-    k_pop_eval_tc<S, kL3TC><<<grid, T::TPB, smem, s>>>(m, a, chunks);
+    if (m.clamp_out) {
+        ensure_dynamic_smem((const void*)k_pop_eval_tc<S, kL3TC, true>, (int)smem);
+        k_pop_eval_tc<S, kL3TC, true><<<grid, T::TPB, smem, s>>>(m, a, chunks);
+    } else {
+        ensure_dynamic_smem((const void*)k_pop_eval_tc<S, kL3TC, false>, (int)smem);
+        k_pop_eval_tc<S, kL3TC, false><<<grid, T::TPB, smem, s>>>(m, a, chunks);
+    }
 }
 
 // ---------------------------------------------------------------------------------------------------------
@@ -523,7 +683,7 @@ void launch_tc(cudaStream_t s, const DevModel& m, const PopArgs& a) {
 // 128-pixel tile), its two units are the + and - decodes of the tile (X = the +/- perturbed features, which
 // share their taps and are gathered together, one item ahead, while the layer-2 MMAs of the current item
 // run). The output layer runs on the FP32 pipe.
-template <class S, class LY>
+template <class S, class LY, bool CLAMP>
 __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, const float* __restrict__ wg, const float* __restrict__ z,
                                                          const float* __restrict__ eps, long long nz, const float* __restrict__ tgt,
                                                          int K, unsigned active, float sg, float inv_px, float* __restrict__ dpix,
@@ -545,7 +705,11 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
     if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
     for (int i = threadIdx.x; i < T::SIGN; i += T::TPB) sw[i] = 0.0f;
     __syncthreads();
-    for (int k = threadIdx.x; k < m.P; k += T::TPB) T::store(sw, k, wg[k]);
+    for (int k = threadIdx.x; k < T::P; k += T::TPB) sw[T::oRaw + k] = wg[k];
+    __syncthreads();
+    stage_set_a<S>(sw, m.leak, threadIdx.x, T::TPB);
+    __syncthreads();
+    stage_set_b<S>(sw, threadIdx.x, T::TPB);
     tc::fence_proxy_async_smem();
     init_one_block<T>(tbase, g, warp);
     tc::fence_before_sync();
@@ -600,11 +764,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         wait_mma();
         load_acc<S::H1>(trow, T::cD, h);
         tc::wait_ld();
-#pragma unroll
-        for (int j = 0; j < S::H1; j += 2) {
-            const float2 v = leaky_pair(make_float2(h[j], h[j + 1]), leak);
-            h[j] = v.x; h[j + 1] = v.y;
-        }
+        relu2<S::H1>(h);
         store_split<T::K2>(trow, T::cH, h);
         tc::wait_st();
         tc::fence_before_sync();
@@ -618,39 +778,39 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == issuer) issue_layer1<T>(tb, sb, bar);
+        if (warp == issuer) issue_layer1<T>(tbase, tb, sb, bar);
     }
 #pragma unroll 1
     for (long long item = i0; item < i1 && ok; item++) {
         const bool more = item + 1 < i1;
-        float h[S::H2];
+        float h[T::L3TC ? S::H2 : T::D2COLS];
         float np[S::NIN], nm[S::NIN], nt[S::NOUT];
         // + unit
         layer1_to_layer2();
         if (!ok) break;
         if (more) gather(item + 1, np, nm, nt);    // overlaps the layer-2 MMAs
         wait_mma();
-        load_acc<S::H2>(trow, T::cD, h);
+        load_acc<T::L3TC ? S::H2 : T::D2COLS>(trow, T::cD, h);
         tc::wait_ld();
         store_x(fm);
         tc::wait_st();
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
-        if (warp == issuer) issue_layer1<T>(tb, sb, bar);
-        const float ep = out_layer_error<S>(m, sw, h, t, leak);
+        if (warp == issuer) issue_layer1<T>(tbase, tb, sb, bar);
+        const float ep = out_layer_error<S, CLAMP>(m, sw, h, t, leak);
         // - unit
         layer1_to_layer2();
         if (!ok) break;
         wait_mma();
-        load_acc<S::H2>(trow, T::cD, h);
+        load_acc<T::L3TC ? S::H2 : T::D2COLS>(trow, T::cD, h);
         tc::wait_ld();
         if (more) { store_x(np); tc::wait_st(); }
         tc::fence_before_sync();
         ok = stream_sync_and(bar_id, ok);
         if (!ok) break;
-        if (more && warp == issuer) issue_layer1<T>(tb, sb, bar);
-        const float em = out_layer_error<S>(m, sw, h, t, leak);
+        if (more && warp == issuer) issue_layer1<T>(tbase, tb, sb, bar);
+        const float em = out_layer_error<S, CLAMP>(m, sw, h, t, leak);
         {
             const int k = (int)(item / ntiles);
             const long long p = p_begin + (item - (long long)k * ntiles) * kTcRows + tid;
@@ -670,6 +830,166 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
     if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, kTmemCols); }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// --qat selector search on the tensor core (qat_search, main.cpp:2088-2139; the reference's k_qat_search,
+// cuda/ntc_cuda.cu:451-492). For level-0 cells of cw x ch pixels (the image a whole multiple of the level, so every
+// texel's footprint is its cell) and n = 2^bits candidates per channel, one texel's candidates x pixels are
+// rpt = n cw ch consecutive rows of a 128-row tile (rpt a power of two <= 32, so one warp holds a texel), and a tile
+// covers 128 / rpt texels. Per channel, in order: every row decodes its pixel with the channel set to its candidate
+// (the MMA pipeline of the latent pass, one weight set), each candidate's cell loss is its pixels' errors summed in
+// raster order in double by warp shuffles, and the reference's rule (the current value first, a strictly smaller
+// loss wins, in index order) picks the value that is installed before the next channel is searched. The cell losses
+// carry the 3xTF32 rounding (~1e-6 relative), so near-ties can resolve differently from the exact kernel; the
+// reference's own harness accepts exactly that (main.cpp:3136-3146: differing texels within 1e-4 of each other, the
+// searched image's loss within 1e-6).
+template <class S, class LY, bool CLAMP>
+__global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_qat_tc(DevModel m, const float* __restrict__ wg, float* z,
+                                                               const float* __restrict__ tgt, const float* __restrict__ grid,
+                                                               int bits, int cw, int ch, long long t_begin, long long t_end,
+                                                               int* __restrict__ err) {
+    using T = TcShape<S>;
+    extern __shared__ __align__(1024) float sw[];   // one weight set [T::SIGN]
+    __shared__ __align__(8) uint64_t bars[T::STREAMS];
+    __shared__ uint32_t tbase;
+    const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5, lane = threadIdx.x & 31;
+    const int issuer = g & 3;
+    const int bar_id = 1 + g;
+    uint64_t* bar = &bars[g];
+
+    if (threadIdx.x < 32) tc::tmem_alloc(&tbase, kTmemCols);
+    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init_fence(); }
+    for (int i = threadIdx.x; i < T::SIGN; i += T::TPB) sw[i] = 0.0f;
+    __syncthreads();
+    for (int k = threadIdx.x; k < T::P; k += T::TPB) sw[T::oRaw + k] = wg[k];
+    __syncthreads();
+    stage_set_a<S>(sw, m.leak, threadIdx.x, T::TPB);
+    __syncthreads();
+    stage_set_b<S>(sw, threadIdx.x, T::TPB);
+    tc::fence_proxy_async_smem();
+    init_one_block<T>(tbase, g, warp);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+
+    const uint32_t tb = tbase + (uint32_t)(T::COLS * g);
+    const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+    const uint32_t sb = tc::smem_addr(sw) >> 4;
+    const float leak = m.leak;
+    uint32_t waited = 0;
+    bool ok = true;
+    auto wait_mma = [&]() {
+        const bool done = tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+        if (done) waited++;
+        ok = ok && done;
+        tc::fence_after_sync();
+    };
+
+    const DevLevel& L0 = m.lv[0];
+    const int n = 1 << bits, cellpix = cw * ch, rpt = n * cellpix, tpt = kTcRows / rpt;
+    const int slot = tid / rpt, local = tid - slot * rpt, k = local / cellpix, pi = local - k * cellpix;
+    const int group = lane & ~(rpt - 1);        // first lane of this texel's rows
+    const float* gv = grid + bits * 257;
+    const long long ntiles = (t_end - t_begin + tpt - 1) / tpt;
+    const long long nstreams = (long long)gridDim.x * T::STREAMS, gs = (long long)blockIdx.x * T::STREAMS + g;
+    const long long i0 = gs * ntiles / nstreams, i1 = (gs + 1) * ntiles / nstreams;
+
+#pragma unroll 1
+    for (long long tile = i0; tile < i1 && ok; tile++) {
+        const long long t = t_begin + tile * tpt + slot;
+        const bool live = t < t_end;
+        const long long tcl = live ? t : t_end - 1;   // rows past the end shadow the last texel and install nothing
+        const int tx = (int)(tcl % L0.W), ty = (int)(tcl / L0.W);
+        const int px = tx * cw + pi % cw, py = ty * ch + pi / cw;
+        float* zt = z + L0.off + tcl * L0.C;
+        float tt[S::NOUT];
+#pragma unroll
+        for (int c = 0; c < S::NOUT; c++) tt[c] = __ldg(tgt + ((long long)py * m.W + px) * S::NOUT + c);
+#pragma unroll 1
+        for (int c = 0; c < LY::C0; c++) {
+            // X = this row's features with channel c set to candidate k
+            {
+                float f[S::NIN];
+                layout_features<LY>(m, z, px, py, f);
+#pragma unroll
+                for (int i = 0; i < LY::C0; i++) if (i == c) f[i] = gv[k];
+                float x[T::K1];
+#pragma unroll
+                for (int i = 0; i < T::K1; i++) x[i] = i < S::NIN ? f[i] : (i == S::NIN ? 1.0f : 0.0f);
+                store_split<T::K1>(trow, T::cX, x);
+            }
+            tc::wait_st();
+            tc::fence_before_sync();
+            ok = stream_sync_and(bar_id, ok);
+            if (!ok) break;
+            if (warp == issuer) issue_layer1<T>(tbase, tb, sb, bar);
+            float h[S::H1 > T::D2COLS ? S::H1 : T::D2COLS];
+            wait_mma();
+            load_acc<S::H1>(trow, T::cD, h);
+            tc::wait_ld();
+            relu2<S::H1>(h);
+            store_split<T::K2>(trow, T::cH, h);
+            tc::wait_st();
+            tc::fence_before_sync();
+            ok = stream_sync_and(bar_id, ok);
+            if (!ok) break;
+            if (warp == issuer) issue_layer2<T>(tbase, tb, sb, bar);
+            wait_mma();
+            load_acc<T::L3TC ? S::H2 : T::D2COLS>(trow, T::cD, h);
+            tc::wait_ld();
+            const float e = out_layer_error<S, CLAMP>(m, sw, h, tt, leak);
+            // candidate k's cell loss: its pixels' errors in raster order (rows pi = 0, 1, ...), in double
+            double loss = (double)e;
+            for (int j = 1; j < cellpix; j++) loss += (double)__shfl_down_sync(0xffffffffu, e, j);
+            // the reference's choice: the smallest loss among k != cur (ties to the smaller k) wins if below loss[cur]
+            const int cur = qat_index(zt[c], bits);
+            const double lcur = __shfl_sync(0xffffffffu, loss, group + cur * cellpix);
+            const bool cand = pi == 0 && k != cur;
+            double best = cand ? loss : 0.0;
+            int bk = cand ? k : n;
+            for (int o = cellpix; o < rpt; o <<= 1) {
+                const double ob = __shfl_xor_sync(0xffffffffu, best, o);
+                const int okk = __shfl_xor_sync(0xffffffffu, bk, o);
+                if (okk < n && (bk >= n || ob < best || (ob == best && okk < bk))) { best = ob; bk = okk; }
+            }
+            const int win = (bk < n && best < lcur) ? bk : cur;
+            __syncwarp();
+            if (live && local == 0) zt[c] = gv[win];
+            __syncwarp();
+        }
+    }
+    if (!ok) {
+        if (tid == 0) atomicExch(err, 1);
+        tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (threadIdx.x < 32) { tc::fence_after_sync(); tc::tmem_dealloc(tbase, kTmemCols); }
+}
+
+template <class S>
+bool launch_qat_tc_shape(cudaStream_t s, const DevModel& m, const float* w, float* zdec, const float* tgt, const float* qgrid,
+                         int bits, int cw, int ch, long long t_begin, long long t_end, int* err) {
+    using T = TcShape<S>;
+    using LY = typename LayoutForNin<S::NIN>::type;
+    if constexpr (std::is_void_v<LY>) {
+        return false;
+    } else {
+        if (!LY::matches(m) || !m.lv[0].nearest) return false;
+        const int rpt = (1 << bits) * cw * ch;
+        if (bits < 1 || cw < 1 || ch < 1 || rpt > 32 || (rpt & (rpt - 1)) != 0) return false;
+        const size_t smem = (size_t)T::SIGN * sizeof(float);
+        const int tpt = kTcRows / rpt;
+        const long long ntiles = (t_end - t_begin + tpt - 1) / tpt;
+        const int blocks = (int)std::min<long long>(device_sm_count(), (ntiles + T::STREAMS - 1) / T::STREAMS);
+        auto go = [&](auto kernel) {
+            ensure_dynamic_smem((const void*)kernel, (int)smem);
+            kernel<<<blocks, T::TPB, smem, s>>>(m, w, zdec, tgt, qgrid, bits, cw, ch, t_begin, t_end, err);
+        };
+        if (m.clamp_out) go(k_qat_tc<S, LY, true>); else go(k_qat_tc<S, LY, false>);
+        return true;
+    }
+}
+
 template <class S>
 void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const float* zdec, const float* eps, long long nz,
                    const float* tgt, int K, unsigned active, float sg, float inv_px, float* dpix, long long p_begin,
@@ -680,15 +1000,17 @@ void launch_lat_tc(cudaStream_t s, const DevModel& m, const float* w, const floa
     const int nsm = device_sm_count();
     const long long items = (long long)K * ((p_end - p_begin + kTcRows - 1) / kTcRows);
     const int grid = (int)std::min<long long>(nsm, (items + T::STREAMS - 1) / T::STREAMS);
+    auto go = [&](auto kernel) {
+        ensure_dynamic_smem((const void*)kernel, (int)smem);
+        kernel<<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
+    };
     if constexpr (!std::is_void_v<LY>) {
         if (LY::matches(m)) {
-            ensure_dynamic_smem((const void*)k_lat_eval_tc<S, LY>, (int)smem);
-            k_lat_eval_tc<S, LY><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
+            if (m.clamp_out) go(k_lat_eval_tc<S, LY, true>); else go(k_lat_eval_tc<S, LY, false>);
             return;
         }
     }
-    ensure_dynamic_smem((const void*)k_lat_eval_tc<S, void>, (int)smem);
-    k_lat_eval_tc<S, void><<<grid, T::TPB, smem, s>>>(m, w, zdec, eps, nz, tgt, K, active, sg, inv_px, dpix, p_begin, p_end, pstride, err);
+    if (m.clamp_out) go(k_lat_eval_tc<S, void, true>); else go(k_lat_eval_tc<S, void, false>);
 }
 
 }  // namespace
@@ -706,6 +1028,21 @@ bool launch_pop_eval_tc(cudaStream_t s, int shape, const DevModel& m, const PopA
     }
     NTCB_CHECK(cudaGetLastError());
     return true;
+}
+
+bool launch_qat_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, float* zdec, const float* tgt, const float* grid,
+                   int bits, int cw, int ch, long long t_begin, long long t_end, int* err) {
+    if (t_end <= t_begin) return true;
+    if (err == nullptr) return false;
+    bool done = false;
+    switch (shape) {
+#define NTCB_CASE(ID, NIN, H1, H2, NOUT) case ID: done = launch_qat_tc_shape<FixedShape<NIN, H1, H2, NOUT>>(s, m, w, zdec, tgt, grid, bits, cw, ch, t_begin, t_end, err); break;
+        NTCB_FIXED_SHAPES(NTCB_CASE)
+#undef NTCB_CASE
+        default: return false;
+    }
+    if (done) NTCB_CHECK(cudaGetLastError());
+    return done;
 }
 
 bool launch_lat_eval_tc(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,

@@ -65,6 +65,57 @@ def test_shadow_pull_matches_reference(lam, cuda_device):
     ref.close()
 
 
+def test_dct_level_at_config4_size(cuda_device):
+    """Config 4's DCT-coded level 0 at its own size (1024 x 1024, q 50, the default --dct-lambda recipe: 0.5 with
+    truncation and the ES rate term, lambda-lo 0.25): the reference fits the scale codes and snaps on the host, the
+    device rebuilds the plane from the reference's symbols, runs latent ES steps with the rate term and the snap after
+    each, and one shadow pull; then pulls both sides once more from the same state and compares shadow, plane, symbols
+    and codes bit for bit."""
+    if not refcpu_available():
+        pytest.skip("reference CPU library not built")
+    from neural_block_textures_b200 import dct
+    cfg = model.config(4)
+    spec = cfg.spec
+    tgt = cfg.target()
+    z, p = spec.init_params()
+    ref = RefSession(spec, tgt)
+    ref.set_model(z, p)
+    lam = dct.lambda_recipe(list(spec.dct_q))
+    ref.dct_probe_codes(spec.dct_q, lam=lam, rate_es=True, rate_trunc=True, lambda_lo=0.25)
+    sym, code, step = ref.dct_full_state()
+    zr0, _ = ref.get_model()
+    n0 = spec.levels[0].size
+    with Trainer() as tr:
+        ok, why = tr.init(spec.model_desc(), zr0, p, tgt)
+        assert ok, why
+        d = _desc(ref.dct_desc_fields())
+        tr.set_dct(d, code, sym, step)
+        assert np.array_equal(tr.download_zq()[:n0].view(np.uint32), ref.zdec()[:n0].view(np.uint32)), "plane after set_dct"
+        for it in range(1, 4):                    # latent ES with the rate term, snap after each step, shadow pull
+            tr.lat_step(it, cfg.lat_sigma, cfg.lat_lr, cfg.lat_pairs)
+            tr.shadow_pull(0, n0, 0.01)
+        rate = tr.download_dct_rate(code.size)
+        assert rate["evals"] > 0 and np.all(rate["bits"] >= 0)
+        zd, pd = tr.download_model()
+        dsym, dcode = tr.download_dct(code.size)
+        # the same pull from the device's state on both sides
+        ref.set_model(zd, pd)
+        ref.dct_set_symbols(dsym, dcode)
+        ref.dct_shadow_pull(0.0)                  # re-snap the host copy from the device's shadow
+        tr.shadow_pull(0, n0, 0.0)
+        assert np.array_equal(tr.download_zq()[:n0].view(np.uint32), ref.zdec()[:n0].view(np.uint32)), "re-snapped plane"
+        tr.shadow_pull(0, n0, 0.01)
+        ref.dct_shadow_pull(0.01)
+        zd2, _ = tr.download_model()
+        zr2, _ = ref.get_model()
+        assert np.array_equal(zd2.view(np.uint32), zr2.view(np.uint32)), "shadow after the pull"
+        assert np.array_equal(tr.download_zq()[:n0].view(np.uint32), ref.zdec()[:n0].view(np.uint32)), "plane after the pull"
+        dsym, dcode = tr.download_dct(code.size)
+        rsym, rcode, _ = ref.dct_full_state()
+        assert np.array_equal(dsym, rsym) and np.array_equal(dcode, rcode), "symbols / codes after the pull"
+    ref.close()
+
+
 def _sample_pairs(N: int, n: int) -> list[int]:
     return sorted(set(int(x) for x in np.linspace(0, N - 1, n)))
 
