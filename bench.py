@@ -421,6 +421,9 @@ class Arm:
         self.Kl = K if self.has_lat else 0
         self.sharded = self.native = None
         L0 = spec.levels[0]
+        self.dct_pull = 0.0
+        if spec.dct_q:
+            self._dct_live(spec)
         if world > 1 and args.shard_driver == "native":
             self.native = NativeShardedES(self.tr, dist, device="cuda",
                                           p2p=(self.N, self.Kl, self.qat) if args.exchange == "p2p" else None)
@@ -431,6 +434,28 @@ class Arm:
         elif world > 1:
             self.sharded = ShardedES(self.tr, dist, self.N, device="cuda", stream=self.stream, K=self.Kl, image=(spec.W, spec.H),
                                      level0=(L0.W, L0.H, L0.C) if spec.qat_bits else None, P=spec.P)
+
+    def _dct_live(self, spec):
+        """A DCT-coded level 0 (config 4) goes live as the reference trainer's switch does (main.cpp:4099-4107): scale
+        codes from the sensitivity probe (here the device probe), the step tables of --dct-q, the default --dct-lambda
+        recipe with truncation and the ES rate term (lambda-lo 0.25), the default dead-zone (off) and shadow pull (0.01).
+        The symbols start at zero and the first latent step's snap derives them from the shadow latent."""
+        from neural_block_textures_b200 import abi, dct
+        tr = self.tr
+        codes, _ = tr.dct_probe()
+        C0 = spec.levels[0].C
+        steps = np.ascontiguousarray(np.concatenate([dct.build_steps(q, spec.dct_dc_step) for q in spec.dct_q]).reshape(-1), np.int32)
+        lam = dct.lambda_recipe(list(spec.dct_q))
+        d = abi.DctDesc()
+        d.live, d.C, d.BW, d.BH, d.N, d.dc_step = 1, C0, spec.W // 8, spec.H // 8, 8, spec.dct_dc_step
+        d.rate_es, d.rate_trunc = 1, 1
+        d.rate_scale = float(np.float32(lam / (16.0 * 65025.0 * spec.W * spec.H)))
+        for k, v in enumerate(dct.lam_t16(lam, True)):
+            d.lam_t16[k] = float(v)
+        d.lo_w16, d.deadzone = 4, 0
+        tr.set_dct(d, codes, np.zeros(codes.size * 64, np.int16), steps)
+        self.dct_pull = 0.01
+        self.dct_n0 = spec.levels[0].size
 
     def exchange(self) -> str:
         if self.native is None and self.sharded is None:
@@ -447,6 +472,8 @@ class Arm:
             tr.mlp_step(it, c.mlp_sigma, c.mlp_lr, self.N, self.M)
             if self.has_lat:
                 tr.lat_step(it, c.lat_sigma, c.lat_lr, self.K)
+            if self.dct_pull > 0.0:
+                tr.shadow_pull(0, self.dct_n0, self.dct_pull)
             if self.qat:
                 tr.qat_search()
         else:
@@ -464,6 +491,8 @@ class Arm:
             tr.mlp_step_fd(it, c.fd_h, c.mlp_lr, self.M)
             if self.has_lat:
                 tr.lat_step(it, c.lat_sigma, c.lat_lr, self.K)
+            if self.dct_pull > 0.0:
+                tr.shadow_pull(0, self.dct_n0, self.dct_pull)
             if self.qat:
                 tr.qat_search()
         else:

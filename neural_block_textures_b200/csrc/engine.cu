@@ -1620,7 +1620,15 @@ void ntcb_shard_iteration(ntcb_trainer* t, ntcb_comm* c, int it, int mlp_mode, f
     if (qat) {
         const long long LW = I.d.lv[0].W, LC = I.d.lv[0].C, rows = I.d.lv[0].H / G;
         qat_rows_part(I, r * rows * LW, (r + 1) * rows * LW);
-        gather(I.zdec + I.dm.lv[0].off, (size_t)(rows * LW * LC) * sizeof(float));
+        // the searched rows travel as one-byte grid indices (exact both ways), blocks padded to whole 4-byte words
+        const long long n = rows * LW * LC;
+        const size_t blk = ((size_t)n + 3) / 4 * 4;
+        ensure_xbuf(I, (long long)blk * G);
+        float* z0 = I.zdec + I.dm.lv[0].off;
+        uint8_t* xb = reinterpret_cast<uint8_t*>(I.xbuf);
+        ntcb::launch_qat_pack(I.stream, z0 + r * n, n, (int)LC, I.qat_bits, xb + (size_t)r * blk);
+        gather(I.xbuf, blk);
+        ntcb::launch_qat_unpack(I.stream, xb, (long long)blk, n, G, (int)LC, I.qat_bits, I.qat_grid, z0);
         qat_copy_back(I);
     }
 }

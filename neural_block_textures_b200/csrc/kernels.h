@@ -99,6 +99,11 @@ struct LatAdam {              // Adam on the texels a gather produces (latent, m
 void launch_lat_gather(cudaStream_t s, const DevModel& m, int level, const int* xr, const int* yr, const float* dpix,
                        const float* eps, long long nz, int K, float scale, const RateTerm& rate, float* grad,
                        int rows_per_block, int ty0, int ty1, int row_base, const LatAdam& adam);
+// Level-0 values of n consecutive floats (C channels) as one-byte grid indices, and back: world blocks of blk bytes,
+// block q holding values [q n, (q + 1) n) (the sharded selector search's exchange).
+void launch_qat_pack(cudaStream_t s, const float* z0, long long n, int C, const int* bits, uint8_t* out);
+void launch_qat_unpack(cudaStream_t s, const uint8_t* in, long long blk, long long n, int world, int C, const int* bits,
+                       const float* grid, float* z0);
 // Tensor-core selector search (one bit depth for every level-0 channel, uniform cw x ch pixel cells, the fixed shapes
 // with their compile-time level layout, (2^bits) cw ch <= 32 rows per texel); false when it does not apply (nothing
 // launched). err: device flag set when an MMA completion wait timed out.

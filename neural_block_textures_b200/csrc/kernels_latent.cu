@@ -362,6 +362,32 @@ __global__ void k_qat_generic(DevModel m, const float* __restrict__ wg, float* _
     }
 }
 
+// The selector search's exchange carries level 0 as grid indices, one byte per value: every value of a searched row
+// is a grid value of its channel (qat_index recovers its index exactly and the grid table gives the value back), a
+// quarter of the float bytes on the wire.
+__global__ void k_qat_pack(const float* __restrict__ z0, long long n, int C, const int* __restrict__ bits, uint8_t* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = (uint8_t)qat_index(z0[i], bits[(int)(i % C)]);
+}
+__global__ void k_qat_unpack(const uint8_t* __restrict__ in, long long blk, long long n, int world, int C, const int* __restrict__ bits,
+                             const float* __restrict__ grid, float* __restrict__ z0) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * world) return;
+    const long long q = i / n, j = i - q * n;
+    z0[i] = grid[bits[(int)(j % C)] * 257 + in[q * blk + j]];
+}
+void launch_qat_pack(cudaStream_t s, const float* z0, long long n, int C, const int* bits, uint8_t* out) {
+    if (n <= 0) return;
+    k_qat_pack<<<blocks_for(n, 256), 256, 0, s>>>(z0, n, C, bits, out);
+    NTCB_CHECK(cudaGetLastError());
+}
+void launch_qat_unpack(cudaStream_t s, const uint8_t* in, long long blk, long long n, int world, int C, const int* bits,
+                       const float* grid, float* z0) {
+    if (n <= 0) return;
+    k_qat_unpack<<<blocks_for(n * world, 256), 256, 0, s>>>(in, blk, n, world, C, bits, grid, z0);
+    NTCB_CHECK(cudaGetLastError());
+}
+
 template <class S, int G, int R2>
 void launch_qat_fixed(cudaStream_t s, const DevModel& m, const float* w, float* zdec, const float* tgt, const int* xr0,
                       const int* yr0, const float* grid, const int* bits, long long t_begin, long long t_end) {
