@@ -548,6 +548,30 @@ def timed_steps(arm, step_fn, it, steps, flush, dist):
     return [a.elapsed_time(b) for a, b in evs], it
 
 
+def phase_breakdown(arm, step, it, nb, flush, dist):
+    """Per-phase breakdown: a separate pass of nb steps with every kernel class timed (device time of this library's
+    kernels and, under the native sharded driver, of the exchanges; the rest of a step is idle gaps). This rank's
+    figures, ms per step."""
+    import torch
+    tr, stream = arm.tr, arm.stream
+    tr.kernel_timing_only(None)
+    tr.kernel_timing(True)
+    start_together(stream, dist)
+    for _ in range(nb):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        step(it); it += 1
+    stream.synchronize()
+    breakdown = {}
+    for cls in ("mlp_eval", "lat_eval", "qat", "batch", "noise", "mlp_finish", "mlp_grad", "lat_noise", "lat_gather", "dct_rate",
+                "adam", "snap", "exchange"):
+        ms_c, n_c = tr.kernel_time(cls)
+        if n_c:
+            breakdown[cls] = ms_c / nb
+    tr.kernel_timing(False)
+    return breakdown, it
+
+
 def cfg5_leg(args, world, rank, dist, flush):
     """The north star's scaling configuration (config 5: 2048^2, population 32768) on the same N GPUs, same timing
     rules as the headline (warm-up, ranks lined up, L2 flushed between steps, CUDA events, max over ranks)."""
@@ -566,6 +590,10 @@ def cfg5_leg(args, world, rank, dist, flush):
            "unit": "decodes/s", "decodes_per_step": cfg.decodes_per_iter(), "exchange": arm.exchange(),
            "scaling": "strong", "l2": "flushed between steps (256 MiB memset outside the timed events)",
            "note": "efficiency at N = value(N) / (N value(1)) over the cfg5 objects of the per-N lines"}
+    nb = min(args.steps, 20)
+    breakdown, it = phase_breakdown(arm, arm.step, it, nb, flush, dist)
+    out["phase_ms_per_step"] = {**breakdown, "kernels_total": sum(v for k, v in breakdown.items() if k != "exchange"),
+                                "note": f"rank {rank}, separate pass of {nb} steps with every kernel class timed"}
     arm.close()
     return out
 
@@ -614,24 +642,8 @@ def main():
     tr.kernel_timing(False)
     ms, ms_med, ms_first = max_over_ranks([sum(per_step), statistics.median(per_step), per_step[0]], dist)
 
-    # ---- per-phase breakdown: a separate pass with every kernel class timed (device time of this library's
-    # kernels and, under the native sharded driver, of the exchanges; the rest of a step is idle gaps)
     nb = min(args.steps, 100)
-    tr.kernel_timing_only(None)
-    tr.kernel_timing(True)
-    start_together(stream, dist)
-    for _ in range(nb):
-        with torch.cuda.stream(stream):
-            flush.zero_()
-        step(it); it += 1
-    stream.synchronize()
-    breakdown = {}
-    for cls in ("mlp_eval", "lat_eval", "qat", "batch", "noise", "mlp_finish", "mlp_grad", "lat_noise", "lat_gather", "dct_rate",
-                "adam", "snap", "exchange"):
-        ms_c, n_c = tr.kernel_time(cls)
-        if n_c:
-            breakdown[cls] = ms_c / nb
-    tr.kernel_timing(False)
+    breakdown, it = phase_breakdown(arm, step, it, nb, flush, dist)
     value = decodes * args.steps / (ms * 1e-3)
 
     # ---- FD-phase iterations (mlp_step_fd + lat_step + qat_search), same timing rules

@@ -265,7 +265,8 @@ void ntcb_shard_mlp_apply(ntcb_trainer* t, int it, float sigma, float lr, int N,
 /* The same step with the ES gradient sharded too (no rank regenerates other ranks' noise). A rank's pair range
  * must start and end on a gradient segment (64 pairs; N > 256); ntcb_shard_es_block_bytes returns the size of
  * its exchange block in bytes, or -1 when the range does not qualify (then use the pair above). The block is
- * [2 * n doubles: (L+, L-) per pair][n / 64 * P floats: the rank's gradient segment sums]. After the caller
+ * [2 * n doubles: (L+, L-) per pair][n / 64 * P floats: the rank's gradient segment sums][zero to 12 bytes of
+ * padding to a multiple of 16 bytes]. After the caller
  * all-gathers every rank's block (rank order = pair order, equal n), ntcb_shard_mlp_apply_grad sums all
  * segments in order and runs Adam: the same update, bit for bit, as the single-GPU step. */
 long long ntcb_shard_es_block_bytes(const ntcb_trainer* t, int N, int pair_begin, int pair_end);

@@ -643,14 +643,20 @@ unsigned lat_mask(const Impl& I) {
 // The first half of a latent ES step: the noise of every ES-trained texel for the K pairs of this step, and
 // the per-pixel loss differences of pixels [p_begin, p_end) written into dpix ([K][W H]).
 // Pixels [p_begin, p_end) of all K pairs; pair k's value of pixel p goes to dpix[k * pstride + p - p_begin].
-void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_end, float* dpix, long long pstride) {
+// eps_lo / eps_hi >= 0: the pass reads the noise of flat latent elements [eps_lo, eps_hi) only, and only those are
+// generated (a rank's pixel rows of the texel-row split).
+void lat_eval_part(Impl& I, float sigma, int K, long long p_begin, long long p_end, float* dpix, long long pstride, long long eps_lo = -1,
+                   long long eps_hi = -1) {
     const unsigned mask = lat_mask(I);
     if (!mask) return;
     ensure_lat(I, K);
     int nact = 0;
     for (int l = 0; l < I.d.nlev; l++) if (mask & (1u << l)) nact++;
     const int step = I.lat_step_no;
-    timed(I, "lat_noise", nact, [&] { ntcb::launch_lat_noise(I.stream, I.d.seed, step, K, I.dm, mask, I.nz, I.lat_eps); });
+    timed(I, "lat_noise", eps_lo >= 0 ? 1 : nact, [&] {
+        if (eps_lo >= 0) ntcb::launch_lat_noise_range(I.stream, I.d.seed, step, K, eps_lo, eps_hi, I.nz, I.lat_eps);
+        else ntcb::launch_lat_noise(I.stream, I.d.seed, step, K, I.dm, mask, I.nz, I.lat_eps);
+    });
     const float inv_px = 1.0f / (3.0f * I.d.wsum * (float)I.d.W * (float)I.d.H);
     timed(I, "lat_eval", 1, [&] {
         if (!(I.tensor_pop && ntcb::launch_lat_eval_tc(I.stream, I.shape, I.dm, I.w, I.zdec, I.lat_eps, I.nz, I.tgt, K, mask, sigma,
@@ -858,12 +864,15 @@ size_t copy_out(const Impl& I, const T* dev, size_t count, T* out, size_t cap) {
 }
 
 // ---------------------------------------------------------------------- population sharding (one rank's part)
-// Size of a rank's ES block for pairs [p0, p1): 2 doubles per pair + P floats per gradient segment; -1 when the
-// range is not aligned to the segments (or the population is one segment).
+// Size of a rank's ES block for pairs [p0, p1): 2 doubles per pair + P floats per gradient segment, padded to a
+// multiple of 16 bytes (the blocks sit back to back in the exchange buffer, and each block's fitness doubles must
+// stay 8-byte aligned whatever P is); -1 when the range is not aligned to the segments (or the population is one
+// segment).
+long long es_part_bytes(const Impl& I, int N, int n) { return 4LL * (n / es_seglen(N)) * I.P; }
 long long es_block_bytes(const Impl& I, int N, int p0, int p1) {
     const int seglen = es_seglen(N), n = p1 - p0;
     if (!I.ready || N <= 256 || n <= 0 || p0 % seglen || n % seglen) return -1;
-    return 16LL * n + 4LL * (n / seglen) * I.P;
+    return (16LL * n + es_part_bytes(I, N, n) + 15) / 16 * 16;
 }
 
 // Pairs [p0, p1) of step `it`: minibatch, noise, population, and this rank's block = [fitness | segment sums].
@@ -883,17 +892,16 @@ void shard_mlp_eval_grad_impl(Impl& I, int it, float sigma, int N, int M, int p0
 void shard_mlp_apply_grad_impl(Impl& I, float lr, int N, const void* blocks, int world) {
     const int n = N / world, seglen = es_seglen(N);
     const long long bytes = es_block_bytes(I, N, 0, n);
-    const size_t fit_bytes = 16 * (size_t)n, part_bytes = (size_t)bytes - fit_bytes;
-    const int nseg = N / seglen;
-    ensure_gpart(I, (long long)nseg * I.P);
+    const size_t fit_bytes = 16 * (size_t)n;
     const char* src = static_cast<const char*>(blocks);
-    // [rank][fitness | partials] -> fitness of all N pairs in pair order, partials of all segments in order
+    // [rank][fitness | partials | pad] -> fitness of all N pairs in pair order (kept for the statistics); the
+    // partials are summed in segment order straight from the blocks
     NTCB_CHECK(cudaMemcpy2DAsync(I.fit, fit_bytes, src, (size_t)bytes, fit_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
-    NTCB_CHECK(cudaMemcpy2DAsync(I.gpart, part_bytes, src + fit_bytes, (size_t)bytes, part_bytes, world, cudaMemcpyDeviceToDevice, I.stream));
     timed(I, "mlp_grad", 1, [&] {
         I.mlp_t++;
         float c1, c2; adam_coeffs(I.mlp_t, c1, c2);
-        ntcb::launch_es_grad_adam(I.stream, I.gpart, nseg, I.P, I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
+        ntcb::launch_es_grad_adam_ranks(I.stream, reinterpret_cast<const float*>(src + fit_bytes), bytes / 4, world, n / seglen, I.P,
+                                        I.wgrad, I.w, I.wm, I.wv, lr, c1, c2);
     });
     I.last_N = N; I.last_fd = false; I.last_pairs = N;
     I.dl_pending = N;   // dl / lsum of all N pairs from I.fit when mlp_stats / debug_last_dl ask
@@ -905,7 +913,17 @@ long long shard_lat_rows_impl(Impl& I, float sigma, float lr, int K, int lvl, in
     const auto& L = I.d.lv[lvl];
     ensure_lat(I, K);
     const long long W = I.d.W;
-    lat_eval_part(I, sigma, K, (long long)pa * W, (long long)pb * W, I.dpix, (long long)(pb - pa) * W);
+    // the texel rows that pixel rows [pa, pb) sample (a superset of [ta, tb), whose gathers read the same noise): the
+    // only noise this rank's pass and gathers read
+    std::vector<int> yb, ye;
+    axis_ranges(I.d.H, L.H, L.nearest, yb, ye);
+    int na = L.H, nb = 0;
+    for (int t = 0; t < L.H; t++)
+        if (yb[t] < pb && ye[t] > pa) { na = std::min(na, t); nb = std::max(nb, t + 1); }
+    na = std::min(na, ta); nb = std::max(nb, tb);
+    const long long row = (long long)L.W * L.C;
+    lat_eval_part(I, sigma, K, (long long)pa * W, (long long)pb * W, I.dpix, (long long)(pb - pa) * W, (long long)L.off + na * row,
+                  (long long)L.off + nb * row);
     const long long off = (long long)L.off + (long long)ta * L.W * L.C;
     const float scale = 1.0f / (2.0f * (float)K * sigma);
     I.lat_t++;

@@ -72,6 +72,9 @@ void launch_es_grad_partial(cudaStream_t s, const double* dl, const float* eps, 
 // grad[k] = sum_seg gpart[seg][k] (fixed order), then Adam on (theta, m, v).
 void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2);
+// The same from the ranks' exchange blocks in place: rank r's segs segment sums start at part + r * rank_stride floats.
+void launch_es_grad_adam_ranks(cudaStream_t s, const float* part, long long rank_stride, int world, int segs, int P, float* grad,
+                               float* theta, float* m, float* v, float lr, float c1, float c2);
 void launch_fd_grad_adam(cudaStream_t s, const double* dl, const double* hh, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2);
 void launch_decode(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* z, float* img);
@@ -80,6 +83,8 @@ void launch_dct_probe(cudaStream_t s, const DevModel& m, const float* w, const f
 
 // ---- latent ES and selector search (kernels_latent.cu) ----
 void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevModel& m, unsigned active_mask, long long nz, float* eps);
+// The same noise for the flat latent elements [lo, hi) only (each value depends on its index alone).
+void launch_lat_noise_range(cudaStream_t s, uint64_t seed, int step, int K, long long lo, long long hi, long long nz, float* eps);
 void launch_lat_eval(cudaStream_t s, int shape, const DevModel& m, const float* w, const float* zdec, const float* eps,
                      long long nz, const float* tgt, int K, unsigned active_mask, float sg, float inv_px, float* dpix,
                      long long p_begin, long long p_end, long long pstride);

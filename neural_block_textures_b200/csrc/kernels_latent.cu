@@ -28,13 +28,17 @@ __global__ void k_lat_noise(uint64_t seed, int step, int K, long long lo, long l
         eps[(long long)k * nz + i] = gauss_at(key, (uint64_t)i);
 }
 
+void launch_lat_noise_range(cudaStream_t s, uint64_t seed, int step, int K, long long lo, long long hi, long long nz, float* eps) {
+    if (hi <= lo) return;
+    dim3 grid((unsigned)std::min<long long>(blocks_for(hi - lo, 256), 4096), (unsigned)K);
+    k_lat_noise<<<grid, 256, 0, s>>>(seed, step, K, lo, hi, nz, eps);
+    NTCB_CHECK(cudaGetLastError());
+}
 void launch_lat_noise(cudaStream_t s, uint64_t seed, int step, int K, const DevModel& m, unsigned active_mask, long long nz, float* eps) {
     for (int l = 0; l < m.nlev; l++) {
         if (!(active_mask & (1u << l))) continue;
         const long long lo = m.lv[l].off, n = (long long)m.lv[l].W * m.lv[l].H * m.lv[l].C;
-        dim3 grid((unsigned)std::min<long long>(blocks_for(n, 256), 4096), (unsigned)K);
-        k_lat_noise<<<grid, 256, 0, s>>>(seed, step, K, lo, lo + n, nz, eps);
-        NTCB_CHECK(cudaGetLastError());
+        launch_lat_noise_range(s, seed, step, K, lo, lo + n, nz, eps);
     }
 }
 

@@ -345,21 +345,36 @@ void launch_es_grad_partial(cudaStream_t s, const double* dl, const float* eps, 
     NTCB_CHECK(cudaGetLastError());
 }
 
-__global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P, float* __restrict__ grad, float* __restrict__ theta,
-                               float* __restrict__ m, float* __restrict__ v, float lr, float c1, float c2) {
+// One thread per weight adds the segment sums from segment 0 in order, as single floats (32 segments' loads issued
+// together, then their adds): the order of the single-GPU sum whatever the layout. Segment s lives at part + s * P
+// (one gathered array) or, with RANKS, at part + r * rank_stride + t * P for s = r * segs + t (the ranks' exchange
+// blocks read in place).
+template <bool RANKS>
+__device__ __forceinline__ const float* seg_at(const float* pk, int s, long long rank_stride, int segs, int P) {
+    if constexpr (RANKS) {
+        const int r = s / segs;
+        return pk + r * rank_stride + (long long)(s - r * segs) * P;
+    } else {
+        return pk + (long long)s * P;
+    }
+}
+template <bool RANKS>
+__global__ void k_es_grad_adam(const float* __restrict__ part, long long rank_stride, int segs, int nseg, int P, float* __restrict__ grad,
+                               float* __restrict__ theta, float* __restrict__ m, float* __restrict__ v, float lr, float c1, float c2) {
     const int k = blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= P) return;
-    float g = gpart[k];
+    const float* pk = part + k;
+    float g = pk[0];
     int sg = 1;
     constexpr int U = 32;
     for (; sg + U <= nseg; sg += U) {   // 32 segments' loads together, summed in segment order
-        float v[U];
+        float e[U];
 #pragma unroll
-        for (int j = 0; j < U; j++) v[j] = gpart[(long long)(sg + j) * P + k];
+        for (int j = 0; j < U; j++) e[j] = *seg_at<RANKS>(pk, sg + j, rank_stride, segs, P);
 #pragma unroll
-        for (int j = 0; j < U; j++) g += v[j];
+        for (int j = 0; j < U; j++) g += e[j];
     }
-    for (; sg < nseg; sg++) g += gpart[(long long)sg * P + k];
+    for (; sg < nseg; sg++) g += *seg_at<RANKS>(pk, sg, rank_stride, segs, P);
     grad[k] = g;
     float th = theta[k], mm = m[k], vv = v[k];
     adam_update(th, g, mm, vv, lr, c1, c2);
@@ -367,7 +382,12 @@ __global__ void k_es_grad_adam(const float* __restrict__ gpart, int nseg, int P,
 }
 void launch_es_grad_adam(cudaStream_t s, const float* gpart, int nseg, int P, float* grad, float* theta, float* m, float* v,
                          float lr, float c1, float c2) {
-    k_es_grad_adam<<<blocks_for(P, 64), 64, 0, s>>>(gpart, nseg, P, grad, theta, m, v, lr, c1, c2);
+    k_es_grad_adam<false><<<blocks_for(P, 64), 64, 0, s>>>(gpart, 0, nseg, nseg, P, grad, theta, m, v, lr, c1, c2);
+    NTCB_CHECK(cudaGetLastError());
+}
+void launch_es_grad_adam_ranks(cudaStream_t s, const float* part, long long rank_stride, int world, int segs, int P, float* grad,
+                               float* theta, float* m, float* v, float lr, float c1, float c2) {
+    k_es_grad_adam<true><<<blocks_for(P, 64), 64, 0, s>>>(part, rank_stride, segs, world * segs, P, grad, theta, m, v, lr, c1, c2);
     NTCB_CHECK(cudaGetLastError());
 }
 

@@ -188,16 +188,8 @@ __device__ __forceinline__ void stage_set_a(float* sw, float leak, int tid, int 
             continue;
         }
         k -= nB2x;
-        if (k < nBb) {                        // layer-2 bias step: its rows, then W2 times them
-            float v;
-            if (k < S::H2) {
-                v = bias2_row<S>(W1, b0, b1, leak, k);
-            } else {
-                const int c = k - S::H2;
-                v = 0.0f;
-                for (int q = 0; q < S::H2; q++) v = fmaf(W2[c * S::H2 + q], bias2_row<S>(W1, b0, b1, leak, q), v);
-            }
-            put_split<S>(sw, T::oBbh, T::oBbl, kmajor(k, 0, 8), v);
+        if (k < nBb) {                        // layer-2 bias step: its rows (W2 times them: phase B)
+            if (k < S::H2) put_split<S>(sw, T::oBbh, T::oBbl, kmajor(k, 0, 8), bias2_row<S>(W1, b0, b1, leak, k));
             continue;
         }
         k -= nBb;
@@ -217,21 +209,32 @@ __device__ __forceinline__ void stage_set_a(float* sw, float leak, int tid, int 
     }
 }
 
-// Phase B: the output rows of the X step, W2 (l W1 [W0 | b0]), from phase A's values (hi + lo = the exact float).
+// Phase B: the output rows of the X step, W2 (l W1 [W0 | b0]), and of the bias step, W2 (b1 + ...), from phase A's
+// values (hi + lo = the exact float), so no thread of phase A runs a product of two 24-long sums.
 template <class S>
 __device__ __forceinline__ void stage_set_b(float* sw, int tid, int nthr) {
     using T = TcShape<S>;
     const float* W2 = sw + T::oRaw + S::H1 * S::NIN + S::H1 + S::H2 * S::H1 + S::H2;
     constexpr int XC = S::NIN + (T::XB ? 1 : 0);
-    constexpr int n = T::NLIN * XC;
-    for (int e = tid; e < n; e += nthr) {
-        const int c = e / XC, i = e - c * XC;
-        float v = 0.0f;
-        for (int q = 0; q < S::H2; q++) {
-            const int at = kmajor(q, i, T::K1);
-            v = fmaf(W2[c * S::H2 + q], sw[T::oB2xh + at] + sw[T::oB2xl + at], v);
+    constexpr int nx = T::NLIN * XC, nb = T::B1TC ? T::NLIN : 0;
+    for (int e = tid; e < nx + nb; e += nthr) {
+        if (e < nx) {
+            const int c = e / XC, i = e - c * XC;
+            float v = 0.0f;
+            for (int q = 0; q < S::H2; q++) {
+                const int at = kmajor(q, i, T::K1);
+                v = fmaf(W2[c * S::H2 + q], sw[T::oB2xh + at] + sw[T::oB2xl + at], v);
+            }
+            put_split<S>(sw, T::oB2xh, T::oB2xl, kmajor(S::H2 + c, i, T::K1), v);
+        } else {
+            const int c = e - nx;
+            float v = 0.0f;
+            for (int q = 0; q < S::H2; q++) {
+                const int at = kmajor(q, 0, 8);
+                v = fmaf(W2[c * S::H2 + q], sw[T::oBbh + at] + sw[T::oBbl + at], v);
+            }
+            put_split<S>(sw, T::oBbh, T::oBbl, kmajor(S::H2 + c, 0, 8), v);
         }
-        put_split<S>(sw, T::oB2xh, T::oB2xl, kmajor(S::H2 + c, i, T::K1), v);
     }
 }
 
@@ -518,11 +521,26 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
             // stage both perturbed weight sets of this pair (the previous pair's MMAs have all completed)
             const int cand = pop_cand(a, pl);
             const float* e = (a.mode == 0 && a.sigma != 0.0f) ? a.eps + (long long)pl * m.P : nullptr;
-            for (int k = tid; k < T::P; k += kTcRows) {
-                float wp, wm;
-                perturbed_weight(a, e, k, cand, wp, wm);
-                sw[T::oRaw + k] = wp;
-                sw[T::SIGN + T::oRaw + k] = wm;
+            constexpr int PER = (T::P + kTcRows - 1) / kTcRows, BATCH = 4;   // weights per thread, loaded 4 at a time
+#pragma unroll 1
+            for (int u0 = 0; u0 < PER; u0 += BATCH) {
+                float w0r[BATCH], er[BATCH];
+#pragma unroll
+                for (int u = 0; u < BATCH; u++) {
+                    const int k = tid + (u0 + u) * kTcRows;
+                    w0r[u] = k < T::P ? a.w0[k] : 0.0f;
+                    er[u] = (e && k < T::P) ? e[k] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < BATCH; u++) {
+                    const int k = tid + (u0 + u) * kTcRows;
+                    if (k < T::P) {
+                        float wp, wm;
+                        perturbed_weight_of(a, w0r[u], e ? &er[u] : nullptr, k, cand, wp, wm);
+                        sw[T::oRaw + k] = wp;
+                        sw[T::SIGN + T::oRaw + k] = wm;
+                    }
+                }
             }
             stream_sync(bar_id);
             stage_set_a<S>(sw, leak, tid, kTcRows);

@@ -27,11 +27,14 @@ __device__ __forceinline__ int pop_cand(const PopArgs& a, int i) {
     return a.stats_first ? (i == 0 ? -1 : a.cand_begin + i - 1) : a.cand_begin + i;
 }
 
-__device__ __forceinline__ void perturbed_weight(const PopArgs& a, const float* e, int k, int cand, float& wp, float& wm) {
-    const float w0 = a.w0[k];
+// Weight k of the pair's two sets from its base value w0 and, for an ES pair, its noise *ek (nullptr otherwise).
+__device__ __forceinline__ void perturbed_weight_of(const PopArgs& a, float w0, const float* ek, int k, int cand, float& wp, float& wm) {
     wp = w0; wm = w0;
-    if (e) { const float ek = e[k]; wp = fmaf(a.sigma, ek, w0); wm = fmaf(-a.sigma, ek, w0); }
+    if (ek) { wp = fmaf(a.sigma, *ek, w0); wm = fmaf(-a.sigma, *ek, w0); }
     else if (a.mode == 1 && k == cand) { wp = w0 + a.fd_h; wm = w0 - a.fd_h; }
+}
+__device__ __forceinline__ void perturbed_weight(const PopArgs& a, const float* e, int k, int cand, float& wp, float& wm) {
+    perturbed_weight_of(a, a.w0[k], e ? e + k : nullptr, k, cand, wp, wm);
 }
 
 }  // namespace ntcb

@@ -4,8 +4,8 @@ ntcb_shard_iteration call per iteration, in-place all-gathers on the library's o
 peer-memory exchange kernel over CUDA IPC mappings of every rank's exchange buffer). The ranks
 must end with the same weights and latent as one GPU running the plain Trainer steps, bit for bit (every per-pair,
 per-pixel and per-texel value is computed by the same kernels whichever rank computes it, and the gradient sums
-keep their order). The two-rank cases need >= 2 GPUs and are skipped otherwise; the one-rank native case runs on
-one GPU."""
+keep their order). The 2-, 4- and 8-rank cases (64 pairs, 2 level-1 texel rows and 8 level-0 rows per rank at 8)
+need as many GPUs and are skipped otherwise; the one-rank native cases run on one GPU."""
 import os
 import socket
 
@@ -178,22 +178,22 @@ def test_native_iteration_plan_refusals(cuda_device):
         assert not ok and "minibatch" in why
 
 
-@pytest.mark.parametrize("driver", ["python", "native", "native_p2p"])
-def test_two_gpu_sharding_matches_one_gpu(tmp_path, cuda_device, driver):
+@pytest.mark.parametrize("driver,world", [("python", 2), ("native", 2), ("native_p2p", 2), ("native_p2p", 4), ("native_p2p", 8)])
+def test_sharding_matches_one_gpu(tmp_path, cuda_device, driver, world):
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tmp_path), driver)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, str(tmp_path), driver)) for r in range(world)]
     for pr in procs:
         pr.start()
     for pr in procs:
         pr.join(timeout=300)
         assert pr.exitcode == 0
     z, p, z1, p1 = _one_gpu_reference()
-    for r in range(2):
+    for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"p{r}.npy"), p1), f"rank {r} weights"
         assert np.array_equal(np.load(tmp_path / f"z{r}.npy"), z1), f"rank {r} latent"
     assert not np.array_equal(p1, p)

@@ -85,7 +85,7 @@ class PlumbingTrainer:
 
     def shard_es_block_bytes(self, N, p0, p1):
         n = p1 - p0
-        return 16 * n + 4 * (n // 64) * self.P
+        return (16 * n + 4 * (n // 64) * self.P + 15) // 16 * 16
 
     def shard_mlp_eval_grad(self, it, sigma, N, M, p0, p1, block):
         # fitness doubles: (10 i + 1, 10 i + 2) per pair i; segment floats: 100 seg + k
@@ -94,7 +94,7 @@ class PlumbingTrainer:
         for i in range(p0, p1):
             f[2 * (i - p0)] = 10.0 * i + 1.0
             f[2 * (i - p0) + 1] = 10.0 * i + 2.0
-        g = block[16 * n:].view(torch.float32)
+        g = block[16 * n:16 * n + 4 * (n // 64) * self.P].view(torch.float32)
         for sg in range(n // 64):
             for k in range(self.P):
                 g[sg * self.P + k] = 100.0 * (p0 // 64 + sg) + k
@@ -133,7 +133,7 @@ def _plumbing_main(rank, world, port, out_dir):
 
 def test_latent_qat_fd_sharding_plumbing(tmp_path):
     """Two gloo ranks: each fills only its own image rows / level-0 texel rows / FD weights (P = 11, uneven) /
-    ES block (fitness + gradient segments); after the all-gathers every rank holds the whole arrays in order."""
+    ES block (fitness + gradient segments + padding to 16 bytes); after the all-gathers every rank holds the whole arrays in order."""
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_plumbing_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
@@ -151,6 +151,7 @@ def test_latent_qat_fd_sharding_plumbing(tmp_path):
     for r in range(2):
         want_b.append(np.array([10.0 * i + 1.0 + s for i in range(r * n, (r + 1) * n) for s in range(2)]).view(np.uint8))
         want_b.append(np.array([100.0 * (r * n // 64 + sg) + k for sg in range(n // 64) for k in range(T.P)], np.float32).view(np.uint8))
+        want_b.append(np.zeros((-(16 * n + 4 * (n // 64) * T.P)) % 16, np.uint8))   # the block's padding to 16 bytes
     want_b = np.concatenate(want_b)
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"d{r}.npy"), want_d)
