@@ -664,16 +664,18 @@ def main():
     zh = torch.empty(spec.nz, dtype=torch.float32, pin_memory=True).numpy()
     ph = torch.empty(spec.P, dtype=torch.float32, pin_memory=True).numpy()
     zh[:] = arm.z0; ph[:] = arm.p0
+    zo = torch.empty(spec.nz, dtype=torch.float32, pin_memory=True).numpy()   # the step's results, read into pinned memory
+    po = torch.empty(spec.P, dtype=torch.float32, pin_memory=True).numpy()
     e2e_steps = args.e2e_steps
     for _ in range(2):
         tr.upload_model(zh, ph); step(it); it += 1
-        zz, pp = tr.download_model(); tr.mlp_stats()
+        tr.download_model(zo, po); tr.mlp_stats()
     start_together(stream, dist)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         tr.upload_model(zh, ph)
         step(it); it += 1
-        zz, pp = tr.download_model()
+        tr.download_model(zo, po)
         tr.mlp_stats()
     e2e_s = max_over_ranks([time.perf_counter() - t0], dist)[0]
     e2e_value = decodes * e2e_steps / e2e_s
@@ -732,7 +734,7 @@ def main():
             "phase_ms_per_step": {**breakdown, "kernels_total": sum(v for k, v in breakdown.items() if k != "exchange"),
                                   "note": f"separate pass of {nb} steps with every kernel class timed (events around each launch)"},
             "e2e": {"value": e2e_value, "unit": "decodes/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model + mlp_stats"},
+                    "api": "Trainer.upload_model (pinned host) + mlp_step + lat_step + qat_search + download_model (into pinned host arrays) + mlp_stats"},
             "gpu_launches": launches,
             "fd_phase": fd_line,
             "nccl_exchange": nccl_line,

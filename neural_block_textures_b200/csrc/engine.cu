@@ -93,6 +93,7 @@ struct Trainer::Impl {
     // progress-print statistics: the last set_qes description (host copy) and a device scratch buffer
     ntc_cuda::QesDesc qes_host{};
     char* stats_buf = nullptr; size_t stats_cap = 0;
+    double* hstage = nullptr; size_t hstage_cap = 0;   // pinned host staging of the statistics reads (doubles)
     // counters
     int mlp_t = 0, lat_t = 0, lat_step_no = 0;
     int last_N = 0, last_M = 0, last_pairs = 0; bool last_fd = false;
@@ -275,6 +276,7 @@ void free_all(Impl& I) {
     dfree(I.bidx); dfree(I.feat_t); dfree(I.tgt_t); dfree(I.mlp_eps); dfree(I.part);
     dfree(I.fit); dfree(I.dl); dfree(I.lsum); dfree(I.hh); dfree(I.fit_stats); dfree(I.gpart); dfree(I.xbuf); I.xbuf_cap = 0; dfree(I.tc_err);
     dfree(I.qat_grid); dfree(I.qat_bits); dfree(I.stats_buf); I.stats_cap = 0;
+    if (I.hstage) { cudaFreeHost(I.hstage); I.hstage = nullptr; I.hstage_cap = 0; }
     if (I.p2p_ready)
         for (int q = 0; q < I.p2p.world; q++)
             if (q != I.p2p.rank && I.p2p.base[q]) cudaIpcCloseMemHandle(I.p2p.base[q]);
@@ -607,14 +609,26 @@ void mlp_step_fd_impl(Impl& I, int it, float h, float lr, int M) {
     fd_apply(I, h, lr);
 }
 
+// Pinned host doubles for the statistics reads (a pageable destination costs a staged copy per call).
+double* ensure_hstage(Impl& I, size_t n) {
+    if (n > I.hstage_cap) {
+        if (I.hstage) cudaFreeHost(I.hstage);
+        I.hstage = nullptr; I.hstage_cap = 0;
+        NTCB_CHECK(cudaMallocHost(&I.hstage, n * sizeof(double)));
+        I.hstage_cap = n;
+    }
+    return I.hstage;
+}
+
 void mlp_stats_impl(Impl& I, double& batch_loss, double& diff_std) {
     require_ready(I); set_device(I);
     if (I.last_N == 0) { batch_loss = 0; diff_std = 0; return; }
     if (!I.last_fd) {
         ensure_dl(I);
-        std::vector<double> dl(I.last_N), ls(I.last_N);
-        NTCB_CHECK(cudaMemcpyAsync(dl.data(), I.dl, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
-        NTCB_CHECK(cudaMemcpyAsync(ls.data(), I.lsum, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        double* dl = ensure_hstage(I, 2 * (size_t)I.last_N);
+        double* ls = dl + I.last_N;
+        NTCB_CHECK(cudaMemcpyAsync(dl, I.dl, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        NTCB_CHECK(cudaMemcpyAsync(ls, I.lsum, I.last_N * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
         sync(I);
         double mean = 0, mean2 = 0, lmean = 0;
         for (int i = 0; i < I.last_N; i++) { mean += dl[i]; mean2 += dl[i] * dl[i]; lmean += ls[i]; }
@@ -622,8 +636,9 @@ void mlp_stats_impl(Impl& I, double& batch_loss, double& diff_std) {
         diff_std = std::sqrt(std::max(0.0, mean2 - mean * mean));
         batch_loss = lmean;
     } else {
-        std::vector<double> dl(I.P); double l0[2];
-        NTCB_CHECK(cudaMemcpyAsync(dl.data(), I.dl, I.P * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
+        double* dl = ensure_hstage(I, (size_t)I.P + 2);
+        double* l0 = dl + I.P;
+        NTCB_CHECK(cudaMemcpyAsync(dl, I.dl, I.P * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
         NTCB_CHECK(cudaMemcpyAsync(l0, I.fit_stats, 2 * sizeof(double), cudaMemcpyDeviceToHost, I.stream));
         sync(I);
         double ss = 0;

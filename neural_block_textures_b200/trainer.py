@@ -75,9 +75,16 @@ class Trainer:
     def upload_model(self, z: np.ndarray, p: np.ndarray) -> None:
         self.lib.ntcb_upload_model(self.h, _fptr(z), _fptr(p))
 
-    def download_model(self) -> tuple[np.ndarray, np.ndarray]:
-        z = np.empty(self.nz, np.float32)
-        p = np.empty(self.P, np.float32)
+    def download_model(self, z: np.ndarray | None = None, p: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+        """The latent and the weights; into z / p when given (contiguous float32 of nz / P values, e.g. pinned host
+        arrays reused every step), else into new arrays."""
+        if z is None:
+            z = np.empty(self.nz, np.float32)
+        if p is None:
+            p = np.empty(self.P, np.float32)
+        for a, n in ((z, self.nz), (p, self.P)):
+            if a.dtype != np.float32 or a.size != n or not a.flags["C_CONTIGUOUS"]:
+                raise ValueError(f"download_model: output must be a contiguous float32 array of {n} values")
         self.lib.ntcb_download_model(self.h, _fptr(z), _fptr(p))
         return z, p
 
