@@ -922,12 +922,26 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_qat_tc(DevModel m, const
         float tt[S::NOUT];
 #pragma unroll
         for (int c = 0; c < S::NOUT; c++) tt[c] = __ldg(tgt + ((long long)py * m.W + px) * S::NOUT + c);
+        // the row's features; only level 0 changes between channels (the winners installed so far), so with a second
+        // level its features and the position are gathered once per tile
+        float fb[S::NIN];
+        Tap tap0{};
+        if constexpr (LY::NLEV == 2) {
+            layout_features<LY>(m, z, px, py, fb);
+            tap0 = level_tap(L0, pix_u(m, px), pix_v(m, py));
+        }
 #pragma unroll 1
         for (int c = 0; c < LY::C0; c++) {
             // X = this row's features with channel c set to candidate k
             {
                 float f[S::NIN];
-                layout_features<LY>(m, z, px, py, f);
+                if constexpr (LY::NLEV == 2) {
+#pragma unroll
+                    for (int i = 0; i < S::NIN; i++) f[i] = fb[i];
+                    if (c > 0) sample_level_c<LY::C0>(L0, z + L0.off, tap0, f);
+                } else {
+                    layout_features<LY>(m, z, px, py, f);
+                }
 #pragma unroll
                 for (int i = 0; i < LY::C0; i++) if (i == c) f[i] = gv[k];
                 float x[T::K1];

@@ -41,6 +41,14 @@ def test_decode_full(name, cuda_device):
     assert np.abs(tr.decode_full(z2) - orc.decode_full(p, z2)).max() < 1e-5
     z3, p3 = tr.download_model()
     assert np.array_equal(z3, z) and np.array_equal(p3, p)
+    # into caller arrays (pinned host memory, reused every step in bench.py's end-to-end leg)
+    import torch
+    zo = torch.full((spec.nz,), -1.0, dtype=torch.float32, pin_memory=True).numpy()
+    po = torch.full((spec.P,), -1.0, dtype=torch.float32, pin_memory=True).numpy()
+    z4, p4 = tr.download_model(zo, po)
+    assert z4 is zo and p4 is po and np.array_equal(zo, z) and np.array_equal(po, p)
+    with pytest.raises(ValueError):
+        tr.download_model(np.zeros(spec.nz, np.float64), po)
 
 
 @pytest.mark.parametrize("name", ALL_SPECS)
