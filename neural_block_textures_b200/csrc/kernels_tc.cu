@@ -348,13 +348,15 @@ __device__ __forceinline__ void issue3(uint32_t d, uint32_t a, uint32_t b_hi4, u
     constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
     constexpr uint32_t sbo = (uint32_t)K * 32u;
     tc::fence_after_sync();
+    if (elect_one()) {
 #pragma unroll
-    for (int s = 0; s < K / 8; s++) {
-        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s + 8, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, s > 0 ? 1u : 0u);
-        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
+        for (int s = 0; s < K / 8; s++) {
+            tc::mma_tf32_ts(d, a + 16 * s + 8, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, s > 0 ? 1u : 0u);
+            tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
+            tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
+        }
+        tc::commit(bar);
     }
-    if (elect_one()) tc::commit(bar);
     __syncwarp();
 }
 
@@ -367,23 +369,25 @@ __device__ __forceinline__ void issue_l2(uint32_t d, uint32_t a, uint32_t b_hi4,
     constexpr uint32_t id = tc::idesc_tf32(kTcRows, N);
     constexpr uint32_t sbo = (uint32_t)K * 32u, sbox = (uint32_t)KX * 32u;
     tc::fence_after_sync();
+    if (elect_one()) {
 #pragma unroll
-    for (int s = 0; s < K / 8; s++) {
-        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s + 8, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, s > 0 ? 1u : 0u);
-        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
-    }
+        for (int s = 0; s < K / 8; s++) {
+            tc::mma_tf32_ts(d, a + 16 * s + 8, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, s > 0 ? 1u : 0u);
+            tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_lo4 + 16 * s, 128, sbo), id, 1u);
+            tc::mma_tf32_ts(d, a + 16 * s, tc::sdesc_s4(b_hi4 + 16 * s, 128, sbo), id, 1u);
+        }
 #pragma unroll
-    for (int s = 0; s < KX / 8; s++) {
-        if (elect_one()) tc::mma_tf32_ts(d, ax + 16 * s + 8, tc::sdesc_s4(bx_hi4 + 16 * s, 128, sbox), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, ax + 16 * s, tc::sdesc_s4(bx_lo4 + 16 * s, 128, sbox), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, ax + 16 * s, tc::sdesc_s4(bx_hi4 + 16 * s, 128, sbox), id, 1u);
+        for (int s = 0; s < KX / 8; s++) {
+            tc::mma_tf32_ts(d, ax + 16 * s + 8, tc::sdesc_s4(bx_hi4 + 16 * s, 128, sbox), id, 1u);
+            tc::mma_tf32_ts(d, ax + 16 * s, tc::sdesc_s4(bx_lo4 + 16 * s, 128, sbox), id, 1u);
+            tc::mma_tf32_ts(d, ax + 16 * s, tc::sdesc_s4(bx_hi4 + 16 * s, 128, sbox), id, 1u);
+        }
+        if constexpr (BIAS) {
+            tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_lo4, 128, 256), id, 1u);
+            tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_hi4, 128, 256), id, 1u);
+        }
+        tc::commit(bar);
     }
-    if constexpr (BIAS) {
-        if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_lo4, 128, 256), id, 1u);
-        if (elect_one()) tc::mma_tf32_ts(d, one, tc::sdesc_s4(bb_hi4, 128, 256), id, 1u);
-    }
-    if (elect_one()) tc::commit(bar);
     __syncwarp();
 }
 
