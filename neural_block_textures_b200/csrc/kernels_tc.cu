@@ -12,8 +12,8 @@
 // Row r of a tile is TMEM lane r, so thread t (warp w = t / 32) owns row t: it loads its accumulator row
 // from TMEM, applies bias / activation, and stores the next layer's A operand back to TMEM (A-from-TMEM
 // MMAs). The B operands (both signs' W0 | b0 and W1) sit in shared memory, K-major without swizzle.
-// Warp 0 issues the MMAs converged, one elected lane per instruction, with compile-time TMEM / shared
-// addresses (a divergent single-thread issue loop costs ~4x more per MMA), and commits them to an mbarrier.
+// One warp per stream issues the MMAs: the converged warp elects one lane, which issues all of a layer's MMAs
+// (compile-time TMEM / shared addresses, unrolled) and commits them to an mbarrier.
 //
 // Schedule per stream (u = tile x sign): L1(u) issued -> wait, load, activation, store H -> L2(u) issued ->
 // wait, load D2 -> L1(u + 1) issued (the next tile's features were prefetched one tile ahead), together with
@@ -340,7 +340,8 @@ __device__ __forceinline__ void relu2(float* h) {
     for (int j = 0; j < N; j++) h[j] = h[j] + fabsf(h[j]);
 }
 
-// Warp 0 (converged): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K step), then commit. a: the
+// The issuing warp (converged; one elected lane issues): D = A B^T over K as 3xTF32 (lo*hi, hi*lo, hi*hi per 8-wide K
+// step), then commit. a: the
 // interleaved A operand in TMEM (K step s: hi at a + 16 s, lo at a + 16 s + 8); b_hi4 / b_lo4: the B operands' shared
 // addresses shifted right by 4 (hoisted; each descriptor is then one add).
 template <int K, int N>
