@@ -1514,6 +1514,10 @@ int ntcb_p2p_export(ntcb_trainer* t, int world, int rank, int N, int K, int qat,
     if (!iteration_plan(I, world, rank, 1, N, 1, K, qat, mx, lx, r)) { set_why(why, why_cap, r); return 0; }
     if (I.p2p_buf) { set_why(why, why_cap, "peer exchange already set up for this trainer"); return 0; }
     const size_t cap = (ntcb::p2p_stage_bytes(max_exchange_block(I, world, rank, N, K, qat, mx, lx)) + 255) / 256 * 256;
+    if (cap / 16 * (size_t)std::max(1, world - 1) >= (1ull << 31)) {   // the exchange kernel indexes (peer, line) tasks in 32 bits
+        set_why(why, why_cap, "exchange blocks too large for the peer exchange (use the NCCL exchange)");
+        return 0;
+    }
     const size_t total = ntcb::kP2PHeader + 2 * (size_t)world * cap;
     I.p2p_buf = dalloc<char>(total);
     NTCB_CHECK(cudaMemset(I.p2p_buf, 0, total));

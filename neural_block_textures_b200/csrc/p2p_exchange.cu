@@ -69,7 +69,9 @@ size_t p2p_stage_bytes(size_t bytes) { return ((bytes / 4 + 1) / 2) * 16; }
 void launch_p2p_allgather(cudaStream_t s, const P2PArgs& a, void* dst, size_t bytes, uint32_t epoch, uint32_t poll_limit, int* err) {
     const int nsm = device_sm_count();
     const size_t tasks = (bytes / 4 + 1) / 2 * (size_t)std::max(1, a.world - 1);
-    if (tasks >= (1ull << 31)) NTCB_CHECK(cudaErrorInvalidValue);   // 32-bit task indices: blocks below 2^31 / (world - 1) lines
+    // 32-bit task indices: ntcb_p2p_export refuses staging for blocks of 2^31 / (world - 1) lines or more, and the
+    // sharded iteration checks every block against that staging
+    if (tasks >= (1ull << 31)) NTCB_CHECK(cudaErrorInvalidValue);
     // at most one CTA per SM: every CTA is resident at once, so a polling CTA never holds back a CTA whose stores a
     // peer is waiting for
     const int grid = (int)std::max<size_t>(1, std::min<size_t>((size_t)nsm, (tasks + kP2PThreads - 1) / kP2PThreads));
