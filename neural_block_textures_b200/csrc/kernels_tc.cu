@@ -96,11 +96,13 @@ struct TcShape {
     // split into hi / lo and interleaved by 8-column K steps ([hi 8 | lo 8] per step)
     static constexpr int cD = 0, cD3 = 32, cX = L3TC ? 48 : 32, cH = cX + 2 * K1;
     static constexpr int COLS = cH + 2 * K2;
-    // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread, enough
-    // for up to 6 features; 4 streams is the floor the kernels were tuned at). Measured: 2 streams cost +33 % over 4.
-    static constexpr int STREAMS = (kTmemCols / COLS >= 5 && S::NIN <= 6) ? 5 : 4;
+    // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread: enough for
+    // up to 6 features, and for 8 with the FP32 3-output layer; the 12-output shape keeps 4). Measured: 2 streams cost
+    // +33 % over 4.
+    static constexpr int STREAMS = (kTmemCols / COLS >= 5 && (S::NIN <= 6 || S::NOUT <= 4)) ? 5 : 4;
     static constexpr int TPB = kTcRows * STREAMS;
     static_assert(STREAMS * COLS <= kTmemCols, "TMEM columns");
+    static_assert(STREAMS * 2 * SIGN * 4 + 1024 <= 227 * 1024, "the population kernel's two weight sets per stream fit shared memory");
     // Layer-2 bias (and, without XB, the layer-1 bias) on the tensor core when the streams leave 8 TMEM columns for the
     // constant block; otherwise b1 is added in the epilogue.
     static constexpr bool B1TC = STREAMS * COLS + 8 <= kTmemCols;
