@@ -187,7 +187,10 @@ __device__ __forceinline__ int quantize_group(const DctTables& T, const DctCtaMe
     }
     __syncwarp();
     const bool trunc = lam16 > 0.0f;
-    const unsigned long long mask = (trunc || with_bits) ? group_mask(T, sm, g, st, trunc, l) : 0ull;
+    // the four groups of a warp may hold blocks of different scale codes (lam16 differs): the mask's shuffles run on
+    // every lane whenever any group needs them
+    const bool need = __any_sync(0xffffffffu, trunc || with_bits);
+    const unsigned long long mask = need ? group_mask(T, sm, g, st, trunc, l) : 0ull;
     __syncwarp();
     int bits = 0, nt = 0, nz = 0;
     if (l == 0) {
