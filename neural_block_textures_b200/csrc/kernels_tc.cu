@@ -96,6 +96,11 @@ struct TcShape {
     // split into hi / lo and interleaved by 8-column K steps ([hi 8 | lo 8] per step)
     static constexpr int cD = 0, cD3 = 32, cX = L3TC ? 48 : 32, cH = cX + 2 * K1;
     static constexpr int COLS = cH + 2 * K2;
+    // Layer 1 accumulates into the H columns (N1 <= 2 K2), which its epilogue overwrites row by row with the split
+    // activations: layer 1 of the next unit then never waits for the threads to finish reading the layer-2
+    // accumulator D. With the tensor-core output layer, whose MMAs read H while the next layer 1 runs, it uses D.
+    static constexpr int cL1 = L3TC ? cD : cH;
+    static_assert(L3TC || N1 <= 2 * K2, "the layer-1 accumulator fits the H columns");
     // Streams per CTA: as many as the SM's TMEM holds, up to 5 (640 threads leave 102 registers per thread: enough for
     // up to 6 features, and for 8 with the FP32 3-output layer; the 12-output shape keeps 4). Measured: 2 streams cost
     // +33 % over 4.
@@ -402,9 +407,9 @@ constexpr uint32_t s4() { static_assert(FLOATS % 4 == 0, "B operand blocks are 1
 template <class T>
 __device__ __forceinline__ void issue_layer1(uint32_t tbase, uint32_t tb, uint32_t sb4, uint64_t* bar) {
     if constexpr (T::XB)
-        issue3<T::K1, T::N1>(tb + T::cD, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), bar);
+        issue3<T::K1, T::N1>(tb + T::cL1, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), bar);
     else   // the features over K1, then b0 against the constant block
-        issue_l2<T::K1, 0, T::N1, true>(tb + T::cD, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), 0, 0, 0, tbase + T::cOne,
+        issue_l2<T::K1, 0, T::N1, true>(tb + T::cL1, tb + T::cX, sb4 + s4<T::oB1h>(), sb4 + s4<T::oB1l>(), 0, 0, 0, tbase + T::cOne,
                                         sb4 + s4<T::oB0h>(), sb4 + s4<T::oB0l>(), bar);
 }
 // Layer 2 of unit (A = H and X of the stream, B = the sign's H-step, X-step and bias blocks).
@@ -459,7 +464,8 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
     constexpr int NS = T::STREAMS;
     extern __shared__ __align__(1024) float dyn[];   // [NS][2][T::SIGN]
     __shared__ __align__(8) uint64_t bars[NS];
-    __shared__ __align__(8) uint64_t bars3[NS];   // output-layer commits (separate: see below)
+    __shared__ __align__(8) uint64_t bars1[NS];   // layer-1 commits (separate: see below)
+    __shared__ __align__(8) uint64_t bars3[NS];   // output-layer commits
     __shared__ uint32_t tbase;
     __shared__ double red[NS][4];
     const int g = threadIdx.x >> 7, tid = threadIdx.x & 127, warp = tid >> 5;
@@ -470,13 +476,17 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
     const int bar_id = 1 + g;
     float* sw = dyn + g * 2 * T::SIGN;
     uint64_t* bar = &bars[g];
-    // The output-layer MMAs and the next unit's layer 1 are committed back to back. On one mbarrier both
-    // phases could complete before a thread polls, leaving the barrier at the parity it waits for (it would
-    // then wait for a phase nobody completes); with their own barrier, commits and waits alternate on each.
+    // Layer 1, layer 2 and the tensor-core output layer commit to three mbarriers. On one mbarrier two commits could
+    // both complete before a slow thread polls for the first (sign 1's layer 1 goes out as soon as the issuing warp has
+    // seen layer 2 complete, with no stream barrier in between; the output-layer MMAs and the next layer 1 go out back
+    // to back), leaving the barrier at the parity that thread waits for: it would then wait for a phase nobody
+    // completes. On its own barrier each kind's next commit needs every thread past a stream barrier it reaches only
+    // after waiting for the previous one, so commits and waits alternate on each.
+    uint64_t* bar1 = &bars1[g];
     uint64_t* bar3 = &bars3[g];
 
     if (threadIdx.x < 32) tc::tmem_alloc(&tbase, kTmemCols);
-    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init(bar3, 1); tc::mbar_init_fence(); }
+    if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_init(bar1, 1); tc::mbar_init(bar3, 1); tc::mbar_init_fence(); }
     for (int i = threadIdx.x; i < NS * 2 * T::SIGN; i += T::TPB) dyn[i] = 0.0f;   // padding stays zero
     tc::fence_before_sync();
     __syncthreads();
@@ -490,12 +500,18 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
     const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
     const uint32_t sb0 = tc::smem_addr(sw) >> 4, sb1 = sb0 + s4<T::SIGN>();   // the signs' weight sets, address >> 4
     const float leak = m.leak;
-    uint32_t waited = 0, waited3 = 0;   // completed phases this thread has observed on bar / bar3
+    uint32_t waited = 0, waited1 = 0, waited3 = 0;   // completed phases this thread has observed on bar / bar1 / bar3
     bool ok = true;
 
     auto wait_mma = [&]() {
         const bool done = tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
         if (done) waited++;
+        ok = ok && done;
+        tc::fence_after_sync();
+    };
+    auto wait_mma1 = [&]() {
+        const bool done = tc::mbar_wait_bounded(bar1, waited1 & 1u, kTcWaitPolls);
+        if (done) waited1++;
         ok = ok && done;
         tc::fence_after_sync();
     };
@@ -569,7 +585,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         tc::wait_st();
         tc::fence_before_sync();
         stream_sync(bar_id);
-        if (warp == issuer) issue_layer1<T>(tbase, tb, sb0, bar);
+        if (warp == issuer) issue_layer1<T>(tbase, tb, sb0, bar1);
 
 #pragma unroll 1
         for (int base = row0; base < row1; base += kTcRows) {
@@ -588,8 +604,8 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 const float* ws = sw + sg * T::SIGN;
                 float h[S::H1 > T::D2COLS ? S::H1 : T::D2COLS];
                 // layer 1 result -> H (h1 + |h1|, the folded leaky ReLU)
-                wait_mma();
-                load_acc<S::H1>(trow, T::cD, h);
+                wait_mma1();
+                load_acc<S::H1>(trow, T::cL1, h);
                 tc::wait_ld();
                 relu2<S::H1>(h);
                 store_split<T::K2>(trow, T::cH, h);
@@ -600,6 +616,12 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                 if (warp == issuer) issue_layer2<T>(tbase, tb, sb, bar);
                 // layer 2 result -> registers (with the FP32 output layer: h2 and W2 h2)
                 wait_mma();
+                if constexpr (!L3TC) {
+                    // sign 1 of this tile: the same features, and its layer 1 accumulates into the H columns, which
+                    // layer 2 has finished reading; issued at once, no stream barrier, overlapping this unit's loads
+                    // and output layer (the issuing warp's lanes agree on the wait's outcome first)
+                    if (sg == 0 && warp == issuer && __all_sync(0xffffffffu, ok)) issue_layer1<T>(tbase, tb, sb1, bar1);
+                }
                 load_acc<L3TC ? S::H2 : T::D2COLS>(trow, T::cD, h);
                 tc::wait_ld();
                 // next unit's layer 1: the other sign of this tile, or the next tile's + sign
@@ -627,7 +649,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     if (!ok) break;
                     if (warp == issuer) {
                         issue3<T::K3, T::N3>(tb + T::cD3, tb + T::cH, sb + s4<T::oB3h>(), sb + s4<T::oB3l>(), bar3);
-                        if (next) issue_layer1<T>(tbase, tb, sg ? sb0 : sb1, bar);
+                        if (next) issue_layer1<T>(tbase, tb, sg ? sb0 : sb1, bar1);
                     }
                     wait_mma3();
                     float o[T::NOUTP];
@@ -643,15 +665,18 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
                     }
                     if (valid) { if (sg == 0) acc_p += (double)e; else acc_m += (double)e; }
                 } else {
-                    if (sg == 1 && more) {
-                        store_x();
-                        load_x(base + 2 * kTcRows);
-                        tc::wait_st();
+                    if (sg == 1) {
+                        // the next tile's features into X (free since layer 2 finished), then its + sign's layer 1
+                        if (more) {
+                            store_x();
+                            load_x(base + 2 * kTcRows);
+                            tc::wait_st();
+                        }
+                        tc::fence_before_sync();
+                        ok = stream_sync_and(bar_id, ok);
+                        if (!ok) break;
+                        if (more && warp == issuer) issue_layer1<T>(tbase, tb, sb0, bar1);
                     }
-                    tc::fence_before_sync();
-                    ok = stream_sync_and(bar_id, ok);
-                    if (!ok) break;
-                    if (next && warp == issuer) issue_layer1<T>(tbase, tb, sg ? sb0 : sb1, bar);
                     // output layer and error of this unit, overlapping the tensor core's next layer 1
                     double e = 0.0;
                     if constexpr (!L3TC) e = valid ? (double)out_layer_error<S, CLAMP>(m, ws, h, t, leak) : 0.0;
@@ -673,6 +698,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_pop_eval_tc(DevModel m, 
         // A wait timed out: flag it, give the outstanding MMAs one more bounded wait, then free TMEM.
         if (tid == 0) atomicExch(a.tc_err, 1);
         tc::mbar_wait_bounded(bar, waited & 1u, kTcWaitPolls);
+        tc::mbar_wait_bounded(bar1, waited1 & 1u, kTcWaitPolls);
         if (L3TC) tc::mbar_wait_bounded(bar3, waited3 & 1u, kTcWaitPolls);
     }
     tc::fence_before_sync();
@@ -787,7 +813,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_lat_eval_tc(DevModel m, 
     auto layer1_to_layer2 = [&]() {
         float h[S::H1];
         wait_mma();
-        load_acc<S::H1>(trow, T::cD, h);
+        load_acc<S::H1>(trow, T::cL1, h);
         tc::wait_ld();
         relu2<S::H1>(h);
         store_split<T::K2>(trow, T::cH, h);
@@ -963,7 +989,7 @@ __global__ void __launch_bounds__(TcShape<S>::TPB, 1) k_qat_tc(DevModel m, const
             if (warp == issuer) issue_layer1<T>(tbase, tb, sb, bar);
             float h[S::H1 > T::D2COLS ? S::H1 : T::D2COLS];
             wait_mma();
-            load_acc<S::H1>(trow, T::cD, h);
+            load_acc<S::H1>(trow, T::cL1, h);
             tc::wait_ld();
             relu2<S::H1>(h);
             store_split<T::K2>(trow, T::cH, h);
